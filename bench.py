@@ -1,0 +1,341 @@
+#!/usr/bin/env python
+"""Throughput benchmark of the rotated-surface bipartite-conv pre-decoder (d = 13, 13 rounds, 8 layers, C = 128, bf16).
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl b200|reference]
+    (N > 1: torchrun --nproc-per-node N bench.py --gpus N ..., one rank per GPU)
+
+A step is one forward pass of the pre-decoder over this rank's shard of a 262,144-shot batch (shards of
+262144 / N shots, no collective on the data path): detectors -> 16 bipartite steps -> X/Z logits -> residual
+syndrome.  Inputs are seeded phenomenological shots (p = 0.005) drawn on the device; weights are seeded.
+`value` times K steps on device-resident inputs with CUDA events (max over ranks); `e2e` times the same steps through
+the public PreDecoder API from pinned host memory, copies in and out included; `roofline` is the bipartite-step
+kernel's algorithmic tensor FLOP rate (CUDA events around every step launch of the last timed step) against the
+measured sustained bf16 peak; `cpu_baseline` times the CPU oracle (the reference's fp32 index_select + matmul path,
+restated) on this host's cores for a bounded sample.  --impl reference times only that CPU path.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from dataclasses import replace
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "syndromes/sec/GPU at d=13 (1/2/4/8 B200, % roofline); p99 per-round latency d=17"
+UNIT = "syndromes/s"
+TOTAL_SHOTS = 262144
+SEED = 1234
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--config", default="d13_bf16")
+    ap.add_argument("--shots", type=int, default=TOTAL_SHOTS, help="total shots per step over all GPUs")
+    ap.add_argument("--chunk", type=int, default=16384, help="shots per pass through the network")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return {"bf16_tflops": p["bf16_tflops"], "bf16_tflops_sustained": p["bf16_tflops_sustained"],
+                "hbm_gbs": p["hbm_gbs"], "source": "measured"}
+    except Exception:
+        return {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def workload(cfg, g, shots_per_gpu, n):
+    return {"workload": f"rotated surface d={cfg.d}, {cfg.rounds} rounds, phenomenological p={cfg.p}; "
+                        f"{cfg.layers} layers x [check->data, data->check], C={cfg.channels}, K={cfg.K}, "
+                        f"{cfg.dtype}; X/Z head + residual syndrome",
+            "d": cfg.d, "rounds": cfg.rounds, "layers": cfg.layers, "channels": cfg.channels, "K": cfg.K,
+            "checks": g.N_c, "data_nodes": g.N_d, "global_batch": shots_per_gpu * n, "shots_per_gpu": shots_per_gpu,
+            "parallelism": f"shots sharded over {n} GPU(s), no collective",
+            "l2": "inputs larger than L2 (detectors 573 MB per 262144 shots; 18 GB activations per 16384-shot pass)"}
+
+
+class ClockSampler:
+    """nvidia-smi samples of this GPU's clocks and throttle reasons while the timed region runs."""
+    FIELDS = ["index", "clocks.sm", "clocks.max.sm", "power.draw", "clocks_event_reasons.active",
+              "clocks_event_reasons.hw_slowdown", "clocks_event_reasons.hw_thermal_slowdown",
+              "clocks_event_reasons.sw_thermal_slowdown", "clocks_event_reasons.sw_power_cap"]
+
+    def __init__(self, device_index):
+        import torch
+        self.sel = []
+        try:
+            u = str(torch.cuda.get_device_properties(device_index).uuid)
+            if u:
+                self.sel = ["-i", u if u.startswith("GPU-") else "GPU-" + u]
+        except Exception:
+            self.sel = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", *self.sel, "--query-gpu=" + ",".join(self.FIELDS),
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=10)
+            except Exception:
+                self.proc.kill()
+        return False
+
+    def summary(self):
+        rows = []
+        for line in (self.out or "").strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) != len(self.FIELDS):
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[4:]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        busy = [r for r in rows if r[2] > 0.5 * max(x[2] for x in rows)] or rows
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in busy:
+            for nm, v in zip(names, r[3][1:]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(r[0] for r in busy), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": sorted(reasons), "samples": len(busy), "power_w_max": max(r[2] for r in rows)}
+
+
+def cpu_rate(g, cfg, params, det, seconds):
+    """The CPU oracle (fp32 torch on every host thread) on a bounded sample -> (shots/s, shots, threads)."""
+    import torch
+    from oracle import predecoder_oracle as orc
+    torch.set_num_threads(os.cpu_count() or 1)
+    cfg32 = replace(cfg, dtype="f32")
+    batch = 2
+    done, t0 = 0, time.perf_counter()
+    with torch.no_grad():
+        orc.predecoder(g, cfg32, params, det[:1], dtype=torch.float32)      # warm-up
+        t0 = time.perf_counter()
+        while True:
+            sl = det[done % len(det):done % len(det) + batch]
+            orc.predecoder(g, cfg32, params, sl, dtype=torch.float32)
+            done += len(sl)
+            if time.perf_counter() - t0 >= seconds:
+                break
+    dt = time.perf_counter() - t0
+    return done / dt, done, torch.get_num_threads()
+
+
+def run_reference(args, cfg, g, params, rank, world):
+    """--impl reference: the CPU path of the reference (restated by the oracle), rank 0 only."""
+    if rank != 0:
+        return
+    import numpy as np
+    import torch
+    from codecoder_b200.sampler import sample
+    from oracle import predecoder_oracle as orc
+    torch.set_num_threads(os.cpu_count() or 1)
+    det, _ = sample(g, cfg.p, 64, SEED)
+    cfg32 = replace(cfg, dtype="f32")
+    t0 = time.perf_counter()
+    with torch.no_grad():
+        orc.predecoder(g, cfg32, params, det[:1], dtype=torch.float32)
+    per_shot = max(time.perf_counter() - t0, 1e-3)
+    shots = int(max(1, min(64, 10.0 / per_shot)))          # a step of about 10 s
+    times = []
+    with torch.no_grad():
+        for k in range(args.warmup + args.steps):
+            t = time.perf_counter()
+            orc.predecoder(g, cfg32, params, det[:shots], dtype=torch.float32)
+            if k >= args.warmup:
+                times.append(time.perf_counter() - t)
+    total = sum(times)
+    rate = shots * len(times) / total
+    sample_desc = f"{shots} shots per step of the d={cfg.d} workload (fp32 CPU oracle)"
+    line = {"metric": METRIC, "value": rate, "unit": UNIT, "impl": "reference", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / len(times),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": workload(cfg, g, args.shots // world, world),
+            "cpu_baseline": {"value": rate, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+                             "sample": sample_desc},
+            "e2e": {"value": rate, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    from codecoder_b200.geometry import RotatedSurface
+    from codecoder_b200.params import CONFIGS, flops_per_shot, init_params
+    cfg = CONFIGS[args.config]
+    g = RotatedSurface(cfg.d, cfg.rounds)
+    params = init_params(cfg, SEED)
+    if args.impl == "reference":
+        run_reference(args, cfg, g, params, rank, world)
+        return
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from codecoder_b200.build import build
+    from codecoder_b200.modules import PreDecoder
+    from codecoder_b200.sampler import sample_torch
+
+    if rank == 0:
+        build()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+        dist.barrier()
+        build()                                         # no-op once rank 0 built it
+
+    shots = args.shots // world
+    det, _ = sample_torch(g, cfg.p, shots, SEED + 7919 * rank, device=dev)
+    pd = PreDecoder(g, cfg, params, device=dev, chunk_shots=args.chunk)
+    logits = torch.empty(shots, g.N_d, 2, dtype=torch.float32, device=dev)
+    resid = torch.empty(shots, g.N_c, dtype=torch.uint8, device=dev)
+
+    S = ((min(args.chunk, shots) + 127) // 128) * 128
+    chunks = [min(S, shots - b) for b in range(0, shots, S)]
+    launches_per_fwd = len(chunks) * (2 * cfg.layers + 2)
+    step_flops = []                                     # algorithmic FLOPs of each bipartite-step launch in order
+    for sb in chunks:
+        for _ in range(cfg.layers):
+            step_flops.append(2.0 * cfg.K * cfg.channels ** 2 * g.N_d * sb)
+            step_flops.append(2.0 * cfg.K * cfg.channels ** 2 * g.N_c * sb)
+    ev_pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in step_flops]
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        pd.forward_into(det, logits, resid)
+    torch.cuda.synchronize()
+    if pd.status() != 0:
+        raise RuntimeError("device watchdog fired during warm-up")
+
+    pd.record_step_events(ev_pairs)
+    barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        start.record()
+        for _ in range(args.steps):
+            pd.forward_into(det, logits, resid)
+        end.record()
+        end.synchronize()
+    torch.cuda.synchronize()
+    barrier()
+    ms = max_over_ranks(start.elapsed_time(end))
+    pd.record_step_events([])
+    step_ms = [a.elapsed_time(b) for a, b in ev_pairs]
+    tc_ms = sum(step_ms)
+    tc_flops = sum(step_flops)
+    if pd.status() != 0:
+        raise RuntimeError("device watchdog fired in the timed region")
+
+    value = args.steps * shots * world / (ms / 1000.0)
+    pk = peaks()
+    achieved = tc_flops / (tc_ms / 1000.0) / 1e12
+    fps = flops_per_shot(cfg, g.N_c, g.N_d)
+    roof = {"bound": "tensor", "kernel": "gmm_tc_kernel (bipartite step)", "achieved": achieved,
+            "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s", "frac": achieved / pk["bf16_tflops_sustained"],
+            "peak_kind": f"{pk['source']} sustained bf16 (cuBLAS)", "traffic": None,
+            "avg_launch_ms": tc_ms / len(step_ms), "launches": len(step_ms),
+            "flop_per_unit": 2 * cfg.K * cfg.channels ** 2, "unit_desc": "target node x shot",
+            "whole_step_frac": value / world * fps / 1e12 / pk["bf16_tflops_sustained"]}
+    tr_path = os.path.join(REPO, "profiles", "gmm_tc_d13_traffic.json")
+    if os.path.exists(tr_path):
+        with open(tr_path) as f:
+            tr = json.load(f)
+        units_per_launch = (sum(step_flops) / len(step_flops)) / (2 * cfg.K * cfg.channels ** 2)
+        roof["traffic"] = tr["bytes_per_node_shot"] * units_per_launch
+        roof["traffic_source"] = tr.get("source", "")
+
+    e2e = None
+    if not args.no_e2e:
+        det_h = det.cpu().pin_memory()
+        lg_h = torch.empty(logits.shape, dtype=logits.dtype, pin_memory=True)
+        rs_h = torch.empty(resid.shape, dtype=resid.dtype, pin_memory=True)
+        d_in = torch.empty_like(det)
+        for _ in range(1):
+            d_in.copy_(det_h, non_blocking=True)
+            pd.forward_into(d_in, logits, resid)
+            lg_h.copy_(logits, non_blocking=True)
+            rs_h.copy_(resid, non_blocking=True)
+        torch.cuda.synchronize()
+        barrier()
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record()
+        for _ in range(args.steps):
+            d_in.copy_(det_h, non_blocking=True)
+            pd.forward_into(d_in, logits, resid)
+            lg_h.copy_(logits, non_blocking=True)
+            rs_h.copy_(resid, non_blocking=True)
+        e2.record()
+        e2.synchronize()
+        barrier()
+        ms2 = max_over_ranks(s2.elapsed_time(e2))
+        e2e = {"value": args.steps * shots * world / (ms2 / 1000.0), "unit": UNIT,
+               "h2d_bytes_per_step": det.numel() * world,
+               "d2h_bytes_per_step": (logits.numel() * 4 + resid.numel()) * world,
+               "api": "codecoder_b200.modules.PreDecoder.forward_into (C ABI bpc_predecoder_forward)"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        det_np = det[:64].cpu().numpy()
+        rate, n_shots, threads = cpu_rate(g, cfg, params, det_np, args.cpu_seconds)
+        cpu = {"value": rate, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"{n_shots} shots of the d={cfg.d} workload through the CPU oracle (fp32 torch "
+                         f"index_select + matmul, the reference's gather_mm path), {threads} threads"}
+
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": cfg.dtype, "data": "synthetic",
+                "config": workload(cfg, g, shots, world), "per_gpu": value / world, "roofline": roof,
+                "cpu_baseline": cpu, "e2e": e2e, "clocks": clk.summary(),
+                "gpu_launches": launches_per_fwd * args.steps, "flop_per_shot": fps}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,66 @@
+// Internal launch interface of the bipartite-conv kernels (host side, shared by the C ABI and the pre-decoder).
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <string>
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace bpc {
+
+enum EpiMode : int {
+  kEpiStore = 0,      // y = acc
+  kEpiGeluInit = 1,   // y = GELU(acc)
+  kEpiGeluResid = 2,  // y = y + GELU(acc)
+};
+
+// Optional work fused into the epilogue of the last check -> data step of the pre-decoder.
+struct HeadEpilogue {
+  const float* head_w = nullptr;   // (2, Co) fp32, null = no head
+  const float* head_b = nullptr;   // (2,)
+  float* logits = nullptr;         // logits[shot * lg_shot_stride + node * lg_node_stride + j], j = 0 X, 1 Z
+  int64_t lg_shot_stride = 0, lg_node_stride = 0;
+  uint32_t* res_bits = nullptr;    // residual bits (checks, res_words), bit s % 32 of word s / 32 = shot s
+  int64_t res_words = 0;
+  const int32_t* xor_nbr = nullptr;  // (NT, 2, 2) checks flipped by a predicted X / Z flip, -1 = none
+};
+
+// y[s, n, :] (op)= sum_r x[s, idx[n, r], :] W_{type(n), r}^T over relations r whose source is in [0, NS).
+// Strides are in elements.  W holds n_wtypes stacked (Co, K Ci) matrices; target n uses set (n >= type_split).
+struct GmmProblem {
+  const void* x = nullptr;
+  int64_t x_shot_stride = 0, x_node_stride = 0;
+  int64_t shots = 0;
+  int NS = 0;
+  const void* w = nullptr;
+  int n_wtypes = 1, type_split = 0;
+  const int32_t* idx = nullptr;
+  int NT = 0, K = 0, Ci = 0, Co = 0;
+  void* y = nullptr;
+  int64_t y_shot_stride = 0, y_node_stride = 0;
+  int epi = kEpiStore;
+  HeadEpilogue head;
+};
+
+// Tensor maps a caller may prepare once and reuse across launches (the pre-decoder does).
+struct GmmMaps {
+  CUtensorMap x;
+  CUtensorMap w;
+};
+
+void set_error(const std::string& msg);
+int fail(int code, const std::string& msg);
+
+// tcgen05 path: bf16 x / W / y, fp32 accumulation in tensor memory.  Ci >= 64 and Ci % 8 == 0, Co % 32 == 0,
+// Co <= 256.  Returns 0 or an error code (message in the thread's last error).
+int gmm_tc_check(const GmmProblem& p);
+int gmm_tc_make_maps(const GmmProblem& p, GmmMaps* maps);
+int gmm_tc_launch(const GmmProblem& p, const GmmMaps& maps, int* status, uint64_t timeout_ns, cudaStream_t stream);
+
+// CUDA-core path: fp32 (f32 = true) or bf16 storage, fp32 accumulation.  Any Ci, Co % 4 == 0, Co <= 256.
+int gmm_fma_launch(const GmmProblem& p, bool f32, cudaStream_t stream);
+
+int num_sms();
+
+}  // namespace bpc

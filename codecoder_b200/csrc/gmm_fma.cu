@@ -1,0 +1,178 @@
+// Bipartite-conv step on the CUDA cores, for narrow channel widths (C < 64) and fp32 networks, where the tensor
+// cores do not apply (fp32 storage) or would idle (K C < 512).  Same arithmetic and epilogues as gmm_tc.cu.
+//
+// Tile = one target node n x 64 shots, 256 threads: thread t handles shot t / 4 and a quarter of the output
+// channels, so the 4 threads of a shot are adjacent lanes (the head's dot product is two shuffles).  For every
+// non-pad relation the relation's weight W_r (C_out x C_in) is staged transposed in shared memory, in slices of
+// C_in that fit 48 KB, and every thread runs C_in x C_out / 4 FMAs in fp32.
+#include <string>
+
+#include "bpc_common.cuh"
+#include "bpc_internal.h"
+
+namespace bpc {
+
+namespace {
+
+constexpr int kFmaShots = 64;
+constexpr int kFmaThreads = 256;
+constexpr int kFmaSmemFloats = 12288;  // 48 KB
+
+template <typename T>
+__device__ __forceinline__ float ld_elem(const T* p);
+template <>
+__device__ __forceinline__ float ld_elem<float>(const float* p) { return *p; }
+template <>
+__device__ __forceinline__ float ld_elem<__nv_bfloat16>(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+template <typename T>
+__device__ __forceinline__ T st_conv(float v);
+template <>
+__device__ __forceinline__ float st_conv<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 st_conv<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+struct FmaArgs {
+  const void* x;
+  int64_t x_shot_stride, x_node_stride;
+  int64_t shots;
+  int NS;
+  const void* w;
+  int type_split;
+  const int32_t* idx;
+  int NT, K, Ci, Co;
+  void* y;
+  int64_t y_shot_stride, y_node_stride;
+  int epi;
+  HeadEpilogue head;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kFmaThreads) gmm_fma_kernel(const FmaArgs a) {
+  __shared__ float ws[kFmaSmemFloats];
+  const int64_t tile = blockIdx.x;
+  const int n = static_cast<int>(tile % a.NT);
+  const int64_t s0 = (tile / a.NT) * kFmaShots;
+  const int t = threadIdx.x;
+  const int g = t & 3;
+  const int64_t shot = s0 + (t >> 2);
+  const bool ok = shot < a.shots;
+  const int cq = a.Co >> 2;                  // output channels per thread (<= 64)
+  const int o0 = g * cq;
+  const T* x = reinterpret_cast<const T*>(a.x);
+  const T* w = reinterpret_cast<const T*>(a.w) + ((n >= a.type_split) ? static_cast<int64_t>(a.Co) * a.K * a.Ci : 0);
+  float acc[64];
+#pragma unroll
+  for (int i = 0; i < 64; ++i) acc[i] = 0.f;
+  const int chunk = min(a.Ci, kFmaSmemFloats / a.Co);
+  for (int r = 0; r < a.K; ++r) {
+    const int src = __ldg(a.idx + static_cast<int64_t>(n) * a.K + r);
+    if (src < 0 || src >= a.NS) continue;   // uniform across the block
+    const T* xr = x + shot * a.x_shot_stride + static_cast<int64_t>(src) * a.x_node_stride;
+    for (int i0 = 0; i0 < a.Ci; i0 += chunk) {
+      const int ni = min(chunk, a.Ci - i0);
+      __syncthreads();
+      for (int e = t; e < ni * a.Co; e += kFmaThreads) {     // ws[i][o] = W[o, r Ci + i0 + i]
+        const int o = e / ni, i = e - o * ni;
+        ws[i * a.Co + o] = ld_elem(w + static_cast<int64_t>(o) * a.K * a.Ci + static_cast<int64_t>(r) * a.Ci + i0 + i);
+      }
+      __syncthreads();
+      if (ok) {
+        for (int i = 0; i < ni; ++i) {
+          const float xv = ld_elem(xr + i0 + i);
+          const float* wrow = ws + i * a.Co + o0;
+#pragma unroll
+          for (int j = 0; j < 64; ++j)
+            if (j < cq) acc[j] = fmaf(xv, wrow[j], acc[j]);
+        }
+      }
+    }
+  }
+  float lg0 = 0.f, lg1 = 0.f;
+  if (ok) {
+    T* yr = reinterpret_cast<T*>(a.y) + shot * a.y_shot_stride + static_cast<int64_t>(n) * a.y_node_stride + o0;
+#pragma unroll
+    for (int j = 0; j < 64; ++j) {
+      if (j < cq) {
+        float v = acc[j];
+        if (a.epi == kEpiGeluInit) v = gelu_erf(v);
+        else if (a.epi == kEpiGeluResid) v = ld_elem(yr + j) + gelu_erf(v);
+        const T sv = st_conv<T>(v);
+        yr[j] = sv;
+        if (a.head.head_w) {
+          const float f = ld_elem(&sv);
+          lg0 = fmaf(f, __ldg(a.head.head_w + o0 + j), lg0);
+          lg1 = fmaf(f, __ldg(a.head.head_w + a.Co + o0 + j), lg1);
+        }
+      }
+    }
+  }
+  if (a.head.head_w) {
+    lg0 += __shfl_xor_sync(0xffffffffu, lg0, 1);
+    lg0 += __shfl_xor_sync(0xffffffffu, lg0, 2);
+    lg1 += __shfl_xor_sync(0xffffffffu, lg1, 1);
+    lg1 += __shfl_xor_sync(0xffffffffu, lg1, 2);
+    lg0 += __ldg(a.head.head_b);
+    lg1 += __ldg(a.head.head_b + 1);
+    if (ok && g == 0) {
+      float* lp = a.head.logits + shot * a.head.lg_shot_stride + static_cast<int64_t>(n) * a.head.lg_node_stride;
+      lp[0] = lg0;
+      lp[1] = lg1;
+    }
+    if (a.head.res_bits) {
+      const int lane = t & 31;
+      const uint32_t b0 = __ballot_sync(0xffffffffu, ok && g == 0 && lg0 > 0.f);
+      const uint32_t b1 = __ballot_sync(0xffffffffu, ok && g == 0 && lg1 > 0.f);
+      uint32_t m0 = 0, m1 = 0;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {             // lanes 4k hold shot k of this warp
+        m0 |= ((b0 >> (4 * k)) & 1u) << k;
+        m1 |= ((b1 >> (4 * k)) & 1u) << k;
+      }
+      const int64_t wshot = s0 + (t >> 5) * 8;  // first shot of this warp, a multiple of 8
+      if (lane < 4) {
+        const int j = lane >> 1;
+        const int32_t c = __ldg(a.head.xor_nbr + static_cast<int64_t>(n) * 4 + lane);
+        const uint32_t m = (j ? m1 : m0) << (wshot & 31);
+        if (c >= 0 && m) atomicXor(a.head.res_bits + static_cast<int64_t>(c) * a.head.res_words + (wshot >> 5), m);
+      }
+    }
+  }
+}
+
+}  // namespace
+
+int gmm_fma_launch(const GmmProblem& p, bool f32, cudaStream_t stream) {
+  if (p.Co < 4 || p.Co > 256 || p.Co % 4 != 0) return fail(2, "CUDA-core path needs C_out in 4..256, multiple of 4");
+  if (p.Ci < 1) return fail(2, "C_in must be positive");
+  if (p.K < 1 || p.NT < 1 || p.NS < 1) return fail(2, "empty problem");
+  if (p.shots <= 0) return 0;
+  FmaArgs a;
+  a.x = p.x;
+  a.x_shot_stride = p.x_shot_stride;
+  a.x_node_stride = p.x_node_stride;
+  a.shots = p.shots;
+  a.NS = p.NS;
+  a.w = p.w;
+  a.type_split = p.n_wtypes > 1 ? p.type_split : p.NT;
+  a.idx = p.idx;
+  a.NT = p.NT;
+  a.K = p.K;
+  a.Ci = p.Ci;
+  a.Co = p.Co;
+  a.y = p.y;
+  a.y_shot_stride = p.y_shot_stride;
+  a.y_node_stride = p.y_node_stride;
+  a.epi = p.epi;
+  a.head = p.head;
+  const int64_t tiles = static_cast<int64_t>(p.NT) * ((p.shots + kFmaShots - 1) / kFmaShots);
+  if (tiles > 0x7fffffffLL) return fail(2, "too many tiles for one launch");
+  if (f32)
+    gmm_fma_kernel<float><<<static_cast<unsigned>(tiles), kFmaThreads, 0, stream>>>(a);
+  else
+    gmm_fma_kernel<__nv_bfloat16><<<static_cast<unsigned>(tiles), kFmaThreads, 0, stream>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(4, std::string("gmm_fma_kernel launch: ") + cudaGetErrorString(e));
+  return 0;
+}
+
+}  // namespace bpc

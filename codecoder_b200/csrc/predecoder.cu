@@ -1,0 +1,357 @@
+// Pre-decoder forward: detector bits -> L x [check -> data, data -> check] bipartite convolutions -> X/Z head ->
+// threshold -> XOR syndrome cancellation, on device buffers, with the caller's workspace.
+//
+// HBM layout of one chunk of S shots (S a multiple of 128; the workspace fixes S):
+//   h_c   (N_c, S, C)  check features, node-major: the 128 shots of a tile x one node are 128 x C contiguous
+//   h_d   (N_d, S, C)  data features, same layout
+//   bits  (N_c, S/32)  uint32 residual syndrome, bit s % 32 of word s / 32 = shot s
+// Per chunk: embed (det -> h_c, det -> bits), 2 L bipartite steps (the last check -> data step also writes the logits
+// and XORs the predicted flips into bits), unpack (bits -> residual bytes).  Logits go straight to the caller's
+// (B, N_d, 2) buffer from the head epilogue.
+#include <algorithm>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/bpc.h"
+#include "bpc_common.cuh"
+#include "bpc_internal.h"
+
+struct bpc_predecoder {
+  bpc_predecoder_config cfg;
+  int32_t* c2d = nullptr;        // (N_d, K)
+  int32_t* d2c = nullptr;        // (N_c, K)
+  int32_t* xor_nbr = nullptr;    // (N_d, 2, 2)
+  uint8_t* check_type = nullptr; // (N_c)
+  void* embed = nullptr;         // (4, C)
+  void* w_c2d = nullptr;         // (L, C, K C)
+  void* w_d2c = nullptr;         // (L, 2, C, K C)
+  float* head_w = nullptr;       // (2, C)
+  float* head_b = nullptr;       // (2)
+  int* status = nullptr;         // device watchdog status word
+  bool weights_set = false;
+  uint64_t timeout_ns = 2000000000ull;
+  std::vector<cudaEvent_t> step_events;   // optional (before, after) pairs around each bipartite-step launch
+};
+
+namespace bpc {
+namespace {
+
+constexpr int kEmbShots = 128;
+constexpr int kEmbNodes = 32;
+
+size_t esize(int dtype) { return dtype == BPC_DTYPE_F32 ? 4 : 2; }
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+// det (rows of N_c bytes, shot-major) -> h_c[n][s][:] = embed[2 type(n) + det] and bits[n][s / 32].
+template <typename T>
+__global__ void __launch_bounds__(256) embed_kernel(const uint8_t* __restrict__ det, int64_t shots, int N_c, int C,
+                                                   const uint8_t* __restrict__ ctype, const T* __restrict__ embed,
+                                                   T* __restrict__ hc, int64_t S, uint32_t* __restrict__ bits,
+                                                   int64_t words) {
+  __shared__ uint8_t tile[kEmbNodes][kEmbShots + 4];
+  __shared__ __align__(16) T emb[4 * 256];
+  const int64_t s0 = static_cast<int64_t>(blockIdx.x) * kEmbShots;
+  const int n0 = blockIdx.y * kEmbNodes;
+  for (int e = threadIdx.x; e < 4 * C; e += blockDim.x) emb[e] = embed[e];
+  for (int e = threadIdx.x; e < kEmbNodes * kEmbShots; e += blockDim.x) {
+    const int s = e / kEmbNodes, j = e - s * kEmbNodes;
+    const int64_t shot = s0 + s;
+    const int n = n0 + j;
+    tile[j][s] = (shot < shots && n < N_c) ? (det[shot * N_c + n] & 1) : 0;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // bit-packed residual initialised with the detectors
+  for (int j = warp; j < kEmbNodes; j += blockDim.x / 32) {
+    const int n = n0 + j;
+    if (n >= N_c) break;
+    for (int w = 0; w < kEmbShots / 32; ++w) {
+      const uint32_t m = __ballot_sync(0xffffffffu, tile[j][w * 32 + lane] != 0);
+      const int64_t word = (s0 >> 5) + w;
+      if (lane == 0 && word < words) bits[static_cast<int64_t>(n) * words + word] = m;
+    }
+  }
+  // features: 16-byte vectors; a (node, shot) row is C elements
+  const int vec = 16 / sizeof(T);
+  const int row_vecs = C / vec;
+  const int64_t smax = (shots - s0) < kEmbShots ? (shots - s0) : kEmbShots;
+  for (int j = 0; j < kEmbNodes; ++j) {
+    const int n = n0 + j;
+    if (n >= N_c) break;
+    const int tb = 2 * ctype[n];
+    T* base = hc + (static_cast<int64_t>(n) * S + s0) * C;
+    for (int e = threadIdx.x; e < smax * row_vecs; e += blockDim.x) {
+      const int s = e / row_vecs, v = e - s * row_vecs;
+      const int tok = tb + tile[j][s];
+      reinterpret_cast<uint4*>(base + static_cast<int64_t>(s) * C)[v] = reinterpret_cast<const uint4*>(emb + tok * C)[v];
+    }
+  }
+}
+
+// bits[n][s / 32] -> residual[shot][n] bytes
+__global__ void __launch_bounds__(256) unpack_kernel(const uint32_t* __restrict__ bits, int64_t words, int64_t shots,
+                                                    int N_c, uint8_t* __restrict__ out) {
+  __shared__ uint32_t w[kEmbNodes][kEmbShots / 32];
+  const int64_t s0 = static_cast<int64_t>(blockIdx.x) * kEmbShots;
+  const int n0 = blockIdx.y * kEmbNodes;
+  for (int e = threadIdx.x; e < kEmbNodes * (kEmbShots / 32); e += blockDim.x) {
+    const int j = e / (kEmbShots / 32), k = e - j * (kEmbShots / 32);
+    const int64_t word = (s0 >> 5) + k;
+    w[j][k] = (n0 + j < N_c && word < words) ? bits[static_cast<int64_t>(n0 + j) * words + word] : 0u;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < kEmbShots * kEmbNodes; e += blockDim.x) {
+    const int s = e / kEmbNodes, j = e - s * kEmbNodes;
+    const int64_t shot = s0 + s;
+    if (shot < shots && n0 + j < N_c) out[shot * N_c + n0 + j] = static_cast<uint8_t>((w[j][s >> 5] >> (s & 31)) & 1u);
+  }
+}
+
+struct Layout {
+  int64_t S;
+  size_t off_hc, off_hd, off_bits, total;
+};
+
+Layout layout_for(const bpc_predecoder_config& c, int64_t chunk) {
+  Layout L;
+  L.S = ((chunk + 127) / 128) * 128;
+  const size_t es = esize(c.dtype);
+  L.off_hc = 0;
+  L.off_hd = align256(L.off_hc + static_cast<size_t>(c.n_checks) * L.S * c.channels * es);
+  L.off_bits = align256(L.off_hd + static_cast<size_t>(c.n_data) * L.S * c.channels * es);
+  L.total = align256(L.off_bits + static_cast<size_t>(c.n_checks) * (L.S / 32) * 4);
+  return L;
+}
+
+template <typename T>
+int copy_in(T** dst, const void* src, size_t bytes) {
+  if (*dst == nullptr) {
+    cudaError_t e = cudaMalloc(reinterpret_cast<void**>(dst), bytes);
+    if (e != cudaSuccess) return fail(BPC_ERR_LAUNCH, std::string("cudaMalloc: ") + cudaGetErrorString(e));
+  }
+  cudaError_t e = cudaMemcpy(*dst, src, bytes, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return fail(BPC_ERR_LAUNCH, std::string("cudaMemcpy: ") + cudaGetErrorString(e));
+  return 0;
+}
+
+}  // namespace
+}  // namespace bpc
+
+using namespace bpc;
+
+extern "C" int bpc_predecoder_create(const bpc_predecoder_config* cfg, const int32_t* c2d, const int32_t* d2c,
+                                     const int32_t* xor_nbr, const uint8_t* check_type, bpc_predecoder** out) {
+  if (!cfg || !c2d || !d2c || !xor_nbr || !check_type || !out) return fail(BPC_ERR_ARG, "null argument");
+  *out = nullptr;
+  const auto& c = *cfg;
+  if (c.layers < 1 || c.channels < 8 || c.channels > 256 || c.channels % 8 || c.K < 1 || c.K > 32 ||
+      c.n_checks < 1 || c.n_data < 1 || c.z_check_begin < 0 || c.z_check_begin > c.n_checks ||
+      (c.dtype != BPC_DTYPE_BF16 && c.dtype != BPC_DTYPE_F32))
+    return fail(BPC_ERR_ARG, "invalid pre-decoder configuration");
+  auto* h = new bpc_predecoder();
+  h->cfg = c;
+  int e = 0;
+  if ((e = copy_in(&h->c2d, c2d, sizeof(int32_t) * c.n_data * c.K)) ||
+      (e = copy_in(&h->d2c, d2c, sizeof(int32_t) * c.n_checks * c.K)) ||
+      (e = copy_in(&h->xor_nbr, xor_nbr, sizeof(int32_t) * c.n_data * 4)) ||
+      (e = copy_in(&h->check_type, check_type, c.n_checks))) {
+    bpc_predecoder_destroy(h);
+    return e;
+  }
+  int zero = 0;
+  if ((e = copy_in(&h->status, &zero, sizeof(int)))) {
+    bpc_predecoder_destroy(h);
+    return e;
+  }
+  *out = h;
+  return 0;
+}
+
+extern "C" int bpc_predecoder_set_weights(bpc_predecoder* h, const void* embed, const void* w_c2d, const void* w_d2c,
+                                          const float* head_w, const float* head_b) {
+  if (!h || !embed || !w_c2d || !w_d2c || !head_w || !head_b) return fail(BPC_ERR_ARG, "null argument");
+  const auto& c = h->cfg;
+  const size_t es = esize(c.dtype);
+  const size_t wl = static_cast<size_t>(c.channels) * c.K * c.channels;
+  int e = 0;
+  if ((e = copy_in(&h->embed, embed, 4 * c.channels * es)) ||
+      (e = copy_in(&h->w_c2d, w_c2d, c.layers * wl * es)) ||
+      (e = copy_in(&h->w_d2c, w_d2c, 2 * c.layers * wl * es)) ||
+      (e = copy_in(&h->head_w, head_w, 2 * c.channels * sizeof(float))) ||
+      (e = copy_in(&h->head_b, head_b, 2 * sizeof(float))))
+    return e;
+  h->weights_set = true;
+  return 0;
+}
+
+extern "C" size_t bpc_predecoder_workspace_size(const bpc_predecoder* h, int64_t chunk_shots) {
+  if (!h || chunk_shots < 1) return 0;
+  return layout_for(h->cfg, chunk_shots).total;
+}
+
+extern "C" int bpc_predecoder_forward(bpc_predecoder* h, const uint8_t* det, float* logits, uint8_t* residual,
+                                      int64_t B, void* workspace, size_t workspace_bytes, bpc_stream_t stream_) {
+  if (!h || !h->weights_set) return fail(BPC_ERR_ARG, "pre-decoder without weights");
+  if (B < 0) return fail(BPC_ERR_ARG, "negative batch");
+  if (B == 0) return 0;
+  if (!det || !logits || !residual || !workspace) return fail(BPC_ERR_ARG, "null buffer");
+  if (reinterpret_cast<uintptr_t>(workspace) & 255) return fail(BPC_ERR_ARG, "workspace must be 256-byte aligned");
+  if (reinterpret_cast<uintptr_t>(logits) & 7) return fail(BPC_ERR_ARG, "logits must be 8-byte aligned");
+  const auto& c = h->cfg;
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  // largest chunk (multiple of 128 shots, at most B rounded up) whose layout fits the workspace
+  int64_t chunk = ((B + 127) / 128) * 128;
+  const size_t per128 = layout_for(c, 128).total;
+  if (workspace_bytes < per128) return fail(BPC_ERR_SPACE, "workspace smaller than one 128-shot chunk");
+  while (chunk > 128 && layout_for(c, chunk).total > workspace_bytes) {
+    const int64_t fit = static_cast<int64_t>(workspace_bytes / per128) * 128;
+    chunk = std::max<int64_t>(128, std::min(chunk - 128, fit));
+  }
+  const Layout L = layout_for(c, chunk);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  void* hc = ws + L.off_hc;
+  void* hd = ws + L.off_hd;
+  uint32_t* bits = reinterpret_cast<uint32_t*>(ws + L.off_bits);
+  const int64_t words = L.S / 32;
+  const bool f32 = c.dtype == BPC_DTYPE_F32;
+  const bool tc = !f32 && c.channels >= 64 && c.channels % 32 == 0;
+  const size_t es = esize(c.dtype);
+  const size_t wl = static_cast<size_t>(c.channels) * c.K * c.channels;
+
+  // the two steps of layer l as bipartite-conv problems on the chunk's buffers
+  GmmProblem c2d, d2c;
+  c2d.x = hc;
+  c2d.x_shot_stride = c.channels;
+  c2d.x_node_stride = L.S * c.channels;
+  c2d.NS = c.n_checks;
+  c2d.idx = h->c2d;
+  c2d.NT = c.n_data;
+  c2d.K = c.K;
+  c2d.Ci = c2d.Co = c.channels;
+  c2d.y = hd;
+  c2d.y_shot_stride = c.channels;
+  c2d.y_node_stride = L.S * c.channels;
+  c2d.n_wtypes = 1;
+  c2d.type_split = c.n_data;
+  d2c = c2d;
+  d2c.x = hd;
+  d2c.NS = c.n_data;
+  d2c.idx = h->d2c;
+  d2c.NT = c.n_checks;
+  d2c.y = hc;
+  d2c.n_wtypes = 2;
+  d2c.type_split = c.z_check_begin;
+  d2c.epi = kEpiGeluResid;
+
+  GmmMaps mc2d, md2c;
+  std::vector<CUtensorMap> wm_c2d, wm_d2c;
+  if (tc) {
+    c2d.shots = d2c.shots = L.S;
+    c2d.w = h->w_c2d;
+    d2c.w = h->w_d2c;
+    if (int e = gmm_tc_make_maps(c2d, &mc2d)) return e;
+    if (int e = gmm_tc_make_maps(d2c, &md2c)) return e;
+    for (int l = 0; l < c.layers; ++l) {
+      GmmMaps tmp;
+      c2d.w = static_cast<const uint8_t*>(h->w_c2d) + l * wl * es;
+      d2c.w = static_cast<const uint8_t*>(h->w_d2c) + 2 * l * wl * es;
+      if (int e = gmm_tc_make_maps(c2d, &tmp)) return e;
+      wm_c2d.push_back(tmp.w);
+      if (int e = gmm_tc_make_maps(d2c, &tmp)) return e;
+      wm_d2c.push_back(tmp.w);
+    }
+  }
+
+  size_t n_rec = 0;
+  for (int64_t b0 = 0; b0 < B; b0 += L.S) {
+    const int64_t Sb = std::min<int64_t>(L.S, B - b0);
+    {
+      dim3 grid(static_cast<unsigned>((Sb + kEmbShots - 1) / kEmbShots),
+                static_cast<unsigned>((c.n_checks + kEmbNodes - 1) / kEmbNodes));
+      if (f32)
+        embed_kernel<float><<<grid, 256, 0, stream>>>(det + b0 * c.n_checks, Sb, c.n_checks, c.channels,
+                                                      h->check_type, static_cast<const float*>(h->embed),
+                                                      static_cast<float*>(hc), L.S, bits, words);
+      else
+        embed_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
+            det + b0 * c.n_checks, Sb, c.n_checks, c.channels, h->check_type,
+            static_cast<const __nv_bfloat16*>(h->embed), static_cast<__nv_bfloat16*>(hc), L.S, bits, words);
+      cudaError_t e = cudaGetLastError();
+      if (e != cudaSuccess) return fail(BPC_ERR_LAUNCH, std::string("embed_kernel: ") + cudaGetErrorString(e));
+    }
+    c2d.shots = d2c.shots = Sb;
+    for (int l = 0; l < c.layers; ++l) {
+      c2d.w = static_cast<const uint8_t*>(h->w_c2d) + l * wl * es;
+      d2c.w = static_cast<const uint8_t*>(h->w_d2c) + 2 * l * wl * es;
+      c2d.epi = l == 0 ? kEpiGeluInit : kEpiGeluResid;
+      c2d.head = HeadEpilogue();
+      if (l == c.layers - 1) {
+        c2d.head.head_w = h->head_w;
+        c2d.head.head_b = h->head_b;
+        c2d.head.logits = logits + b0 * c.n_data * 2;
+        c2d.head.lg_shot_stride = static_cast<int64_t>(c.n_data) * 2;
+        c2d.head.lg_node_stride = 2;
+        c2d.head.res_bits = bits;
+        c2d.head.res_words = words;
+        c2d.head.xor_nbr = h->xor_nbr;
+      }
+      for (int step = 0; step < 2; ++step) {
+        const GmmProblem& p = step == 0 ? c2d : d2c;
+        const bool rec = 2 * n_rec + 1 < h->step_events.size();
+        if (rec) cudaEventRecord(h->step_events[2 * n_rec], stream);
+        int e;
+        if (tc) {
+          GmmMaps m = step == 0 ? mc2d : md2c;
+          m.w = step == 0 ? wm_c2d[l] : wm_d2c[l];
+          e = gmm_tc_launch(p, m, h->status, h->timeout_ns, stream);
+        } else {
+          e = gmm_fma_launch(p, f32, stream);
+        }
+        if (e) return e;
+        if (rec) cudaEventRecord(h->step_events[2 * n_rec + 1], stream);
+        n_rec += rec;
+      }
+    }
+    {
+      dim3 grid(static_cast<unsigned>((Sb + kEmbShots - 1) / kEmbShots),
+                static_cast<unsigned>((c.n_checks + kEmbNodes - 1) / kEmbNodes));
+      unpack_kernel<<<grid, 256, 0, stream>>>(bits, words, Sb, c.n_checks, residual + b0 * c.n_checks);
+      cudaError_t e = cudaGetLastError();
+      if (e != cudaSuccess) return fail(BPC_ERR_LAUNCH, std::string("unpack_kernel: ") + cudaGetErrorString(e));
+    }
+  }
+  return 0;
+}
+
+extern "C" int bpc_predecoder_record_step_events(bpc_predecoder* h, void* const* events, int n_pairs) {
+  if (!h || n_pairs < 0 || (n_pairs > 0 && !events)) return fail(BPC_ERR_ARG, "invalid event list");
+  h->step_events.assign(reinterpret_cast<cudaEvent_t const*>(events),
+                        reinterpret_cast<cudaEvent_t const*>(events) + 2 * static_cast<size_t>(n_pairs));
+  return 0;
+}
+
+extern "C" int bpc_predecoder_status(bpc_predecoder* h, bpc_stream_t stream, int* status) {
+  if (!h || !status) return fail(BPC_ERR_ARG, "null argument");
+  int v = 0;
+  cudaError_t e = cudaMemcpyAsync(&v, h->status, sizeof(int), cudaMemcpyDeviceToHost,
+                                  reinterpret_cast<cudaStream_t>(stream));
+  if (e == cudaSuccess) e = cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(BPC_ERR_LAUNCH, std::string("status read: ") + cudaGetErrorString(e));
+  *status = v;
+  if (v != 0) {
+    const int zero = 0;
+    cudaMemcpy(h->status, &zero, sizeof(int), cudaMemcpyHostToDevice);
+    return fail(BPC_ERR_DEVICE, "a kernel watchdog fired (status " + std::to_string(v) + ")");
+  }
+  return 0;
+}
+
+extern "C" void bpc_predecoder_destroy(bpc_predecoder* h) {
+  if (!h) return;
+  for (void* p : {static_cast<void*>(h->c2d), static_cast<void*>(h->d2c), static_cast<void*>(h->xor_nbr),
+                  static_cast<void*>(h->check_type), h->embed, h->w_c2d, h->w_d2c, static_cast<void*>(h->head_w),
+                  static_cast<void*>(h->head_b), static_cast<void*>(h->status)})
+    if (p) cudaFree(p);
+  delete h;
+}

@@ -1,0 +1,165 @@
+"""Modules on the B200 kernels: BipartiteConv (drop-in for the reference's module) and PreDecoder.
+
+BipartiteConv(C, geo, impl) keeps the reference's constructor, parameter names (w_c2d, w_d2c: one (C, K C) matrix per
+target type), registered tables (c2d{k}, inv_c2d{k}, d2c{k}, inv_d2c{k}) and forward (cascade_net.py:213-233).  It
+takes the reference's Geometry (BB codes, K = 12) or geometry.RotatedSurface (K = 8).
+
+PreDecoder(geo, cfg, params) runs the whole rotated-surface pre-decoder (params.py) in one C-ABI call per batch:
+forward(det) -> (logits (B, N_d, 2) fp32, residual (B, N_c) uint8).
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+import numpy as np
+import torch
+from torch import nn
+
+from . import _lib
+from .ops import gather_mm
+
+
+class BipartiteConv(nn.Module):
+    """check -> data -> check at width C, linear and bias-free (cascade_net.py:213-233).  impl is kept for the
+    reference's signature; every impl runs the B200 kernels."""
+
+    def __init__(self, C, geo, impl="b200"):
+        super().__init__()
+        self.C, self.impl = C, impl
+        K = int(np.asarray(geo.c2d[0]).shape[1])
+        self.K = K
+        std = 1 / math.sqrt(K * C)
+        self.w_c2d = nn.ParameterList([nn.Parameter(torch.randn(C, K * C) * std) for _ in range(len(geo.c2d))])
+        self.w_d2c = nn.ParameterList([nn.Parameter(torch.randn(C, K * C) * std) for _ in range(len(geo.d2c))])
+        for name in ("c2d", "d2c"):
+            for k in range(len(getattr(geo, name))):
+                self.register_buffer(f"{name}{k}", torch.as_tensor(np.asarray(getattr(geo, name)[k])),
+                                     persistent=False)
+                self.register_buffer(f"inv_{name}{k}", torch.as_tensor(np.asarray(getattr(geo, "inv_" + name)[k])),
+                                     persistent=False)
+
+    def forward(self, x):                               # (B, N checks, C) -> (B, N checks, C)
+        data = torch.cat([gather_mm(x, self.w_c2d[d], getattr(self, f"c2d{d}"), getattr(self, f"inv_c2d{d}"))
+                          for d in range(len(self.w_c2d))], 1)
+        return torch.cat([gather_mm(data, self.w_d2c[c], getattr(self, f"d2c{c}"), getattr(self, f"inv_d2c{c}"))
+                          for c in range(len(self.w_d2c))], 1)
+
+
+class PreDecoder:
+    """The rotated-surface pre-decoder on one GPU through libbpc.so (bpc_predecoder_*).
+
+    geo: geometry.RotatedSurface; cfg: params.PreDecoderConfig; params: params.init_params-style dict (fp32 numpy).
+    chunk_shots: shots per pass through the network (sets the workspace: 2 x (N_c + N_d) x C activations)."""
+
+    def __init__(self, geo, cfg, params, device=None, chunk_shots: int = 16384):
+        self.geo, self.cfg = geo, cfg
+        self.device = torch.device(device if device is not None else "cuda")
+        if self.device.type != "cuda":
+            raise RuntimeError("PreDecoder runs on a CUDA device only (no CPU path)")
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        if cfg.K != geo.K or cfg.d != geo.d or cfg.rounds != geo.R:
+            raise ValueError("configuration and geometry disagree")
+        self.dtype = _lib.BPC_DTYPE_BF16 if cfg.dtype == "bf16" else _lib.BPC_DTYPE_F32
+        L = _lib.lib()
+        c = _lib.PredecoderConfig(cfg.layers, cfg.channels, cfg.K, self.dtype, geo.N_c, geo.N_d, geo.T * geo.nh)
+        self._keep = {
+            "c2d": np.ascontiguousarray(geo.c2d[0], np.int32),
+            "d2c": np.ascontiguousarray(geo.d2c_all, np.int32),
+            "xor": np.ascontiguousarray(geo.xor_nbr, np.int32),
+            "ctype": np.ascontiguousarray(geo.check_type, np.uint8),
+        }
+        h = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            _lib.check(L.bpc_predecoder_create(ctypes.byref(c), *(a.ctypes.data for a in self._keep.values()),
+                                               ctypes.byref(h)), "bpc_predecoder_create")
+        self._h = h
+        self.set_weights(params)
+        self.chunk_shots = int(chunk_shots)
+        self._ws = None
+
+    def set_weights(self, params: dict) -> None:
+        cfg = self.cfg
+
+        def conv(a):
+            t = torch.as_tensor(np.ascontiguousarray(a, np.float32))
+            if cfg.dtype == "bf16":
+                return t.to(torch.bfloat16).contiguous()
+            return t.contiguous()
+
+        emb = conv(params["embed"])
+        wc = conv(np.asarray(params["w_c2d"]).reshape(cfg.layers, cfg.channels, cfg.K * cfg.channels))
+        wd = conv(np.asarray(params["w_d2c"]).reshape(cfg.layers, 2, cfg.channels, cfg.K * cfg.channels))
+        hw = np.ascontiguousarray(params["head_w"], np.float32)
+        hb = np.ascontiguousarray(params["head_b"], np.float32)
+        with torch.cuda.device(self.device):
+            _lib.check(_lib.lib().bpc_predecoder_set_weights(self._h, emb.data_ptr(), wc.data_ptr(), wd.data_ptr(),
+                                                             hw.ctypes.data, hb.ctypes.data),
+                       "bpc_predecoder_set_weights")
+
+    def workspace_bytes(self, shots: int) -> int:
+        return int(_lib.lib().bpc_predecoder_workspace_size(self._h, int(shots)))
+
+    def _workspace(self, B: int) -> torch.Tensor:
+        want = self.workspace_bytes(min(max(B, 1), self.chunk_shots))
+        if self._ws is None or self._ws.numel() < want:
+            self._ws = torch.empty(want, dtype=torch.uint8, device=self.device)
+        return self._ws
+
+    def forward_into(self, det: torch.Tensor, logits: torch.Tensor, residual: torch.Tensor) -> None:
+        """det (B, N_c) uint8 -> logits (B, N_d, 2) fp32, residual (B, N_c) uint8, all on this device."""
+        B = det.shape[0]
+        for t, shape, dt in ((det, (B, self.geo.N_c), torch.uint8), (logits, (B, self.geo.N_d, 2), torch.float32),
+                             (residual, (B, self.geo.N_c), torch.uint8)):
+            if t.device != self.device or tuple(t.shape) != shape or t.dtype != dt or not t.is_contiguous():
+                raise ValueError(f"expected a contiguous {dt} tensor {shape} on {self.device}")
+        if B == 0:
+            return
+        ws = self._workspace(B)
+        rc = _lib.lib().bpc_predecoder_forward(self._h, det.data_ptr(), logits.data_ptr(), residual.data_ptr(), B,
+                                               ws.data_ptr(), ws.numel(),
+                                               torch.cuda.current_stream(self.device).cuda_stream)
+        _lib.check(rc, "bpc_predecoder_forward")
+
+    def forward(self, det: torch.Tensor):
+        """det (B, N_c) uint8 on this device -> (logits (B, N_d, 2) fp32, residual (B, N_c) uint8)."""
+        det = det.to(self.device, torch.uint8).contiguous()
+        B = det.shape[0]
+        logits = torch.empty(B, self.geo.N_d, 2, dtype=torch.float32, device=self.device)
+        residual = torch.empty(B, self.geo.N_c, dtype=torch.uint8, device=self.device)
+        self.forward_into(det, logits, residual)
+        return logits, residual
+
+    __call__ = forward
+
+    def record_step_events(self, pairs) -> None:
+        """pairs: list of (start, end) torch.cuda.Event(enable_timing=True); the next forward calls record them
+        around their bipartite-step launches in launch order (empty list: off)."""
+        flat = [e for pr in pairs for e in pr]
+        for e in flat:
+            e.record()                                   # make torch create the underlying CUDA event
+        torch.cuda.synchronize(self.device)
+        arr = (ctypes.c_void_p * max(1, len(flat)))(*[e.cuda_event for e in flat])
+        _lib.check(_lib.lib().bpc_predecoder_record_step_events(self._h, arr, len(pairs)),
+                   "bpc_predecoder_record_step_events")
+        self._step_events = flat
+
+    def status(self) -> int:
+        """Device watchdog status (0 = every wait completed); synchronises the current stream, raises otherwise."""
+        s = ctypes.c_int(0)
+        rc = _lib.lib().bpc_predecoder_status(self._h, torch.cuda.current_stream(self.device).cuda_stream,
+                                              ctypes.byref(s))
+        _lib.check(rc, "bpc_predecoder_status")
+        return s.value
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            _lib.lib().bpc_predecoder_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,108 @@
+/* bpc.h -- C ABI of the B200 bipartite-conv pre-decoder library (libbpc.so).
+ *
+ * Plain pointers and sizes only.  Every device pointer is caller-owned device memory, every launch goes on the
+ * caller's stream (a cudaStream_t passed as bpc_stream_t; 0 = the legacy default stream), and no entry point
+ * allocates device memory after bpc_predecoder_create / bpc_predecoder_set_weights.  Every function returns
+ * BPC_OK (0) or an error code; bpc_last_error() gives the calling thread's last message.  The reference's host side
+ * returns 0 / non-0 with an error buffer in the same way (evaluation/timing/d7/router.cc:229,380).
+ */
+#ifndef BPC_H_
+#define BPC_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define BPC_API __attribute__((visibility("default")))
+#else
+#define BPC_API
+#endif
+
+typedef struct CUstream_st* bpc_stream_t;
+
+enum {
+  BPC_OK = 0,
+  BPC_ERR_ARG = 2,      /* invalid shape, stride, alignment or dtype */
+  BPC_ERR_DRIVER = 3,   /* the CUDA driver lacks an entry point or rejected a tensor map */
+  BPC_ERR_LAUNCH = 4,   /* a kernel launch or CUDA runtime call failed */
+  BPC_ERR_DEVICE = 5,   /* a kernel reported a watchdog timeout through the status word */
+  BPC_ERR_SPACE = 6     /* the workspace is smaller than bpc_predecoder_workspace_size() */
+};
+
+enum { BPC_DTYPE_F32 = 0, BPC_DTYPE_BF16 = 1 };
+
+/* Library version, (major << 16) | minor. */
+BPC_API int bpc_version(void);
+
+/* Copies the calling thread's last error message (NUL-terminated, truncated to len) and returns its length. */
+BPC_API int bpc_last_error(char* buf, int len);
+
+/* One bipartite-convolution step, the reference's gather_mm forward:
+ *   y[b, n, :] = sum_r x[b, idx[n, r], :] W_r^T,   W (Co, K*Ci) row-major, W_r = W[:, r*Ci:(r+1)*Ci]
+ * x (B, NS, Ci), y (B, NT, Co), idx (NT, K) int32 with NS (or any value outside [0, NS)) reading a zero row.
+ * dtype BPC_DTYPE_BF16: bf16 x / w / y, fp32 accumulation (tcgen05 tensor cores when Ci >= 64, Co % 32 == 0,
+ * Co <= 256; CUDA cores otherwise); BPC_DTYPE_F32: fp32 throughout on the CUDA cores.
+ * Replaces: training/bb/ising_compare/bb/cascade_net.py:140-153,174-175 (_GatherMM.forward / gather_mm) and
+ * cascade_triton.py:100-117,139-148 (gmm with transposed=False, the op cascade::gmm). */
+BPC_API int bpc_gather_mm_fwd(const void* x, const void* w, const int32_t* idx, void* y, int64_t B, int32_t NS, int32_t NT,
+                      int32_t K, int32_t Ci, int32_t Co, int32_t dtype, bpc_stream_t stream);
+
+/* ------------------------------------------------------------------------------------------------------------
+ * Pre-decoder: detectors (B, N_c) uint8 -> per-data-node X/Z logits (B, N_d, 2) fp32 and the residual syndrome
+ * (B, N_c) uint8, through `layers` x [check -> data, data -> check] bipartite convolutions of width `channels`.
+ * Replaces the module stack BipartiteConv.forward / CascadeBB.forward (cascade_net.py:228-233,342-343) for the
+ * rotated surface code; the X/Z head and the syndrome cancellation have no reference counterpart in-tree (the
+ * reference calls NVIDIA Ising-Decoding's pre-decoder for the residual, evaluation/convlines/opponents.py:43-86). */
+typedef struct bpc_predecoder bpc_predecoder;
+
+typedef struct {
+  int32_t layers;          /* L */
+  int32_t channels;        /* C */
+  int32_t K;               /* relations per target (8 for the rotated surface code) */
+  int32_t dtype;           /* BPC_DTYPE_BF16 or BPC_DTYPE_F32 */
+  int32_t n_checks;        /* N_c */
+  int32_t n_data;          /* N_d */
+  int32_t z_check_begin;   /* first Z-check node: checks [0, z) use the X weights of a data -> check step */
+} bpc_predecoder_config;
+
+/* Tables (host memory, copied): c2d (N_d, K) int32 source check per data node (N_c = pad), d2c (N_c, K) int32 source
+ * data node per check (N_d = pad), xor_nbr (N_d, 2, 2) int32 checks flipped by a predicted X / Z flip (-1 = none),
+ * check_type (N_c) uint8 0 X / 1 Z.  Allocates the handle's device tables and weights. */
+BPC_API int bpc_predecoder_create(const bpc_predecoder_config* cfg, const int32_t* c2d, const int32_t* d2c,
+                          const int32_t* xor_nbr, const uint8_t* check_type, bpc_predecoder** out);
+
+/* Weights (host memory, copied; element type = cfg.dtype except head_w / head_b which are fp32):
+ * embed (4, C); w_c2d (L, C, K*C); w_d2c (L, 2, C, K*C) (X then Z checks); head_w (2, C); head_b (2). */
+BPC_API int bpc_predecoder_set_weights(bpc_predecoder* h, const void* embed, const void* w_c2d, const void* w_d2c,
+                               const float* head_w, const float* head_b);
+
+/* Workspace bytes that let bpc_predecoder_forward process `chunk_shots` shots per pass (rounded up to 128). */
+BPC_API size_t bpc_predecoder_workspace_size(const bpc_predecoder* h, int64_t chunk_shots);
+
+/* Forward pass on device buffers: det (B, N_c) uint8, logits (B, N_d, 2) fp32, residual (B, N_c) uint8.  Shots are
+ * processed in chunks of the size the workspace allows; nothing is allocated.  Asynchronous on `stream`. */
+BPC_API int bpc_predecoder_forward(bpc_predecoder* h, const uint8_t* det, float* logits, uint8_t* residual, int64_t B,
+                           void* workspace, size_t workspace_bytes, bpc_stream_t stream);
+
+/* Measurement hook: `events` holds 2 * n_pairs cudaEvent_t created by the caller (timing enabled).  Every later
+ * bpc_predecoder_forward records events[2 i] just before and events[2 i + 1] just after its i-th bipartite-step
+ * launch (i counts from 0 in each call, in launch order: per chunk, per layer, check -> data then data -> check), for
+ * as many launches as there are pairs.  n_pairs = 0 turns it off.  No reference counterpart (the reference times
+ * whole CUDA-graph replays, evaluation/timing/gpu_term.py:5-10). */
+BPC_API int bpc_predecoder_record_step_events(bpc_predecoder* h, void* const* events, int n_pairs);
+
+/* Reads (and clears) the device status word the kernels' watchdogs write; synchronises `stream`.
+ * *status = 0 when every wait completed.  Returns BPC_ERR_DEVICE when a watchdog fired. */
+BPC_API int bpc_predecoder_status(bpc_predecoder* h, bpc_stream_t stream, int* status);
+
+BPC_API void bpc_predecoder_destroy(bpc_predecoder* h);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BPC_H_ */

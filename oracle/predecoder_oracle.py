@@ -1,0 +1,136 @@
+"""CPU oracle of the bipartite-conv pre-decoder path -- TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg may import this module, and only as the checker
+(or the timed CPU baseline): the product path (codecoder_b200) never calls it.
+
+What it restates:
+  gather_mm      the reference's _GatherMM.forward (training/bb/ising_compare/bb/cascade_net.py:146-153): pad the
+                 sources with a zero row, index_select by the (NT, K) table, one matmul with W^T (C_out, K C_in).
+                 gather_mm_loop is the literal per-relation sum y = sum_r x[idx[:, r]] W_r^T of the Triton kernel's
+                 docstring (cascade_triton.py:5,40) for small cases.
+  bipartite_conv BipartiteConv.forward (cascade_net.py:228-233): check -> data for every data type, concatenated,
+                 then data -> check for every check type.
+  predecoder     the rotated-surface pre-decoder of codecoder_b200.params (embed, L x [c2d, GELU, residual;
+                 d2c, GELU, residual], X / Z head, threshold, XOR cancellation).  Storage rounding is emulated: a
+                 bf16 network rounds every stored activation to bf16 exactly where the device stores bf16, and
+                 accumulates in float64 here (fp32 on the device).
+  cancel         the GF(2) syndrome cancellation, integer numpy.
+Parity pin: tests/golden/*.npz were produced by the reference's own gather_mm / BipartiteConv (imported from the
+reference tree by tests/golden/make_golden.py); tests/test_oracle.py checks this module against them.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+
+def gather_mm(x: torch.Tensor, w: torch.Tensor, idx) -> torch.Tensor:
+    """y[b, n] = W cat_r x[b, idx[n, r]], idx == NS reads a zero row (cascade_net.py:146-153)."""
+    idx = torch.as_tensor(np.asarray(idx), dtype=torch.int64)
+    B, N, C = x.shape
+    nt, K = idx.shape
+    xp = torch.cat([x, x.new_zeros(B, 1, C)], 1)
+    g = xp.index_select(1, idx.reshape(-1)).view(B, nt, K * C)
+    return g @ w.t()
+
+
+def gather_mm_loop(x: np.ndarray, w: np.ndarray, idx: np.ndarray) -> np.ndarray:
+    """Literal per-relation form in float64 (small cases only)."""
+    B, N, C = x.shape
+    nt, K = idx.shape
+    co = w.shape[0]
+    y = np.zeros((B, nt, co))
+    x64 = x.astype(np.float64)
+    w64 = w.astype(np.float64).reshape(co, K, C)
+    for r in range(K):
+        src = idx[:, r]
+        ok = src < N
+        y[:, ok] += x64[:, src[ok]] @ w64[:, r].T
+    return y
+
+
+def bipartite_conv(x, w_c2d, w_d2c, c2d, d2c):
+    """check features (B, N_c, C) -> check features (B, N_c, C), linear (cascade_net.py:228-233)."""
+    data = torch.cat([gather_mm(x, w, t) for w, t in zip(w_c2d, c2d)], 1)
+    return torch.cat([gather_mm(data, w, t) for w, t in zip(w_d2c, d2c)], 1)
+
+
+def _store(a: torch.Tensor, bf16: bool) -> torch.Tensor:
+    return a.to(torch.bfloat16).to(a.dtype) if bf16 else a
+
+
+def cancel(det: np.ndarray, e: np.ndarray, geo) -> np.ndarray:
+    """residual[c] = det[c] ^ XOR over data nodes n with c in xor_nbr[n, j] of e[n, j] (uint8 in, uint8 out)."""
+    det = np.asarray(det, np.uint8)
+    res = det.copy()
+    B = det.shape[0]
+    nbr = geo.xor_nbr
+    for j in range(2):
+        for k in range(2):
+            c = nbr[:, j, k]
+            ok = c >= 0
+            flips = e[:, ok, j].astype(np.uint8)             # (B, n_ok)
+            np.bitwise_xor.at(res, (np.arange(B)[:, None], c[ok][None, :]), flips)
+    return res
+
+
+def predecoder(geo, cfg, params: dict, det: np.ndarray, dtype=torch.float64, return_features: bool = False):
+    """Full forward -> (logits (B, N_d, 2) float64, residual (B, N_c) uint8[, h_c, h_d])."""
+    bf16 = cfg.dtype == "bf16"
+    det_t = torch.as_tensor(np.asarray(det, np.uint8)).long()
+    tok = 2 * torch.as_tensor(geo.check_type) + det_t
+    emb = torch.as_tensor(params["embed"]).to(dtype)
+    hc = _store(emb[tok], bf16)
+    B = det_t.shape[0]
+    hd = None
+    c2d = geo.c2d
+    d2c = geo.d2c
+    for layer in range(cfg.layers):
+        wc = [_store(torch.as_tensor(w).to(dtype), bf16) for w in params["w_c2d"][layer]]
+        wd = [_store(torch.as_tensor(w).to(dtype), bf16) for w in params["w_d2c"][layer]]
+        acc = torch.cat([gather_mm(hc, w, t) for w, t in zip(wc, c2d)], 1)
+        upd = F.gelu(acc)
+        hd = _store(upd if hd is None else hd + upd, bf16)
+        acc = torch.cat([gather_mm(hd, w, t) for w, t in zip(wd, d2c)], 1)
+        hc = _store(hc + F.gelu(acc), bf16)
+    hw = torch.as_tensor(params["head_w"]).to(dtype)
+    hb = torch.as_tensor(params["head_b"]).to(dtype)
+    logits = hd @ hw.t() + hb
+    e = (logits > 0).numpy().astype(np.uint8)
+    residual = cancel(det, e, geo)
+    if return_features:
+        return logits.numpy(), residual, hc.numpy(), hd.numpy()
+    return logits.numpy(), residual
+
+
+def band_mask(logits_ref: np.ndarray, tol: float) -> np.ndarray:
+    """Data-node logits within tol x RMS of zero: their sign, and so the residual bits around them, may differ
+    between two correct implementations."""
+    rms = float(np.sqrt(np.mean(np.square(logits_ref)))) if logits_ref.size else 1.0
+    return np.abs(logits_ref) < tol * max(rms, 1e-30)
+
+
+def logit_error(logits: np.ndarray, logits_ref: np.ndarray) -> float:
+    """max |a - b| / max(|b|, rms(b)) over all entries (a relative error that stays finite near zero)."""
+    if logits_ref.size == 0:
+        return 0.0
+    rms = float(np.sqrt(np.mean(np.square(logits_ref))))
+    den = np.maximum(np.abs(logits_ref), max(rms, 1e-30))
+    return float(np.max(np.abs(logits - logits_ref) / den))
+
+
+def residual_mismatch_outside_band(res, res_ref, logits_ref, geo, tol) -> int:
+    """Residual bits that differ at checks none of whose cancelling data nodes lies in the band."""
+    band = band_mask(logits_ref, tol)                     # (B, N_d, 2)
+    B = res.shape[0]
+    touched = np.zeros((B, geo.N_c), bool)
+    nbr = geo.xor_nbr
+    for j in range(2):
+        for k in range(2):
+            c = nbr[:, j, k]
+            ok = c >= 0
+            bi, ni = np.nonzero(band[:, ok, j])
+            touched[bi, c[ok][ni]] = True
+    diff = (np.asarray(res) != np.asarray(res_ref)) & ~touched
+    return int(diff.sum())

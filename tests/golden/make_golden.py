@@ -1,0 +1,158 @@
+"""Generate the golden fixtures of tests/golden from the reference's own code.
+
+Run in a checkout that has the reference tree (default /root/reference, or REFERENCE_ROOT):
+    python tests/golden/make_golden.py
+It imports the reference's bb.cascade_net (training/bb/ising_compare/bb/cascade_net.py) unchanged and records:
+  bb72_c14_conv.npz      the reference's Geometry('bb72') tables, the trained relation matrices of the released C14
+                         network's first block (weights/cascade_bb72/C14.pt, key 'ema', rounded to bf16), a seeded
+                         input, and the outputs of the reference's gather_mm, gather_mm_ref and BipartiteConv.forward
+                         (fp32, CPU)
+  surface_gmm.npz        the rotated-surface tables of codecoder_b200.geometry run through the reference's gather_mm
+                         (several channel widths, including C_in != C_out)
+  predecoder_<cfg>.npz   the pre-decoder composed from the reference's gather_mm on seeded shots: det, logits,
+                         residual (weights regenerate from the stored seed with codecoder_b200.params.init_params)
+The fixtures are small; the device never reads the reference tree.
+"""
+import hashlib
+import os
+import sys
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+REF = os.environ.get("REFERENCE_ROOT", "/root/reference")
+sys.path[:0] = [REPO, os.path.join(REF, "training/bb/ising_compare"), os.path.join(REF, "training/bb/qldpc_neural")]
+
+from bb import cascade_net as cn  # noqa: E402  (the reference, unchanged)
+
+from codecoder_b200.geometry import RotatedSurface  # noqa: E402
+from codecoder_b200.params import CONFIGS, init_params, round_bf16, storage_params  # noqa: E402
+from codecoder_b200.sampler import sample  # noqa: E402
+
+
+def bf16_bits(a):
+    return (np.ascontiguousarray(round_bf16(a)).view(np.uint32) >> 16).astype(np.uint16)
+
+
+def params_sha(params):
+    h = hashlib.sha256()
+    for k in sorted(params):
+        h.update(k.encode())
+        h.update(np.ascontiguousarray(params[k], np.float32).tobytes())
+    return h.hexdigest()
+
+
+def make_bb72():
+    geo = cn.Geometry("bb72")
+    ck = torch.load(os.path.join(REF, "weights/cascade_bb72/C14.pt"), map_location="cpu", weights_only=False)
+    ema = ck["ema"]
+    C = ck["cfg"]["H"] // 4
+    conv = cn.BipartiteConv(C, geo, impl="torch")
+    names = ["w_c2d.0", "w_c2d.1", "w_d2c.0", "w_d2c.1"]
+    ws = {n: torch.as_tensor(round_bf16(ema["blocks.0.conv." + n].float().numpy())) for n in names}
+    with torch.no_grad():
+        conv.w_c2d[0].copy_(ws["w_c2d.0"])
+        conv.w_c2d[1].copy_(ws["w_c2d.1"])
+        conv.w_d2c[0].copy_(ws["w_d2c.0"])
+        conv.w_d2c[1].copy_(ws["w_d2c.1"])
+    rng = np.random.default_rng(1401)
+    B = 2
+    x = torch.as_tensor(round_bf16(rng.standard_normal((B, geo.N, C)).astype(np.float32)))
+    with torch.no_grad():
+        y_mod = conv(x)
+        y0 = cn.gather_mm(x, conv.w_c2d[0], torch.as_tensor(geo.c2d[0]), torch.as_tensor(geo.inv_c2d[0]))
+        y0_ref = cn.gather_mm_ref(x, conv.w_c2d[0], torch.as_tensor(geo.c2d[0]))
+    assert torch.allclose(y0, y0_ref, atol=1e-4), "reference gather_mm != gather_mm_ref"
+    out = {"x_bf16": bf16_bits(x.numpy()), "y_module": y_mod.numpy(), "y_c2d0": y0.numpy(), "C": C, "B": B,
+           "N": geo.N, "T": geo.T, "n2": geo.n2}
+    for n in names:
+        out[n.replace(".", "_") + "_bf16"] = bf16_bits(ws[n].numpy())
+    for k in range(2):
+        out[f"c2d{k}"] = geo.c2d[k].astype(np.int32)
+        out[f"d2c{k}"] = geo.d2c[k].astype(np.int32)
+        out[f"inv_c2d{k}"] = geo.inv_c2d[k].astype(np.int32)
+        out[f"inv_d2c{k}"] = geo.inv_d2c[k].astype(np.int32)
+    np.savez_compressed(os.path.join(HERE, "bb72_c14_conv.npz"), **out)
+    print("bb72_c14_conv", {k: getattr(v, "shape", v) for k, v in out.items()})
+
+
+def make_surface_gmm():
+    out = {}
+    rng = np.random.default_rng(1402)
+    cases = [("d5_c64", 5, 5, 64, 64, 3), ("d5_c128", 5, 5, 128, 128, 2), ("d3_ci64_co128", 3, 3, 64, 128, 5),
+             ("d3_c96", 3, 3, 96, 96, 4), ("d5_c32", 5, 5, 32, 32, 4)]
+    for name, d, R, ci, co, B in cases:
+        geo = RotatedSurface(d, R)
+        for step, idx, ns in (("c2d", geo.c2d[0], geo.N_c), ("d2c", geo.d2c_all, geo.N_d)):
+            x = round_bf16(rng.standard_normal((B, ns, ci)).astype(np.float32))
+            w = round_bf16((rng.standard_normal((co, geo.K * ci)) / np.sqrt(geo.K * ci)).astype(np.float32))
+            inv = geo.inverse(idx, ns)
+            with torch.no_grad():
+                y = cn.gather_mm(torch.as_tensor(x), torch.as_tensor(w), torch.as_tensor(idx), torch.as_tensor(inv))
+            key = f"{name}_{step}"
+            out[key + "_x"] = bf16_bits(x)
+            out[key + "_w"] = bf16_bits(w)
+            out[key + "_idx"] = idx.astype(np.int32)
+            out[key + "_y"] = y.numpy()
+            out[key + "_meta"] = np.array([d, R, ci, co, B, ns], np.int64)
+    np.savez_compressed(os.path.join(HERE, "surface_gmm.npz"), **out)
+    print("surface_gmm", len(out) // 5, "cases")
+
+
+def reference_predecoder(geo, cfg, params, det):
+    """The pre-decoder composed from the reference's gather_mm (fp32, CPU), bf16 storage rounding for a bf16
+    network applied where the device stores bf16."""
+    bf = cfg.dtype == "bf16"
+
+    def st(a):
+        return a.to(torch.bfloat16).float() if bf else a
+
+    p = storage_params(cfg, params)
+    det_t = torch.as_tensor(det).long()
+    tok = 2 * torch.as_tensor(geo.check_type) + det_t
+    hc = st(torch.as_tensor(p["embed"])[tok])
+    hd = None
+    for layer in range(cfg.layers):
+        acc = torch.cat([cn.gather_mm(hc, torch.as_tensor(w), torch.as_tensor(t), torch.as_tensor(geo.inverse(t, geo.N_c)))
+                         for w, t in zip(p["w_c2d"][layer], geo.c2d)], 1)
+        hd = st(F.gelu(acc) if hd is None else hd + F.gelu(acc))
+        acc = torch.cat([cn.gather_mm(hd, torch.as_tensor(w), torch.as_tensor(t), torch.as_tensor(geo.inverse(t, geo.N_d)))
+                         for w, t in zip(p["w_d2c"][layer], geo.d2c)], 1)
+        hc = st(hc + F.gelu(acc))
+    logits = hd @ torch.as_tensor(p["head_w"]).t() + torch.as_tensor(p["head_b"])
+    e = (logits > 0).numpy().astype(np.uint8)
+    res = det.astype(np.uint8).copy()
+    for n in range(geo.N_d):                      # literal per-node XOR loop (small cases)
+        for j in range(2):
+            for c in geo.xor_nbr[n, j]:
+                if c >= 0:
+                    res[:, c] ^= e[:, n, j]
+    return logits.numpy(), res, hc.numpy()
+
+
+def make_predecoder():
+    from dataclasses import replace
+    cases = [("d3_fp32", replace(CONFIGS["d5_fp32"], d=3, rounds=3, layers=2, channels=32), 64),
+             ("d5_fp32", CONFIGS["d5_fp32"], 64),
+             ("d5_bf16_c64", replace(CONFIGS["d9_bf16"], d=5, rounds=5, layers=3, channels=64), 32)]
+    for name, cfg, B in cases:
+        geo = RotatedSurface(cfg.d, cfg.rounds)
+        seed = 7000 + cfg.d
+        params = init_params(cfg, seed)
+        det, err = sample(geo, cfg.p * 10, B, seed + 1)       # denser than the workload so the fixture has events
+        with torch.no_grad():
+            logits, res, hc = reference_predecoder(geo, cfg, params, det)
+        np.savez_compressed(os.path.join(HERE, f"predecoder_{name}.npz"), det=det, logits=logits, residual=res,
+                            seed=seed, d=cfg.d, rounds=cfg.rounds, layers=cfg.layers,
+                            channels=cfg.channels, dtype=cfg.dtype, params_sha256=params_sha(params))
+        print("predecoder", name, det.shape, logits.shape, float(np.abs(logits).mean()))
+
+
+if __name__ == "__main__":
+    torch.manual_seed(0)
+    make_bb72()
+    make_surface_gmm()
+    make_predecoder()

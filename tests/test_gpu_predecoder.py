@@ -1,0 +1,111 @@
+"""The pre-decoder on the GPU through the C ABI against the golden fixtures and the CPU oracle.
+
+Parity bar: logits within 1e-4 (fp32 network) or 2e-2 (bf16 network) of the oracle, relative to max(|ref|, rms(ref));
+residual syndromes bit-exact at every check none of whose cancelling data nodes has an oracle logit inside that band
+around zero (those are counted and reported); and bit-exact against the XOR of the GPU's own thresholded logits."""
+import os
+from dataclasses import replace
+
+import numpy as np
+import pytest
+import torch
+
+from codecoder_b200.geometry import RotatedSurface
+from codecoder_b200.modules import PreDecoder
+from codecoder_b200.params import CONFIGS, PreDecoderConfig, init_params, storage_params
+from codecoder_b200.sampler import sample
+from oracle import predecoder_oracle as orc
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def run(cfg, seed, B, p=None, chunk_shots=16384, oracle_dtype=torch.float64):
+    g = RotatedSurface(cfg.d, cfg.rounds)
+    params = init_params(cfg, seed)
+    det, _ = sample(g, p if p is not None else cfg.p, B, seed + 1)
+    pd = PreDecoder(g, cfg, params, device=DEV, chunk_shots=chunk_shots)
+    logits, res = pd(torch.as_tensor(det).to(DEV))
+    torch.cuda.synchronize()
+    assert pd.status() == 0
+    lg, rs = logits.cpu().numpy(), res.cpu().numpy()
+    ref_lg, ref_rs = orc.predecoder(g, cfg, storage_params(cfg, params), det, dtype=oracle_dtype)
+    return g, det, lg, rs, ref_lg, ref_rs, pd
+
+
+def check_parity(g, cfg, det, lg, rs, ref_lg, ref_rs):
+    tol = 1e-4 if cfg.dtype == "f32" else 2e-2
+    err = orc.logit_error(lg, ref_lg)
+    assert err < tol, f"logit error {err}"
+    # the cancellation kernel is exact on the GPU's own logits
+    assert np.array_equal(orc.cancel(det, (lg > 0).astype(np.uint8), g), rs)
+    bad = orc.residual_mismatch_outside_band(rs, ref_rs, ref_lg, g, tol)
+    assert bad == 0
+    return int(orc.band_mask(ref_lg, tol).sum())
+
+
+@pytest.mark.parametrize("name", ["d3_fp32", "d5_fp32", "d5_bf16_c64"])
+def test_predecoder_golden(golden_dir, name):
+    z = np.load(os.path.join(golden_dir, f"predecoder_{name}.npz"))
+    cfg = PreDecoderConfig(d=int(z["d"]), rounds=int(z["rounds"]), layers=int(z["layers"]),
+                           channels=int(z["channels"]), dtype=str(z["dtype"]))
+    g = RotatedSurface(cfg.d, cfg.rounds)
+    params = init_params(cfg, int(z["seed"]))
+    pd = PreDecoder(g, cfg, params, device=DEV)
+    logits, res = pd(torch.as_tensor(z["det"]).to(DEV))
+    lg, rs = logits.cpu().numpy(), res.cpu().numpy()
+    check_parity(g, cfg, z["det"], lg, rs, z["logits"], z["residual"])
+
+
+def test_predecoder_d5_fp32_config():
+    cfg = CONFIGS["d5_fp32"]
+    g, det, lg, rs, ref_lg, ref_rs, _ = run(cfg, 101, 1024)
+    check_parity(g, cfg, det, lg, rs, ref_lg, ref_rs)
+
+
+def test_predecoder_d9_bf16_config():
+    cfg = CONFIGS["d9_bf16"]
+    g, det, lg, rs, ref_lg, ref_rs, _ = run(cfg, 202, 200, p=0.02)
+    band = check_parity(g, cfg, det, lg, rs, ref_lg, ref_rs)
+    print("d9 band logits", band, "of", ref_lg.size)
+
+
+def test_predecoder_d13_bf16_config():
+    cfg = CONFIGS["d13_bf16"]
+    g, det, lg, rs, ref_lg, ref_rs, _ = run(cfg, 303, 48, p=0.02, oracle_dtype=torch.float32)
+    band = check_parity(g, cfg, det, lg, rs, ref_lg, ref_rs)
+    print("d13 band logits", band, "of", ref_lg.size)
+
+
+def test_predecoder_d11_c96_tensor_path():
+    cfg = CONFIGS["d11_train"]          # C = 96: tensor cores with a zero-filled half K block
+    g, det, lg, rs, ref_lg, ref_rs, _ = run(replace(cfg, layers=2), 404, 40, p=0.02, oracle_dtype=torch.float32)
+    check_parity(g, replace(cfg, layers=2), det, lg, rs, ref_lg, ref_rs)
+
+
+def test_predecoder_chunking_and_determinism():
+    cfg = replace(CONFIGS["d9_bf16"], layers=3)
+    g = RotatedSurface(cfg.d, cfg.rounds)
+    params = init_params(cfg, 505)
+    det, _ = sample(g, 0.02, 300, 506)
+    d = torch.as_tensor(det).to(DEV)
+    one = PreDecoder(g, cfg, params, device=DEV, chunk_shots=16384)
+    many = PreDecoder(g, cfg, params, device=DEV, chunk_shots=128)     # 3 passes of 128 shots
+    a_lg, a_rs = one(d)
+    b_lg, b_rs = many(d)
+    c_lg, c_rs = one(d)
+    assert torch.equal(a_lg, b_lg) and torch.equal(a_rs, b_rs)
+    assert torch.equal(a_lg, c_lg) and torch.equal(a_rs, c_rs)
+
+
+def test_predecoder_empty_and_single_shot():
+    cfg = replace(CONFIGS["d9_bf16"], layers=2)
+    g = RotatedSurface(cfg.d, cfg.rounds)
+    params = init_params(cfg, 606)
+    pd = PreDecoder(g, cfg, params, device=DEV)
+    lg, rs = pd(torch.zeros(0, g.N_c, dtype=torch.uint8, device=DEV))
+    assert lg.shape == (0, g.N_d, 2) and rs.shape == (0, g.N_c)
+    det, _ = sample(g, 0.02, 1, 607)
+    lg, rs = pd(torch.as_tensor(det).to(DEV))
+    ref_lg, ref_rs = orc.predecoder(g, cfg, storage_params(cfg, params), det)
+    check_parity(g, cfg, det, lg.cpu().numpy(), rs.cpu().numpy(), ref_lg, ref_rs)

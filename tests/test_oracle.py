@@ -1,0 +1,80 @@
+"""The CPU oracle against the golden fixtures written by the reference's own gather_mm / BipartiteConv."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from codecoder_b200.geometry import RotatedSurface
+from codecoder_b200.params import PreDecoderConfig, init_params, storage_params
+from oracle import predecoder_oracle as orc
+
+
+def bf16_to_f32(u16):
+    return (np.asarray(u16, np.uint32) << 16).view(np.float32)
+
+
+@pytest.fixture(scope="module")
+def bb72(golden_dir):
+    return dict(np.load(os.path.join(golden_dir, "bb72_c14_conv.npz")))
+
+
+def test_oracle_gather_mm_matches_reference_bb72_c14(bb72):
+    x = torch.as_tensor(bf16_to_f32(bb72["x_bf16"]))
+    w = torch.as_tensor(bf16_to_f32(bb72["w_c2d_0_bf16"]))
+    y = orc.gather_mm(x, w, bb72["c2d0"])
+    np.testing.assert_allclose(y.numpy(), bb72["y_c2d0"], rtol=1e-5, atol=1e-5)
+    y64 = orc.gather_mm_loop(x.numpy(), w.numpy(), bb72["c2d0"].astype(np.int64))
+    np.testing.assert_allclose(y64, bb72["y_c2d0"], rtol=1e-4, atol=1e-4)
+
+
+def test_oracle_bipartite_conv_matches_reference_module(bb72):
+    x = torch.as_tensor(bf16_to_f32(bb72["x_bf16"]))
+    w = {k: torch.as_tensor(bf16_to_f32(bb72[k + "_bf16"])) for k in ("w_c2d_0", "w_c2d_1", "w_d2c_0", "w_d2c_1")}
+    y = orc.bipartite_conv(x, [w["w_c2d_0"], w["w_c2d_1"]], [w["w_d2c_0"], w["w_d2c_1"]],
+                           [bb72["c2d0"], bb72["c2d1"]], [bb72["d2c0"], bb72["d2c1"]])
+    np.testing.assert_allclose(y.numpy(), bb72["y_module"], rtol=1e-4, atol=1e-4)
+
+
+def test_oracle_gather_mm_matches_reference_surface(golden_dir):
+    z = np.load(os.path.join(golden_dir, "surface_gmm.npz"))
+    keys = sorted({k.rsplit("_", 1)[0] for k in z.files})
+    assert len(keys) == 10
+    for key in keys:
+        x = torch.as_tensor(bf16_to_f32(z[key + "_x"]))
+        w = torch.as_tensor(bf16_to_f32(z[key + "_w"]))
+        idx = z[key + "_idx"]
+        d, R, ci, co, B, ns = z[key + "_meta"]
+        g = RotatedSurface(int(d), int(R))
+        table = g.c2d[0] if key.endswith("c2d") else g.d2c_all
+        assert np.array_equal(table, idx), "fixture tables = this geometry's tables"
+        np.testing.assert_allclose(orc.gather_mm(x, w, idx).numpy(), z[key + "_y"], rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("name", ["d3_fp32", "d5_fp32", "d5_bf16_c64"])
+def test_oracle_predecoder_matches_reference_composition(golden_dir, name):
+    z = np.load(os.path.join(golden_dir, f"predecoder_{name}.npz"))
+    cfg = PreDecoderConfig(d=int(z["d"]), rounds=int(z["rounds"]), layers=int(z["layers"]),
+                           channels=int(z["channels"]), dtype=str(z["dtype"]))
+    g = RotatedSurface(cfg.d, cfg.rounds)
+    params = init_params(cfg, int(z["seed"]))
+    import hashlib
+    h = hashlib.sha256()
+    for k in sorted(params):
+        h.update(k.encode())
+        h.update(np.ascontiguousarray(params[k], np.float32).tobytes())
+    assert h.hexdigest() == str(z["params_sha256"]), "seeded weights changed"
+    p = storage_params(cfg, params)
+    logits, res = orc.predecoder(g, cfg, p, z["det"])
+    tol = 1e-4 if cfg.dtype == "f32" else 2e-2
+    assert orc.logit_error(logits, z["logits"]) < (1e-5 if cfg.dtype == "f32" else 1e-2)
+    assert orc.residual_mismatch_outside_band(res, z["residual"], z["logits"], g, tol) == 0
+    # the fixture's residual is exactly det ^ cancel(its own logits)
+    e = (z["logits"] > 0).astype(np.uint8)
+    assert np.array_equal(orc.cancel(z["det"], e, g), z["residual"])
+
+
+def test_band_helpers():
+    ref = np.array([[[1.0, -2.0], [1e-6, 0.5]]])
+    assert orc.band_mask(ref, 1e-3).sum() == 1
+    assert orc.logit_error(ref, ref) == 0.0
