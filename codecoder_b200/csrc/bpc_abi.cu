@@ -2,7 +2,7 @@
 #include <cstring>
 #include <string>
 
-#include "../../include/bpc.h"
+#include "bpc.h"
 #include "bpc_internal.h"
 
 namespace bpc {

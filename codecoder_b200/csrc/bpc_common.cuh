@@ -153,6 +153,22 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
          (static_cast<uint32_t>(M >> 4) << 24);
 }
 
-__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+// GELU in its tanh form (Hendrycks & Gimpel 2016): 0.5 x (1 + tanh(sqrt(2 / pi) (x + 0.044715 x^3))).
+// gelu_tanh: CUDA's tanhf (fp32 networks).  gelu_tanh_fast: the hardware tanh.approx.f32 (one MUFU op, relative
+// error about 2^-11), used where the result is rounded to bf16 (relative step 2^-8) right after.
+__device__ __forceinline__ float tanh_approx(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float u = 0.7978845608028654f * fmaf(0.044715f * x, x * x, x);
+  return 0.5f * x * (1.0f + tanhf(u));
+}
+__device__ __forceinline__ float gelu_tanh_fast(float x) {
+  const float u = 0.7978845608028654f * fmaf(0.044715f * x, x * x, x);
+  const float hx = 0.5f * x;
+  return fmaf(hx, tanh_approx(u), hx);
+}
 
 }  // namespace bpc

@@ -94,8 +94,8 @@ __global__ void __launch_bounds__(kFmaThreads) gmm_fma_kernel(const FmaArgs a) {
     for (int j = 0; j < 64; ++j) {
       if (j < cq) {
         float v = acc[j];
-        if (a.epi == kEpiGeluInit) v = gelu_erf(v);
-        else if (a.epi == kEpiGeluResid) v = ld_elem(yr + j) + gelu_erf(v);
+        if (a.epi == kEpiGeluInit) v = gelu_tanh(v);
+        else if (a.epi == kEpiGeluResid) v = ld_elem(yr + j) + gelu_tanh(v);
         const T sv = st_conv<T>(v);
         yr[j] = sv;
         if (a.head.head_w) {

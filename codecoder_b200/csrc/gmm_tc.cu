@@ -32,19 +32,23 @@ namespace bpc {
 
 namespace {
 
-constexpr int kThreads = 192;
-constexpr int kBlockM = 128;          // shots per tile
+constexpr int kThreads = 320;         // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
+constexpr int kEpiWarps = 8;
+constexpr int kBlockM = 128;          // rows of one MMA (shots)
 constexpr int kKBlock = 64;           // channels per 128-byte swizzled row
-constexpr int kABytes = kBlockM * kKBlock * 2;
+constexpr int kSubBytes = kBlockM * kKBlock * 2;   // one 128-row x 64-channel A block
 constexpr int kMaxStages = 8;
 constexpr int kSmemLimit = 232448;    // 227 KB opt-in per CTA
+
+// Shots per tile = 128 MT: MT = 2 lets two MMAs share every W stage (half the W traffic per FLOP) while the
+// accumulators (2 buffers x MT x Co fp32 columns) still fit the 512 TMEM columns.
+__host__ __device__ constexpr int mt_for(int Co) { return Co <= 128 ? 2 : 1; }
 
 struct TcArgs {
   const int32_t* idx;
   int NT, NS, K, Ci, Co;
   int type_split, n_kb, stages;
   int64_t shots;
-  int64_t shot_blocks;
   int64_t num_tiles;
   void* y;
   int64_t y_shot_stride, y_node_stride;
@@ -64,14 +68,23 @@ __device__ __forceinline__ uint32_t valid_mask(const int32_t* idx, int n, int K,
   return m;
 }
 
+__device__ __forceinline__ void ld_row_chunk(const __nv_bfloat16* p, uint4 (&r)[4]) {
+  const uint4* q = reinterpret_cast<const uint4*>(p);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) r[j] = q[j];
+}
+
+template <int MT, int NCH>
 __global__ void __launch_bounds__(kThreads, 1)
     gmm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW, const TcArgs a) {
+  constexpr int Co = NCH * 32;
+  constexpr int kTileM = kBlockM * MT;
+  constexpr uint32_t kABytes = kSubBytes * MT;
+  constexpr uint32_t kStageBytes = kABytes + Co * 128;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int S = a.stages;
-  const uint32_t b_bytes = static_cast<uint32_t>(a.Co) * 128u;
-  const uint32_t stage_bytes = kABytes + b_bytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * stage_bytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * kStageBytes);
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
   uint64_t* accf = bars + 2 * S;
@@ -90,7 +103,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(smem_u32(&accf[i]), 1);
-      mbar_init(smem_u32(&acce[i]), 4);
+      mbar_init(smem_u32(&acce[i]), kEpiWarps);
     }
     mbar_init(smem_u32(drain), 1);
     *abort_flag = 0;
@@ -116,8 +129,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int64_t tile = blockIdx.x; tile < a.num_tiles && ok; tile += gridDim.x) {
         const int n = static_cast<int>(tile % a.NT);
-        const int s0 = static_cast<int>((tile / a.NT) * kBlockM);
-        const int wrow = (n >= a.type_split) ? a.Co : 0;
+        const int s0 = static_cast<int>((tile / a.NT) * kTileM);
+        const int wrow = (n >= a.type_split) ? Co : 0;
         for (int r = 0; r < a.K && ok; ++r) {
           const int src = __ldg(a.idx + static_cast<int64_t>(n) * a.K + r);
           if (src < 0 || src >= a.NS) continue;
@@ -126,11 +139,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               ok = false;
               break;
             }
-            const uint32_t sa = smem_u32(smem + stage * stage_bytes);
+            const uint32_t sa = smem_u32(smem + stage * kStageBytes);
             const uint32_t fb = smem_u32(&full[stage]);
-            mbar_arrive_expect_tx(fb, stage_bytes);
-            tma_load_3d(sa, &tmA, kb * kKBlock, s0, src, fb);
-            tma_load_3d(sa + kABytes, &tmW, kb * kKBlock, r, wrow, fb);
+            mbar_arrive_expect_tx(fb, kStageBytes);
+            tma_load_3d(sa, &tmA, kb * kKBlock, s0, src, fb);          // kTileM shots x 64 channels
+            tma_load_3d(sa + kABytes, &tmW, kb * kKBlock, r, wrow, fb);  // Co rows x 64 channels of W_r
             armed |= 1u << stage;
             armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
             if (++stage == S) {
@@ -154,7 +167,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = idesc_bf16_f32(kBlockM, a.Co);
+      const uint32_t idesc = idesc_bf16_f32(kBlockM, Co);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -168,7 +181,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * a.Co);
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * MT * Co);
         uint32_t accumulate = 0;
         for (int r = 0; r < a.K && ok; ++r) {
           if (!(vm & (1u << r))) continue;
@@ -178,12 +191,13 @@ __global__ void __launch_bounds__(kThreads, 1)
               break;
             }
             tc_fence_after();
-            const uint32_t sa = smem_u32(smem + stage * stage_bytes);
+            const uint32_t sa = smem_u32(smem + stage * kStageBytes);
             const int ksteps = min(4, (a.Ci - kb * kKBlock + 15) / 16);
             for (int k = 0; k < ksteps; ++k) {
-              const uint64_t ad = sdesc_k_sw128(sa + k * 32);
               const uint64_t bd = sdesc_k_sw128(sa + kABytes + k * 32);
-              tc_mma_ss(d_tmem, ad, bd, idesc, accumulate);
+#pragma unroll
+              for (int m = 0; m < MT; ++m)
+                tc_mma_ss(d_tmem + m * Co, sdesc_k_sw128(sa + m * kSubBytes + k * 32), bd, idesc, accumulate);
               accumulate = 1;
             }
             tc_commit(smem_u32(&empty[stage]));   // frees the stage when these MMAs have read it
@@ -194,7 +208,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if (!ok) break;
-        tc_commit(smem_u32(&accf[acc]));          // accumulator ready for the epilogue
+        tc_commit(smem_u32(&accf[acc]));          // accumulators ready for the epilogue
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1u;
       }
@@ -205,70 +219,79 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ------------------------------------------------------------------ epilogue (warps 2..5)
+    // ------------------------------------------------------------------ epilogue (warps 2..9)
     const int q = warp & 3;                   // TMEM lane quarter this warp may access
-    const int row = q * 32 + lane;            // shot within the tile
+    const int m = (warp - 2) >> 2;            // which 128-shot sub-tile
+    const int row = q * 32 + lane;
+    const bool active = m < MT;
+    const bool resid = a.epi == kEpiGeluResid;
     int acc = 0;
     uint32_t acc_phase = 0;
-    const int Co = a.Co;
     for (int64_t tile = blockIdx.x; tile < a.num_tiles; tile += gridDim.x) {
       const int n = static_cast<int>(tile % a.NT);
-      const int64_t s0 = (tile / a.NT) * kBlockM;
-      const uint32_t vm = valid_mask(a.idx, n, a.K, a.NS);
-      if (!mbar_wait(smem_u32(&accf[acc]), acc_phase, abort_flag, a.status, a.timeout_ns)) break;
-      tc_fence_after();
+      const int64_t s0 = (tile / a.NT) * kTileM + m * kBlockM;
       const int64_t shot = s0 + row;
-      const bool ok = shot < a.shots;
+      const bool ok = active && shot < a.shots;
       __nv_bfloat16* yrow = reinterpret_cast<__nv_bfloat16*>(a.y) + shot * a.y_shot_stride +
                             static_cast<int64_t>(n) * a.y_node_stride;
+      // the residual rows do not depend on the MMAs: start loading them before waiting for the accumulator
+      uint4 r0[4], r1[4];
+      if (resid && ok) {
+        ld_row_chunk(yrow, r0);
+        if (NCH > 1) ld_row_chunk(yrow + 32, r1);
+      }
+      const uint32_t vm = active ? valid_mask(a.idx, n, a.K, a.NS) : 0u;
+      if (!mbar_wait(smem_u32(&accf[acc]), acc_phase, abort_flag, a.status, a.timeout_ns)) break;
+      tc_fence_after();
       float lg0 = 0.f, lg1 = 0.f;
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * Co);
-      for (int c0 = 0; c0 < Co; c0 += 32) {
-        float v[32];
-        tmem_ld32(taddr + c0, v);
-        if (vm == 0) {
+      if (active) {
+        const uint32_t taddr =
+            tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * MT * Co + m * Co);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = 0.f;
-        }
-        if (ok) {
-          uint4* yp = reinterpret_cast<uint4*>(yrow + c0);
-          float out[32];
-          if (a.epi == kEpiStore) {
+        for (int c = 0; c < NCH; ++c) {
+          float v[32];
+          tmem_ld32(taddr + c * 32, v);
+          if (vm == 0) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) out[i] = v[i];
-          } else if (a.epi == kEpiGeluInit) {
+            for (int i = 0; i < 32; ++i) v[i] = 0.f;
+          }
+          uint4 cur[4];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) out[i] = gelu_erf(v[i]);
-          } else {
+          for (int j = 0; j < 4; ++j) cur[j] = (c & 1) ? r1[j] : r0[j];
+          if (resid && ok && c + 2 < NCH) {
+            if (c & 1) ld_row_chunk(yrow + (c + 2) * 32, r1);
+            else ld_row_chunk(yrow + (c + 2) * 32, r0);
+          }
+          if (ok) {
+            uint4* yp = reinterpret_cast<uint4*>(yrow + c * 32);
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              const uint4 u = yp[j];
-              const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+              const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&cur[j]);
+              uint4 u;
+              __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(&u);
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
-                const float2 f = __bfloat1622float2(h[e]);
-                out[j * 8 + 2 * e] = f.x + gelu_erf(v[j * 8 + 2 * e]);
-                out[j * 8 + 2 * e + 1] = f.y + gelu_erf(v[j * 8 + 2 * e + 1]);
+                float x0 = v[j * 8 + 2 * e], x1 = v[j * 8 + 2 * e + 1];
+                if (a.epi != kEpiStore) {
+                  x0 = gelu_tanh_fast(x0);
+                  x1 = gelu_tanh_fast(x1);
+                }
+                if (resid) {
+                  const float2 f = __bfloat1622float2(h[e]);
+                  x0 += f.x;
+                  x1 += f.y;
+                }
+                o[e] = __floats2bfloat162_rn(x0, x1);
+                if (a.head.head_w) {
+                  const float2 f = __bfloat1622float2(o[e]);   // the stored (rounded) value feeds the head
+                  const int col = c * 32 + j * 8 + 2 * e;
+                  lg0 = fmaf(f.x, __ldg(a.head.head_w + col), lg0);
+                  lg0 = fmaf(f.y, __ldg(a.head.head_w + col + 1), lg0);
+                  lg1 = fmaf(f.x, __ldg(a.head.head_w + Co + col), lg1);
+                  lg1 = fmaf(f.y, __ldg(a.head.head_w + Co + col + 1), lg1);
+                }
               }
-            }
-          }
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            uint4 u;
-            __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(out[j * 8 + 2 * e], out[j * 8 + 2 * e + 1]);
-            yp[j] = u;
-            if (a.head.head_w) {
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const float2 f = __bfloat1622float2(h[e]);   // the stored (rounded) value feeds the head
-                const int c = c0 + j * 8 + 2 * e;
-                lg0 = fmaf(f.x, __ldg(a.head.head_w + c), lg0);
-                lg0 = fmaf(f.y, __ldg(a.head.head_w + c + 1), lg0);
-                lg1 = fmaf(f.x, __ldg(a.head.head_w + Co + c), lg1);
-                lg1 = fmaf(f.y, __ldg(a.head.head_w + Co + c + 1), lg1);
-              }
+              yp[j] = u;
             }
           }
         }
@@ -276,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&acce[acc]));
-      if (a.head.head_w) {
+      if (active && a.head.head_w) {
         lg0 += __ldg(a.head.head_b);
         lg1 += __ldg(a.head.head_b + 1);
         if (ok) {
@@ -290,8 +313,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane < 4) {
             const int j = lane >> 1;
             const int32_t c = __ldg(a.head.xor_nbr + static_cast<int64_t>(n) * 4 + lane);
-            const uint32_t m = j ? m1 : m0;
-            if (c >= 0 && m) atomicXor(a.head.res_bits + static_cast<int64_t>(c) * a.head.res_words + (s0 >> 5) + q, m);
+            const uint32_t msk = j ? m1 : m0;
+            if (c >= 0 && msk)
+              atomicXor(a.head.res_bits + static_cast<int64_t>(c) * a.head.res_words + (s0 >> 5) + q, msk);
           }
         }
       }
@@ -322,13 +346,34 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
 }
 
 int smem_bytes_for(int Co, int stages) {
-  return 1024 + stages * (kABytes + Co * 128) + (2 * stages + 5) * 8 + 8;
+  return 1024 + stages * (kSubBytes * mt_for(Co) + Co * 128) + (2 * stages + 5) * 8 + 8;
 }
 
 int stages_for(int Co) {
   int s = kMaxStages;
   while (s > 2 && smem_bytes_for(Co, s) > kSmemLimit) --s;
   return s;
+}
+
+using KernelFn = void (*)(CUtensorMap, CUtensorMap, TcArgs);
+
+template <int NCH>
+KernelFn kernel_for() {
+  return &gmm_tc_kernel<mt_for(NCH * 32), NCH>;
+}
+
+KernelFn select_kernel(int Co) {
+  switch (Co / 32) {
+    case 1: return kernel_for<1>();
+    case 2: return kernel_for<2>();
+    case 3: return kernel_for<3>();
+    case 4: return kernel_for<4>();
+    case 5: return kernel_for<5>();
+    case 6: return kernel_for<6>();
+    case 7: return kernel_for<7>();
+    case 8: return kernel_for<8>();
+    default: return nullptr;
+  }
 }
 
 }  // namespace
@@ -368,7 +413,7 @@ int gmm_tc_make_maps(const GmmProblem& p, GmmMaps* maps) {
     cuuint64_t dims[3] = {static_cast<cuuint64_t>(p.Ci), static_cast<cuuint64_t>(p.shots),
                           static_cast<cuuint64_t>(p.NS)};
     cuuint64_t strides[2] = {static_cast<cuuint64_t>(p.x_shot_stride) * 2, static_cast<cuuint64_t>(p.x_node_stride) * 2};
-    cuuint32_t box[3] = {kKBlock, kBlockM, 1};
+    cuuint32_t box[3] = {kKBlock, static_cast<cuuint32_t>(kBlockM * mt_for(p.Co)), 1};
     cuuint32_t es[3] = {1, 1, 1};
     CUresult r = enc(&maps->x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(p.x), dims, strides, box, es,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -403,8 +448,8 @@ int gmm_tc_launch(const GmmProblem& p, const GmmMaps& maps, int* status, uint64_
   a.n_kb = (p.Ci + kKBlock - 1) / kKBlock;
   a.stages = stages_for(p.Co);
   a.shots = p.shots;
-  a.shot_blocks = (p.shots + kBlockM - 1) / kBlockM;
-  a.num_tiles = a.shot_blocks * p.NT;
+  const int64_t tile_m = kBlockM * mt_for(p.Co);
+  a.num_tiles = ((p.shots + tile_m - 1) / tile_m) * p.NT;
   a.y = p.y;
   a.y_shot_stride = p.y_shot_stride;
   a.y_node_stride = p.y_node_stride;
@@ -413,17 +458,23 @@ int gmm_tc_launch(const GmmProblem& p, const GmmMaps& maps, int* status, uint64_
   a.status = status;
   a.timeout_ns = timeout_ns;
   uint32_t cols = 32;
-  while (cols < static_cast<uint32_t>(2 * p.Co)) cols <<= 1;
+  while (cols < static_cast<uint32_t>(2 * mt_for(p.Co) * p.Co)) cols <<= 1;
   a.tmem_cols = cols;
   const int smem = smem_bytes_for(p.Co, a.stages);
-  static int configured = 0;
-  if (configured < smem) {
-    cudaError_t e = cudaFuncSetAttribute(gmm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+  KernelFn fn = select_kernel(p.Co);
+  if (!fn) return fail(2, "unsupported C_out for the tcgen05 path");
+  static bool configured[9] = {false};
+  if (!configured[p.Co / 32]) {
+    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kSmemLimit);
     if (e != cudaSuccess) return fail(4, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
-    configured = kSmemLimit;
+    configured[p.Co / 32] = true;
   }
   const int64_t grid = std::min<int64_t>(a.num_tiles, num_sms());
-  gmm_tc_kernel<<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(maps.x, maps.w, a);
+  void* args[] = {const_cast<CUtensorMap*>(&maps.x), const_cast<CUtensorMap*>(&maps.w), &a};
+  cudaError_t le = cudaLaunchKernel(reinterpret_cast<const void*>(fn), dim3(static_cast<unsigned>(grid)),
+                                    dim3(kThreads), args, static_cast<size_t>(smem), stream);
+  if (le != cudaSuccess) return fail(4, std::string("gmm_tc_kernel launch: ") + cudaGetErrorString(le));
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(4, std::string("gmm_tc_kernel launch: ") + cudaGetErrorString(e));
   return 0;

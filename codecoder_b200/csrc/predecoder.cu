@@ -13,7 +13,7 @@
 #include <string>
 #include <vector>
 
-#include "../../include/bpc.h"
+#include "bpc.h"
 #include "bpc_common.cuh"
 #include "bpc_internal.h"
 

@@ -5,6 +5,7 @@ The network (a rotated-surface variant of the reference's bipartite convolution,
   embed    h_c = E[tok]  (4, C);  h_d = 0
   layer l  h_d <- h_d + GELU(gather_mm(h_c, Wc2d[l], c2d))                  check -> data, one data type
            h_c <- h_c + GELU(gather_mm(h_d, Wd2c[l, type], d2c[type]))      data -> check, per check type X / Z
+           GELU is the tanh form, 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))) (torch's approximate='tanh')
   head     logits[n] = Wh h_d[n] + bh   (N_d, 2): predicted X / Z flip of data node n
   cancel   e = logits > 0;  residual[c] = det[c] ^ XOR of e[q, 1 - type(c)] over the data qubits q around c at
            the same round (geometry.RotatedSurface.xor_nbr)

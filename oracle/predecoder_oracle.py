@@ -90,10 +90,10 @@ def predecoder(geo, cfg, params: dict, det: np.ndarray, dtype=torch.float64, ret
         wc = [_store(torch.as_tensor(w).to(dtype), bf16) for w in params["w_c2d"][layer]]
         wd = [_store(torch.as_tensor(w).to(dtype), bf16) for w in params["w_d2c"][layer]]
         acc = torch.cat([gather_mm(hc, w, t) for w, t in zip(wc, c2d)], 1)
-        upd = F.gelu(acc)
+        upd = F.gelu(acc, approximate="tanh")
         hd = _store(upd if hd is None else hd + upd, bf16)
         acc = torch.cat([gather_mm(hd, w, t) for w, t in zip(wd, d2c)], 1)
-        hc = _store(hc + F.gelu(acc), bf16)
+        hc = _store(hc + F.gelu(acc, approximate="tanh"), bf16)
     hw = torch.as_tensor(params["head_w"]).to(dtype)
     hb = torch.as_tensor(params["head_b"]).to(dtype)
     logits = hd @ hw.t() + hb

@@ -118,10 +118,11 @@ def reference_predecoder(geo, cfg, params, det):
     for layer in range(cfg.layers):
         acc = torch.cat([cn.gather_mm(hc, torch.as_tensor(w), torch.as_tensor(t), torch.as_tensor(geo.inverse(t, geo.N_c)))
                          for w, t in zip(p["w_c2d"][layer], geo.c2d)], 1)
-        hd = st(F.gelu(acc) if hd is None else hd + F.gelu(acc))
+        g_ = F.gelu(acc, approximate="tanh")
+        hd = st(g_ if hd is None else hd + g_)
         acc = torch.cat([cn.gather_mm(hd, torch.as_tensor(w), torch.as_tensor(t), torch.as_tensor(geo.inverse(t, geo.N_d)))
                          for w, t in zip(p["w_d2c"][layer], geo.d2c)], 1)
-        hc = st(hc + F.gelu(acc))
+        hc = st(hc + F.gelu(acc, approximate="tanh"))
     logits = hd @ torch.as_tensor(p["head_w"]).t() + torch.as_tensor(p["head_b"])
     e = (logits > 0).numpy().astype(np.uint8)
     res = det.astype(np.uint8).copy()
