@@ -57,7 +57,7 @@ extern "C" int bpc_gather_mm_fwd(const void* x, const void* w, const int32_t* id
   p.y_node_stride = Co;
   p.epi = kEpiStore;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (dtype == BPC_DTYPE_BF16 && Ci >= 64 && Ci % 8 == 0 && Co % 32 == 0 && Co <= 256) {
+  if (dtype == BPC_DTYPE_BF16 && Ci >= 64 && Ci % 8 == 0 && Co % 32 == 0 && Co <= 256 && K <= 16) {
     if (int e = gmm_tc_check(p)) return e;
     GmmMaps maps;
     if (int e = gmm_tc_make_maps(p, &maps)) return e;

@@ -42,6 +42,10 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
                "r"(bytes)
                : "memory");
 }
+// Add `bytes` to the transaction count of the current phase without arriving.
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -146,6 +150,30 @@ __device__ __forceinline__ uint64_t sdesc_k_sw128(uint32_t saddr) {
   d |= static_cast<uint64_t>(2) << 61;
   return d;
 }
+// Descriptor of a K-major operand in the canonical layout without swizzle: 8-row x 16-byte core matrices stored as
+// 128 contiguous bytes, core matrices adjacent in M `sbo` bytes apart and adjacent in K `lbo` bytes apart.
+__device__ __forceinline__ uint64_t sdesc_k_none(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  return d;
+}
+// 1D bulk copy global -> this CTA's shared memory (both 16-byte aligned, size a multiple of 16), counted on an
+// mbarrier in bytes.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
+// Ask L2 to fetch [src, src + bytes) (16-byte aligned, size a multiple of 16) without waiting for it.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
+               : "memory");
+}
+
 // Instruction descriptor for kind::f16: fp32 accumulator (bits 4-5 = 1), A and B bf16 (bits 7-9, 10-12 = 1),
 // both K-major (bits 15, 16 = 0), N >> 3 in bits 17-22, M >> 4 in bits 24-28.
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
@@ -161,6 +189,44 @@ __device__ __forceinline__ float tanh_approx(float x) {
   asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// Packed fp32 pairs (two lanes of one 64-bit register) for the sm_100 f32x2 FMA-pipe instructions.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  return static_cast<uint64_t>(__float_as_uint(lo)) | (static_cast<uint64_t>(__float_as_uint(hi)) << 32);
+}
+__device__ __forceinline__ float f2_lo(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v)); }
+__device__ __forceinline__ float f2_hi(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v >> 32)); }
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// bf16 pair (low half = first element) <-> packed fp32 pair
+__device__ __forceinline__ uint64_t bf2_to_f2(uint32_t h) { return f2_pack(__uint_as_float(h << 16), __uint_as_float(h & 0xFFFF0000u)); }
+__device__ __forceinline__ uint32_t f2_to_bf2(uint64_t v) {
+  const __nv_bfloat162 b = __floats2bfloat162_rn(f2_lo(v), f2_hi(v));
+  return *reinterpret_cast<const uint32_t*>(&b);
+}
+// GELU (tanh form) of a packed pair: u = x (c1 + c2 x^2), 0.5 x (1 + tanh(u)), tanh on the MUFU unit.
+__device__ __forceinline__ uint64_t gelu_tanh_fast2(uint64_t x) {
+  const uint64_t kC1 = f2_pack(0.7978845608028654f, 0.7978845608028654f);
+  const uint64_t kC2 = f2_pack(0.7978845608028654f * 0.044715f, 0.7978845608028654f * 0.044715f);
+  const uint64_t kHalf = f2_pack(0.5f, 0.5f);
+  const uint64_t u = f2_mul(f2_fma(f2_mul(x, x), kC2, kC1), x);
+  const uint64_t t = f2_pack(tanh_approx(f2_lo(u)), tanh_approx(f2_hi(u)));
+  const uint64_t hx = f2_mul(x, kHalf);
+  return f2_fma(hx, t, hx);
+}
+
 __device__ __forceinline__ float gelu_tanh(float x) {
   const float u = 0.7978845608028654f * fmaf(0.044715f * x, x * x, x);
   return 0.5f * x * (1.0f + tanhf(u));

@@ -27,10 +27,19 @@ struct HeadEpilogue {
 };
 
 // y[s, n, :] (op)= sum_r x[s, idx[n, r], :] W_{type(n), r}^T over relations r whose source is in [0, NS).
-// Strides are in elements.  W holds n_wtypes stacked (Co, K Ci) matrices; target n uses set (n >= type_split).
+// Two layouts for x and y (strides in elements, channels in groups of 8 = 16 bytes of bf16):
+//   rows     channel c of shot s at node n is at n node_stride + (c / 8) cg_stride + s shot_stride + c % 8
+//            (cg_stride = 8: a shot's channels contiguous; shot-major (B, N, C) or node-major (N, B, C))
+//   blocked  the tensor-core pre-decoder layout (node, shots / TM, C / 8, TM, 8), TM = gmm_tc_tile_shots(Co):
+//            element (s, n, c) at n node_stride + (s / TM) C TM + (c / 8) TM 8 + (s % TM) 8 + c % 8, so one tile
+//            (TM shots of one node) is one contiguous block of C TM elements; node_stride = C x shot capacity.
+// W holds n_wtypes stacked (Co, K Ci) matrices; target n uses set (n >= type_split).  `order`, if set, is the
+// processing order of the targets (a permutation of 0 .. NT - 1).
 struct GmmProblem {
   const void* x = nullptr;
-  int64_t x_shot_stride = 0, x_node_stride = 0;
+  int64_t x_shot_stride = 0, x_node_stride = 0, x_cg_stride = 8;
+  bool blocked = false;
+  const int32_t* order = nullptr;
   int64_t shots = 0;
   int NS = 0;
   const void* w = nullptr;
@@ -38,7 +47,7 @@ struct GmmProblem {
   const int32_t* idx = nullptr;
   int NT = 0, K = 0, Ci = 0, Co = 0;
   void* y = nullptr;
-  int64_t y_shot_stride = 0, y_node_stride = 0;
+  int64_t y_shot_stride = 0, y_node_stride = 0, y_cg_stride = 8;
   int epi = kEpiStore;
   HeadEpilogue head;
 };
@@ -57,6 +66,8 @@ int fail(int code, const std::string& msg);
 int gmm_tc_check(const GmmProblem& p);
 int gmm_tc_make_maps(const GmmProblem& p, GmmMaps* maps);
 int gmm_tc_launch(const GmmProblem& p, const GmmMaps& maps, int* status, uint64_t timeout_ns, cudaStream_t stream);
+// Shots per tensor-core tile (TM of the blocked layout) for C_out.
+int gmm_tc_tile_shots(int Co);
 
 // CUDA-core path: fp32 (f32 = true) or bf16 storage, fp32 accumulation.  Any Ci, Co % 4 == 0, Co <= 256.
 int gmm_fma_launch(const GmmProblem& p, bool f32, cudaStream_t stream);

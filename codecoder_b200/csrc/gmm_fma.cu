@@ -33,7 +33,7 @@ __device__ __forceinline__ __nv_bfloat16 st_conv<__nv_bfloat16>(float v) { retur
 
 struct FmaArgs {
   const void* x;
-  int64_t x_shot_stride, x_node_stride;
+  int64_t x_shot_stride, x_node_stride, x_cg_stride;
   int64_t shots;
   int NS;
   const void* w;
@@ -41,10 +41,13 @@ struct FmaArgs {
   const int32_t* idx;
   int NT, K, Ci, Co;
   void* y;
-  int64_t y_shot_stride, y_node_stride;
+  int64_t y_shot_stride, y_node_stride, y_cg_stride;
   int epi;
   HeadEpilogue head;
 };
+
+// offset of channel c within a (shot, node) row whose 8-channel groups are cg_stride elements apart
+__device__ __forceinline__ int64_t ch_off(int c, int64_t cg_stride) { return (c >> 3) * cg_stride + (c & 7); }
 
 template <typename T>
 __global__ void __launch_bounds__(kFmaThreads) gmm_fma_kernel(const FmaArgs a) {
@@ -78,7 +81,7 @@ __global__ void __launch_bounds__(kFmaThreads) gmm_fma_kernel(const FmaArgs a) {
       __syncthreads();
       if (ok) {
         for (int i = 0; i < ni; ++i) {
-          const float xv = ld_elem(xr + i0 + i);
+          const float xv = ld_elem(xr + ch_off(i0 + i, a.x_cg_stride));
           const float* wrow = ws + i * a.Co + o0;
 #pragma unroll
           for (int j = 0; j < 64; ++j)
@@ -89,15 +92,16 @@ __global__ void __launch_bounds__(kFmaThreads) gmm_fma_kernel(const FmaArgs a) {
   }
   float lg0 = 0.f, lg1 = 0.f;
   if (ok) {
-    T* yr = reinterpret_cast<T*>(a.y) + shot * a.y_shot_stride + static_cast<int64_t>(n) * a.y_node_stride + o0;
+    T* yr = reinterpret_cast<T*>(a.y) + shot * a.y_shot_stride + static_cast<int64_t>(n) * a.y_node_stride;
 #pragma unroll
     for (int j = 0; j < 64; ++j) {
       if (j < cq) {
         float v = acc[j];
+        T* yp = yr + ch_off(o0 + j, a.y_cg_stride);
         if (a.epi == kEpiGeluInit) v = gelu_tanh(v);
-        else if (a.epi == kEpiGeluResid) v = ld_elem(yr + j) + gelu_tanh(v);
+        else if (a.epi == kEpiGeluResid) v = ld_elem(yp) + gelu_tanh(v);
         const T sv = st_conv<T>(v);
-        yr[j] = sv;
+        *yp = sv;
         if (a.head.head_w) {
           const float f = ld_elem(&sv);
           lg0 = fmaf(f, __ldg(a.head.head_w + o0 + j), lg0);
@@ -150,6 +154,7 @@ int gmm_fma_launch(const GmmProblem& p, bool f32, cudaStream_t stream) {
   a.x = p.x;
   a.x_shot_stride = p.x_shot_stride;
   a.x_node_stride = p.x_node_stride;
+  a.x_cg_stride = p.x_cg_stride;
   a.shots = p.shots;
   a.NS = p.NS;
   a.w = p.w;
@@ -162,6 +167,7 @@ int gmm_fma_launch(const GmmProblem& p, bool f32, cudaStream_t stream) {
   a.y = p.y;
   a.y_shot_stride = p.y_shot_stride;
   a.y_node_stride = p.y_node_stride;
+  a.y_cg_stride = p.y_cg_stride;
   a.epi = p.epi;
   a.head = p.head;
   const int64_t tiles = static_cast<int64_t>(p.NT) * ((p.shots + kFmaShots - 1) / kFmaShots);

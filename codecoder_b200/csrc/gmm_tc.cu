@@ -2,26 +2,34 @@
 //
 //   y[s, n, :] (op)= sum_r x[s, idx[n, r], :] W_{type(n), r}^T            (cascade_triton.py:5,40 -- same arithmetic)
 //
-// Tile = one target node n x 128 shots.  The 128 rows of the MMA are shots, so for a given relation r every row of
-// the tile reads the same source node idx[n, r]: the neighbour "gather" is one strided TMA box per (tile, relation,
-// 64-channel block) -- x viewed as the 3D tensor (channel, shot, node) -- and a pad slot (idx outside [0, NS)) is a
-// relation the tile skips entirely (no load, no MMA).  The same kernel serves shot-major x (B, NS, C), the layout of
-// the reference's op, and the node-major (NS, B, C) layout the pre-decoder keeps its activations in; only the
-// tensor-map strides differ.
+// Tile = one target node n x 128 MT shots.  The rows of the MMA are shots, so for a given relation r every row of
+// the tile reads the same source node idx[n, r]: the neighbour "gather" is one block copy per (tile, relation,
+// 64-channel block), and a pad slot (idx outside [0, NS)) is a relation the tile skips entirely (no load, no MMA).
+// Two activation layouts:
+//   rows     x of any row layout -- shot-major (B, NS, C), the reference op's, or node-major -- viewed as the 3D
+//            tensor (channel, shot, node); one TMA box per stage into the 128-byte-swizzled K-major layout.
+//   blocked  the pre-decoder's (node, shots / TM, C / 8, TM, 8) layout, TM = 128 MT: a tile's activations are one
+//            contiguous block, so a stage is one 1D bulk copy (8 channel groups x TM shots x 16 bytes) straight into
+//            the canonical no-swizzle K-major layout (8-row x 16-byte core matrices), the producer can ask L2 for
+//            the next tile's source and residual blocks one instruction each, and the epilogue's loads and stores
+//            cover 512 contiguous bytes per warp instruction.
+// W_r (Co x 64 channels per stage) always comes by TMA in the 128-byte-swizzled K-major layout.
 //
-// Roles (192 threads, one CTA per SM):
-//   warp 0     TMA producer: A box (128 shots x 64 channels, 16 KB) + W box (Co rows x 64 channels) per stage
-//   warp 1     TMEM owner and MMA issuer: tcgen05.mma M=128 N=Co K=16 from two 128B-swizzled K-major operands,
-//              fp32 accumulator in TMEM, double-buffered (2 x Co columns) so the epilogue of tile i overlaps the
-//              MMAs of tile i + 1
-//   warps 2-5  epilogue: tcgen05.ld of the accumulator (one shot per thread), GELU / residual add, bf16 store,
-//              and for the pre-decoder's last check -> data step the X / Z head, the threshold and the XOR of the
-//              predicted flips into the bit-packed residual syndrome (one ballot + atomicXor per warp and check)
+// Roles (320 threads, one CTA per SM):
+//   warp 0     producer: A block(s) + W box per stage, completion counted in bytes on the stage's mbarrier
+//   warp 1     TMEM owner and MMA issuer: per 16-channel step MT tcgen05.mma M=128 N=Co K=16 sharing the W stage,
+//              fp32 accumulators in TMEM, double-buffered (2 x MT x Co columns) so the epilogue of tile i overlaps
+//              the MMAs of tile i + 1
+//   warps 2-9  epilogue, one shot (TMEM lane) per thread: tcgen05.ld of 32 columns at a time, GELU / residual add
+//              (the residual rows are loaded before the accumulator is waited for), bf16 store, and for the
+//              pre-decoder's last check -> data step the X / Z head, the threshold and the XOR of the predicted flips
+//              into the bit-packed residual syndrome (one ballot + atomicXor per warp and check)
 // Every wait is bounded (mbar_wait); a timeout sets the status word and the CTA drains and returns.
+#include <algorithm>
 #include <cstdio>
 #include <mutex>
 #include <string>
-#include <unordered_map>
+#include <unordered_set>
 
 #include <cudaTypedefs.h>
 
@@ -32,10 +40,10 @@ namespace bpc {
 
 namespace {
 
-constexpr int kThreads = 320;         // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
+constexpr int kThreads = 320;         // warp 0 producer, warp 1 MMA, warps 2-9 epilogue
 constexpr int kEpiWarps = 8;
 constexpr int kBlockM = 128;          // rows of one MMA (shots)
-constexpr int kKBlock = 64;           // channels per 128-byte swizzled row
+constexpr int kKBlock = 64;           // channels per stage
 constexpr int kSubBytes = kBlockM * kKBlock * 2;   // one 128-row x 64-channel A block
 constexpr int kMaxStages = 8;
 constexpr int kSmemLimit = 232448;    // 227 KB opt-in per CTA
@@ -50,8 +58,11 @@ struct TcArgs {
   int type_split, n_kb, stages;
   int64_t shots;
   int64_t num_tiles;
+  const int32_t* order;                   // target processing order (null: node order)
+  const __nv_bfloat16* x;                 // blocked loader only
+  int64_t x_node_stride;                  // blocked loader only (elements)
   void* y;
-  int64_t y_shot_stride, y_node_stride;
+  int64_t y_shot_stride, y_node_stride, y_cg_stride;
   int epi;
   HeadEpilogue head;
   int* status;
@@ -59,32 +70,53 @@ struct TcArgs {
   uint32_t tmem_cols;
 };
 
-__device__ __forceinline__ uint32_t valid_mask(const int32_t* idx, int n, int K, int NS) {
-  uint32_t m = 0;
-  for (int r = 0; r < K; ++r) {
-    const int s = __ldg(idx + static_cast<int64_t>(n) * K + r);
-    if (s >= 0 && s < NS) m |= 1u << r;
-  }
-  return m;
+__device__ __forceinline__ int target_of(const TcArgs& a, int64_t tile) {
+  const int i = static_cast<int>(tile % a.NT);
+  return a.order ? __ldg(a.order + i) : i;
 }
 
-__device__ __forceinline__ void ld_row_chunk(const __nv_bfloat16* p, uint4 (&r)[4]) {
-  const uint4* q = reinterpret_cast<const uint4*>(p);
+constexpr int kMaxK = 16;   // relations per target on the tensor-core path
+
+// A tile's target node and index row.  The K index loads are independent (unrolled, predicated), and every role
+// loads the next tile's row while it works on the current one, so no role waits on a chain of table loads.
+struct TileRow {
+  int n;
+  uint32_t vm;              // relations whose source is in [0, NS)
+  int src[kMaxK];
+};
+
+__device__ __forceinline__ TileRow load_row(const TcArgs& a, int64_t tile) {
+  TileRow t;
+  t.n = target_of(a, tile);
+  const int32_t* row = a.idx + static_cast<int64_t>(t.n) * a.K;
 #pragma unroll
-  for (int j = 0; j < 4; ++j) r[j] = q[j];
+  for (int r = 0; r < kMaxK; ++r) t.src[r] = r < a.K ? __ldg(row + r) : -1;
+  t.vm = 0;
+#pragma unroll
+  for (int r = 0; r < kMaxK; ++r)
+    if (t.src[r] >= 0 && t.src[r] < a.NS) t.vm |= 1u << r;
+  return t;
 }
 
-template <int MT, int NCH>
+// the 4 channel groups (32 channels) of chunk c of one shot's row
+__device__ __forceinline__ void ld_chunk(const __nv_bfloat16* base, int64_t cg_stride, int c, uint4 (&r)[4]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) r[j] = *reinterpret_cast<const uint4*>(base + (4 * c + j) * cg_stride);
+}
+
+template <int MT, int NCH, bool BLOCKED, int EPI, bool HEAD>
 __global__ void __launch_bounds__(kThreads, 1)
     gmm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW, const TcArgs a) {
   constexpr int Co = NCH * 32;
   constexpr int kTileM = kBlockM * MT;
   constexpr uint32_t kABytes = kSubBytes * MT;
-  constexpr uint32_t kStageBytes = kABytes + Co * 128;
+  constexpr uint32_t kItemBytes = kABytes + Co * 128;  // one (relation, 64-channel block) item: A block + W block
+  constexpr uint32_t kCgBytes = kTileM * 16;        // blocked layout: one channel group of the tile's shots
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int S = a.stages;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * kStageBytes);
+  constexpr uint32_t stage_bytes = kItemBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * stage_bytes);
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
   uint64_t* accf = bars + 2 * S;
@@ -108,7 +140,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(smem_u32(drain), 1);
     *abort_flag = 0;
     fence_mbar_init();
-    tma_prefetch_desc(&tmA);
+    if (!BLOCKED) tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmW);
   }
   if (warp == 1) {
@@ -121,29 +153,54 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer
+    // ------------------------------------------------------------------ producer
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
       uint32_t armed = 0, armed_parity = 0;   // stages with a load in flight and the parity it completes
       bool ok = true;
+      TileRow cur = load_row(a, blockIdx.x < a.num_tiles ? blockIdx.x : 0);
       for (int64_t tile = blockIdx.x; tile < a.num_tiles && ok; tile += gridDim.x) {
-        const int n = static_cast<int>(tile % a.NT);
-        const int s0 = static_cast<int>((tile / a.NT) * kTileM);
+        const int n = cur.n;
+        const int64_t s0 = (tile / a.NT) * kTileM;
         const int wrow = (n >= a.type_split) ? Co : 0;
+        const int64_t nt = tile + gridDim.x;
+        const TileRow nxt = load_row(a, nt < a.num_tiles ? nt : tile);
+        if (BLOCKED && nt < a.num_tiles) {
+          // ask L2 for the next tile's source blocks (and residual block) while this tile is loaded and computed
+          const int64_t ns0 = (nt / a.NT) * kTileM;
+#pragma unroll
+          for (int r = 0; r < kMaxK; ++r)
+            if (nxt.vm & (1u << r))
+              bulk_prefetch_l2(a.x + static_cast<int64_t>(nxt.src[r]) * a.x_node_stride + ns0 * a.Ci,
+                               a.Ci * kTileM * 2);
+          if (EPI == kEpiGeluResid)
+            bulk_prefetch_l2(reinterpret_cast<const __nv_bfloat16*>(a.y) + static_cast<int64_t>(nxt.n) * a.y_node_stride +
+                                 ns0 * Co,
+                             Co * kTileM * 2);
+        }
+#pragma unroll 1
         for (int r = 0; r < a.K && ok; ++r) {
-          const int src = __ldg(a.idx + static_cast<int64_t>(n) * a.K + r);
-          if (src < 0 || src >= a.NS) continue;
+          if (!(cur.vm & (1u << r))) continue;
+          const int src = cur.src[r];
+#pragma unroll 1
           for (int kb = 0; kb < a.n_kb; ++kb) {
             if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, a.status, a.timeout_ns)) {
               ok = false;
               break;
             }
-            const uint32_t sa = smem_u32(smem + stage * kStageBytes);
+            const uint32_t sa = smem_u32(smem + stage * stage_bytes);
             const uint32_t fb = smem_u32(&full[stage]);
-            mbar_arrive_expect_tx(fb, kStageBytes);
-            tma_load_3d(sa, &tmA, kb * kKBlock, s0, src, fb);          // kTileM shots x 64 channels
-            tma_load_3d(sa + kABytes, &tmW, kb * kKBlock, r, wrow, fb);  // Co rows x 64 channels of W_r
+            if (BLOCKED) {
+              const int ncg = min(8, (a.Ci - kb * kKBlock) / 8);
+              mbar_arrive_expect_tx(fb, ncg * kCgBytes + Co * 128);
+              bulk_load(sa, a.x + static_cast<int64_t>(src) * a.x_node_stride + s0 * a.Ci + kb * 8 * (kTileM * 8),
+                        ncg * kCgBytes, fb);
+            } else {
+              mbar_arrive_expect_tx(fb, kItemBytes);
+              tma_load_3d(sa, &tmA, kb * kKBlock, static_cast<int32_t>(s0), src, fb);   // kTileM shots x 64 ch
+            }
+            tma_load_3d(sa + kABytes, &tmW, kb * kKBlock, r, wrow, fb);               // Co rows x 64 ch of W_r
             armed |= 1u << stage;
             armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
             if (++stage == S) {
@@ -152,6 +209,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
+        cur = nxt;
       }
       if (!ok) {
         // drain: wait (bounded) for every load this thread issued before leaving the CTA's shared memory
@@ -173,9 +231,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
+      TileRow cur = load_row(a, blockIdx.x < a.num_tiles ? blockIdx.x : 0);
       for (int64_t tile = blockIdx.x; tile < a.num_tiles && ok; tile += gridDim.x) {
-        const int n = static_cast<int>(tile % a.NT);
-        const uint32_t vm = valid_mask(a.idx, n, a.K, a.NS);
+        const uint32_t vm = cur.vm;
+        const int64_t nt = tile + gridDim.x;
+        cur = load_row(a, nt < a.num_tiles ? nt : tile);     // next tile's row, loaded while this one is issued
         if (!mbar_wait(smem_u32(&acce[acc]), acc_phase ^ 1u, abort_flag, a.status, a.timeout_ns)) {
           ok = false;
           break;
@@ -183,22 +243,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * MT * Co);
         uint32_t accumulate = 0;
+#pragma unroll 1
         for (int r = 0; r < a.K && ok; ++r) {
           if (!(vm & (1u << r))) continue;
+#pragma unroll 1
           for (int kb = 0; kb < a.n_kb; ++kb) {
             if (!mbar_wait(smem_u32(&full[stage]), phase, abort_flag, a.status, a.timeout_ns)) {
               ok = false;
               break;
             }
-            tc_fence_after();
-            const uint32_t sa = smem_u32(smem + stage * kStageBytes);
-            const int ksteps = min(4, (a.Ci - kb * kKBlock + 15) / 16);
-            for (int k = 0; k < ksteps; ++k) {
-              const uint64_t bd = sdesc_k_sw128(sa + kABytes + k * 32);
+            // descriptors built once per stage, advanced by constants (the address field counts 16-byte units)
+            const uint32_t sa = smem_u32(smem + stage * stage_bytes);
+            const uint64_t ad0 = BLOCKED ? sdesc_k_none(sa, kCgBytes, 128) : sdesc_k_sw128(sa);
+            const uint64_t bd0 = sdesc_k_sw128(sa + kABytes);
+            const bool full_kb = (kb + 1) * kKBlock <= a.Ci;
+            const int ksteps = full_kb ? 4 : (a.Ci - kb * kKBlock + 15) / 16;
 #pragma unroll
-              for (int m = 0; m < MT; ++m)
-                tc_mma_ss(d_tmem + m * Co, sdesc_k_sw128(sa + m * kSubBytes + k * 32), bd, idesc, accumulate);
-              accumulate = 1;
+            for (int k = 0; k < 4; ++k) {
+              if (k < ksteps) {
+                const uint64_t bd = bd0 + static_cast<uint64_t>((k * 32) >> 4);
+#pragma unroll
+                for (int m = 0; m < MT; ++m) {
+                  const uint32_t aoff = BLOCKED ? (2 * k * kCgBytes + m * kBlockM * 16) : (m * kSubBytes + k * 32);
+                  tc_mma_ss(d_tmem + m * Co, ad0 + static_cast<uint64_t>(aoff >> 4), bd, idesc, accumulate);
+                }
+                accumulate = 1;
+              }
             }
             tc_commit(smem_u32(&empty[stage]));   // frees the stage when these MMAs have read it
             if (++stage == S) {
@@ -220,78 +290,77 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------------ epilogue (warps 2..9)
+    // One shot (TMEM lane) per thread.  Element math runs on packed fp32 pairs (f32x2); the residual row is loaded
+    // before the accumulator wait (whole row up to 128 channels, then two 32-channel chunks ahead).
+    constexpr bool kResid = EPI == kEpiGeluResid;
+    constexpr int kPre = NCH <= 4 ? NCH : 2;          // chunks loaded before the accumulator wait
     const int q = warp & 3;                   // TMEM lane quarter this warp may access
     const int m = (warp - 2) >> 2;            // which 128-shot sub-tile
     const int row = q * 32 + lane;
     const bool active = m < MT;
-    const bool resid = a.epi == kEpiGeluResid;
+    const int64_t cgs = BLOCKED ? kTileM * 8 : a.y_cg_stride;
     int acc = 0;
     uint32_t acc_phase = 0;
+    TileRow cur = load_row(a, blockIdx.x < a.num_tiles ? blockIdx.x : 0);
     for (int64_t tile = blockIdx.x; tile < a.num_tiles; tile += gridDim.x) {
-      const int n = static_cast<int>(tile % a.NT);
+      const int n = cur.n;
+      const uint32_t vm = active ? cur.vm : 0u;
+      {
+        const int64_t nt = tile + gridDim.x;
+        cur = load_row(a, nt < a.num_tiles ? nt : tile);
+      }
       const int64_t s0 = (tile / a.NT) * kTileM + m * kBlockM;
       const int64_t shot = s0 + row;
       const bool ok = active && shot < a.shots;
-      __nv_bfloat16* yrow = reinterpret_cast<__nv_bfloat16*>(a.y) + shot * a.y_shot_stride +
-                            static_cast<int64_t>(n) * a.y_node_stride;
-      // the residual rows do not depend on the MMAs: start loading them before waiting for the accumulator
-      uint4 r0[4], r1[4];
-      if (resid && ok) {
-        ld_row_chunk(yrow, r0);
-        if (NCH > 1) ld_row_chunk(yrow + 32, r1);
+      __nv_bfloat16* yrow = reinterpret_cast<__nv_bfloat16*>(a.y) + static_cast<int64_t>(n) * a.y_node_stride +
+                            (BLOCKED ? (s0 - m * kBlockM) * Co + (m * kBlockM + row) * 8 : shot * a.y_shot_stride);
+      // the residual rows do not depend on the MMAs: load them before waiting for the accumulator
+      uint4 rbuf[kResid ? kPre : 1][4];
+      if (kResid && ok) {
+#pragma unroll
+        for (int c = 0; c < kPre; ++c) ld_chunk(yrow, cgs, c, rbuf[c]);
       }
-      const uint32_t vm = active ? valid_mask(a.idx, n, a.K, a.NS) : 0u;
       if (!mbar_wait(smem_u32(&accf[acc]), acc_phase, abort_flag, a.status, a.timeout_ns)) break;
       tc_fence_after();
-      float lg0 = 0.f, lg1 = 0.f;
+      uint64_t lg0 = 0, lg1 = 0;              // packed partial head sums (two columns each)
       if (active) {
         const uint32_t taddr =
             tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * MT * Co + m * Co);
 #pragma unroll
         for (int c = 0; c < NCH; ++c) {
           float v[32];
-          tmem_ld32(taddr + c * 32, v);
-          if (vm == 0) {
+          if (vm) {
+            tmem_ld32(taddr + c * 32, v);
+          } else {
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] = 0.f;
           }
           uint4 cur[4];
+          if (kResid) {
 #pragma unroll
-          for (int j = 0; j < 4; ++j) cur[j] = (c & 1) ? r1[j] : r0[j];
-          if (resid && ok && c + 2 < NCH) {
-            if (c & 1) ld_row_chunk(yrow + (c + 2) * 32, r1);
-            else ld_row_chunk(yrow + (c + 2) * 32, r0);
+            for (int j = 0; j < 4; ++j) cur[j] = rbuf[c % kPre][j];
+            if (ok && c + kPre < NCH) ld_chunk(yrow, cgs, c + kPre, rbuf[c % kPre]);
           }
           if (ok) {
-            uint4* yp = reinterpret_cast<uint4*>(yrow + c * 32);
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&cur[j]);
               uint4 u;
-              __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(&u);
+              uint32_t* o = reinterpret_cast<uint32_t*>(&u);
+              const uint32_t* h = reinterpret_cast<const uint32_t*>(&cur[j]);
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
-                float x0 = v[j * 8 + 2 * e], x1 = v[j * 8 + 2 * e + 1];
-                if (a.epi != kEpiStore) {
-                  x0 = gelu_tanh_fast(x0);
-                  x1 = gelu_tanh_fast(x1);
-                }
-                if (resid) {
-                  const float2 f = __bfloat1622float2(h[e]);
-                  x0 += f.x;
-                  x1 += f.y;
-                }
-                o[e] = __floats2bfloat162_rn(x0, x1);
-                if (a.head.head_w) {
-                  const float2 f = __bfloat1622float2(o[e]);   // the stored (rounded) value feeds the head
+                uint64_t x = f2_pack(v[j * 8 + 2 * e], v[j * 8 + 2 * e + 1]);
+                if (EPI != kEpiStore) x = gelu_tanh_fast2(x);
+                if (kResid) x = f2_add(x, bf2_to_f2(h[e]));
+                o[e] = f2_to_bf2(x);
+                if (HEAD) {
+                  const uint64_t f = bf2_to_f2(o[e]);   // the stored (rounded) value feeds the head
                   const int col = c * 32 + j * 8 + 2 * e;
-                  lg0 = fmaf(f.x, __ldg(a.head.head_w + col), lg0);
-                  lg0 = fmaf(f.y, __ldg(a.head.head_w + col + 1), lg0);
-                  lg1 = fmaf(f.x, __ldg(a.head.head_w + Co + col), lg1);
-                  lg1 = fmaf(f.y, __ldg(a.head.head_w + Co + col + 1), lg1);
+                  lg0 = f2_fma(f, *reinterpret_cast<const uint64_t*>(a.head.head_w + col), lg0);
+                  lg1 = f2_fma(f, *reinterpret_cast<const uint64_t*>(a.head.head_w + Co + col), lg1);
                 }
               }
-              yp[j] = u;
+              *reinterpret_cast<uint4*>(yrow + (4 * c + j) * cgs) = u;
             }
           }
         }
@@ -299,17 +368,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&acce[acc]));
-      if (active && a.head.head_w) {
-        lg0 += __ldg(a.head.head_b);
-        lg1 += __ldg(a.head.head_b + 1);
+      if (HEAD && active) {
+        const float l0 = f2_lo(lg0) + f2_hi(lg0) + __ldg(a.head.head_b);
+        const float l1 = f2_lo(lg1) + f2_hi(lg1) + __ldg(a.head.head_b + 1);
         if (ok) {
           float2* lp = reinterpret_cast<float2*>(a.head.logits + shot * a.head.lg_shot_stride +
                                                  static_cast<int64_t>(n) * a.head.lg_node_stride);
-          *lp = make_float2(lg0, lg1);
+          *lp = make_float2(l0, l1);
         }
         if (a.head.res_bits) {
-          const uint32_t m0 = __ballot_sync(0xffffffffu, ok && lg0 > 0.f);
-          const uint32_t m1 = __ballot_sync(0xffffffffu, ok && lg1 > 0.f);
+          const uint32_t m0 = __ballot_sync(0xffffffffu, ok && l0 > 0.f);
+          const uint32_t m1 = __ballot_sync(0xffffffffu, ok && l1 > 0.f);
           if (lane < 4) {
             const int j = lane >> 1;
             const int32_t c = __ldg(a.head.xor_nbr + static_cast<int64_t>(n) * 4 + lane);
@@ -345,9 +414,9 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
   return fn;
 }
 
-int smem_bytes_for(int Co, int stages) {
-  return 1024 + stages * (kSubBytes * mt_for(Co) + Co * 128) + (2 * stages + 5) * 8 + 8;
-}
+int item_bytes_for(int Co) { return kSubBytes * mt_for(Co) + Co * 128; }
+
+int smem_bytes_for(int Co, int stages) { return 1024 + stages * item_bytes_for(Co) + (2 * stages + 5) * 8 + 8; }
 
 int stages_for(int Co) {
   int s = kMaxStages;
@@ -357,21 +426,30 @@ int stages_for(int Co) {
 
 using KernelFn = void (*)(CUtensorMap, CUtensorMap, TcArgs);
 
+// rows layout: the plain op (store); blocked layout: the pre-decoder's steps (GELU first / GELU + residual, with or
+// without the head)
 template <int NCH>
-KernelFn kernel_for() {
-  return &gmm_tc_kernel<mt_for(NCH * 32), NCH>;
+KernelFn kernel_for(bool blocked, int epi, bool head) {
+  constexpr int MT = mt_for(NCH * 32);
+  if (!blocked) return (epi == kEpiStore && !head) ? &gmm_tc_kernel<MT, NCH, false, kEpiStore, false> : nullptr;
+  if (epi == kEpiGeluInit)
+    return head ? &gmm_tc_kernel<MT, NCH, true, kEpiGeluInit, true> : &gmm_tc_kernel<MT, NCH, true, kEpiGeluInit, false>;
+  if (epi == kEpiGeluResid)
+    return head ? &gmm_tc_kernel<MT, NCH, true, kEpiGeluResid, true>
+                : &gmm_tc_kernel<MT, NCH, true, kEpiGeluResid, false>;
+  return nullptr;
 }
 
-KernelFn select_kernel(int Co) {
+KernelFn select_kernel(int Co, bool blocked, int epi, bool head) {
   switch (Co / 32) {
-    case 1: return kernel_for<1>();
-    case 2: return kernel_for<2>();
-    case 3: return kernel_for<3>();
-    case 4: return kernel_for<4>();
-    case 5: return kernel_for<5>();
-    case 6: return kernel_for<6>();
-    case 7: return kernel_for<7>();
-    case 8: return kernel_for<8>();
+    case 1: return kernel_for<1>(blocked, epi, head);
+    case 2: return kernel_for<2>(blocked, epi, head);
+    case 3: return kernel_for<3>(blocked, epi, head);
+    case 4: return kernel_for<4>(blocked, epi, head);
+    case 5: return kernel_for<5>(blocked, epi, head);
+    case 6: return kernel_for<6>(blocked, epi, head);
+    case 7: return kernel_for<7>(blocked, epi, head);
+    case 8: return kernel_for<8>(blocked, epi, head);
     default: return nullptr;
   }
 }
@@ -392,14 +470,21 @@ int num_sms() {
 int gmm_tc_check(const GmmProblem& p) {
   if (p.Ci < 64 || p.Ci % 8 != 0) return fail(2, "tcgen05 path needs C_in >= 64 and a multiple of 8");
   if (p.Co < 32 || p.Co > 256 || p.Co % 32 != 0) return fail(2, "tcgen05 path needs C_out in 32..256, multiple of 32");
-  if (p.K < 1 || p.K > 32) return fail(2, "relation count K must be in 1..32");
+  if (p.K < 1 || p.K > kMaxK) return fail(2, "tcgen05 path supports 1..16 relations per target");
   if (p.NT < 1 || p.NS < 1) return fail(2, "empty node set");
   if (p.n_wtypes < 1 || p.n_wtypes > 2) return fail(2, "one or two weight sets");
   const uintptr_t xa = reinterpret_cast<uintptr_t>(p.x), wa = reinterpret_cast<uintptr_t>(p.w),
                   ya = reinterpret_cast<uintptr_t>(p.y);
   if ((xa | wa | ya) & 15) return fail(2, "x, w and y must be 16-byte aligned");
-  if ((p.x_shot_stride | p.x_node_stride | p.y_shot_stride | p.y_node_stride) & 7)
+  if ((p.x_shot_stride | p.x_node_stride | p.x_cg_stride | p.y_shot_stride | p.y_node_stride | p.y_cg_stride) & 7)
     return fail(2, "strides must be multiples of 8 elements");
+  if (p.blocked) {
+    const int64_t tile_m = kBlockM * mt_for(p.Co);
+    if (p.Ci != p.Co || p.x_node_stride % (static_cast<int64_t>(p.Ci) * tile_m) != 0 ||
+        p.y_node_stride % (static_cast<int64_t>(p.Co) * tile_m) != 0 || p.x_node_stride / p.Ci < p.shots ||
+        p.y_node_stride / p.Co < p.shots)
+      return fail(2, "blocked layout needs C_in == C_out and a shot capacity that is a multiple of the tile");
+  }
   if (p.head.head_w && (!p.head.logits || (reinterpret_cast<uintptr_t>(p.head.logits) & 7) ||
                         ((p.head.lg_shot_stride | p.head.lg_node_stride) & 1)))
     return fail(2, "head logits must be 8-byte aligned with even strides");
@@ -409,7 +494,7 @@ int gmm_tc_check(const GmmProblem& p) {
 int gmm_tc_make_maps(const GmmProblem& p, GmmMaps* maps) {
   auto enc = get_encode();
   if (!enc) return fail(3, "cuTensorMapEncodeTiled is not available from the CUDA driver");
-  {
+  if (!p.blocked) {
     cuuint64_t dims[3] = {static_cast<cuuint64_t>(p.Ci), static_cast<cuuint64_t>(p.shots),
                           static_cast<cuuint64_t>(p.NS)};
     cuuint64_t strides[2] = {static_cast<cuuint64_t>(p.x_shot_stride) * 2, static_cast<cuuint64_t>(p.x_node_stride) * 2};
@@ -419,6 +504,8 @@ int gmm_tc_make_maps(const GmmProblem& p, GmmMaps* maps) {
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(3, "cuTensorMapEncodeTiled(x) failed: " + std::to_string(int(r)));
+  } else {
+    maps->x = CUtensorMap{};
   }
   {
     cuuint64_t dims[3] = {static_cast<cuuint64_t>(p.Ci), static_cast<cuuint64_t>(p.K),
@@ -450,9 +537,13 @@ int gmm_tc_launch(const GmmProblem& p, const GmmMaps& maps, int* status, uint64_
   a.shots = p.shots;
   const int64_t tile_m = kBlockM * mt_for(p.Co);
   a.num_tiles = ((p.shots + tile_m - 1) / tile_m) * p.NT;
+  a.order = p.order;
+  a.x = static_cast<const __nv_bfloat16*>(p.x);
+  a.x_node_stride = p.x_node_stride;
   a.y = p.y;
   a.y_shot_stride = p.y_shot_stride;
   a.y_node_stride = p.y_node_stride;
+  a.y_cg_stride = p.y_cg_stride;
   a.epi = p.epi;
   a.head = p.head;
   a.status = status;
@@ -461,23 +552,28 @@ int gmm_tc_launch(const GmmProblem& p, const GmmMaps& maps, int* status, uint64_
   while (cols < static_cast<uint32_t>(2 * mt_for(p.Co) * p.Co)) cols <<= 1;
   a.tmem_cols = cols;
   const int smem = smem_bytes_for(p.Co, a.stages);
-  KernelFn fn = select_kernel(p.Co);
-  if (!fn) return fail(2, "unsupported C_out for the tcgen05 path");
-  static bool configured[9] = {false};
-  if (!configured[p.Co / 32]) {
-    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kSmemLimit);
-    if (e != cudaSuccess) return fail(4, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
-    configured[p.Co / 32] = true;
+  const bool head = p.head.head_w != nullptr;
+  KernelFn fn = select_kernel(p.Co, p.blocked, p.epi, head);
+  if (!fn) return fail(2, "unsupported C_out / layout / epilogue combination for the tcgen05 path");
+  static std::mutex mu;
+  static std::unordered_set<const void*> configured;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!configured.count(reinterpret_cast<const void*>(fn))) {
+      cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+      if (e != cudaSuccess) return fail(4, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+      configured.insert(reinterpret_cast<const void*>(fn));
+    }
   }
   const int64_t grid = std::min<int64_t>(a.num_tiles, num_sms());
   void* args[] = {const_cast<CUtensorMap*>(&maps.x), const_cast<CUtensorMap*>(&maps.w), &a};
   cudaError_t le = cudaLaunchKernel(reinterpret_cast<const void*>(fn), dim3(static_cast<unsigned>(grid)),
                                     dim3(kThreads), args, static_cast<size_t>(smem), stream);
   if (le != cudaSuccess) return fail(4, std::string("gmm_tc_kernel launch: ") + cudaGetErrorString(le));
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return fail(4, std::string("gmm_tc_kernel launch: ") + cudaGetErrorString(e));
   return 0;
 }
+
+int gmm_tc_tile_shots(int Co) { return kBlockM * mt_for(Co); }
 
 }  // namespace bpc

@@ -23,6 +23,7 @@ struct bpc_predecoder {
   int32_t* d2c = nullptr;        // (N_c, K)
   int32_t* xor_nbr = nullptr;    // (N_d, 2, 2)
   uint8_t* check_type = nullptr; // (N_c)
+  int32_t* check_order = nullptr; // (N_c) processing order of the data -> check steps, or null
   void* embed = nullptr;         // (4, C)
   void* w_c2d = nullptr;         // (L, C, K C)
   void* w_d2c = nullptr;         // (L, 2, C, K C)
@@ -43,11 +44,14 @@ constexpr int kEmbNodes = 32;
 size_t esize(int dtype) { return dtype == BPC_DTYPE_F32 ? 4 : 2; }
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
-// det (rows of N_c bytes, shot-major) -> h_c[n][s][:] = embed[2 type(n) + det] and bits[n][s / 32].
+// det (rows of N_c bytes, shot-major) -> h_c features = embed[2 type(n) + det] and bits[n][s / 32].
+// Feature element (shot s, node n, channel c) goes to n node_stride + (c / 8) cg_stride + s shot_stride + c % 8 (rows
+// layouts, tm = 0) or, blocked with tile tm, to n node_stride + (s / tm) C tm + (c / 8) tm 8 + (s % tm) 8 + c % 8.
 template <typename T>
 __global__ void __launch_bounds__(256) embed_kernel(const uint8_t* __restrict__ det, int64_t shots, int N_c, int C,
                                                    const uint8_t* __restrict__ ctype, const T* __restrict__ embed,
-                                                   T* __restrict__ hc, int64_t S, uint32_t* __restrict__ bits,
+                                                   T* __restrict__ hc, int64_t node_stride, int64_t cg_stride,
+                                                   int64_t shot_stride, int tm, uint32_t* __restrict__ bits,
                                                    int64_t words) {
   __shared__ uint8_t tile[kEmbNodes][kEmbShots + 4];
   __shared__ __align__(16) T emb[4 * 256];
@@ -72,19 +76,23 @@ __global__ void __launch_bounds__(256) embed_kernel(const uint8_t* __restrict__ 
       if (lane == 0 && word < words) bits[static_cast<int64_t>(n) * words + word] = m;
     }
   }
-  // features: 16-byte vectors; a (node, shot) row is C elements
-  const int vec = 16 / sizeof(T);
-  const int row_vecs = C / vec;
+  // features in 8-element groups (16 bytes of bf16, 32 of fp32: two 16-byte vectors)
+  constexpr int kVec = 16 / sizeof(T);
+  const int groups = C / 8;
   const int64_t smax = (shots - s0) < kEmbShots ? (shots - s0) : kEmbShots;
   for (int j = 0; j < kEmbNodes; ++j) {
     const int n = n0 + j;
     if (n >= N_c) break;
     const int tb = 2 * ctype[n];
-    T* base = hc + (static_cast<int64_t>(n) * S + s0) * C;
-    for (int e = threadIdx.x; e < smax * row_vecs; e += blockDim.x) {
-      const int s = e / row_vecs, v = e - s * row_vecs;
+    T* base = hc + static_cast<int64_t>(n) * node_stride;
+    for (int e = threadIdx.x; e < groups * smax; e += blockDim.x) {
+      const int g = e / smax, s = e - g * smax;              // shots fastest: contiguous in the chunked layout
       const int tok = tb + tile[j][s];
-      reinterpret_cast<uint4*>(base + static_cast<int64_t>(s) * C)[v] = reinterpret_cast<const uint4*>(emb + tok * C)[v];
+      const int64_t shot = s0 + s;
+      T* dst = tm ? base + (shot / tm) * C * tm + g * tm * 8 + (shot % tm) * 8 : base + g * cg_stride + shot * shot_stride;
+      const uint4* src = reinterpret_cast<const uint4*>(emb + tok * C + g * 8);
+#pragma unroll
+      for (int v = 0; v < 8 / kVec; ++v) reinterpret_cast<uint4*>(dst)[v] = src[v];
     }
   }
 }
@@ -113,9 +121,10 @@ struct Layout {
   size_t off_hc, off_hd, off_bits, total;
 };
 
+// Shot capacity S of a pass: a multiple of 256, the tensor-core kernel's tile in the chunked layout.
 Layout layout_for(const bpc_predecoder_config& c, int64_t chunk) {
   Layout L;
-  L.S = ((chunk + 127) / 128) * 128;
+  L.S = ((chunk + 255) / 256) * 256;
   const size_t es = esize(c.dtype);
   L.off_hc = 0;
   L.off_hd = align256(L.off_hc + static_cast<size_t>(c.n_checks) * L.S * c.channels * es);
@@ -141,7 +150,8 @@ int copy_in(T** dst, const void* src, size_t bytes) {
 using namespace bpc;
 
 extern "C" int bpc_predecoder_create(const bpc_predecoder_config* cfg, const int32_t* c2d, const int32_t* d2c,
-                                     const int32_t* xor_nbr, const uint8_t* check_type, bpc_predecoder** out) {
+                                     const int32_t* xor_nbr, const uint8_t* check_type, const int32_t* check_order,
+                                     bpc_predecoder** out) {
   if (!cfg || !c2d || !d2c || !xor_nbr || !check_type || !out) return fail(BPC_ERR_ARG, "null argument");
   *out = nullptr;
   const auto& c = *cfg;
@@ -158,6 +168,20 @@ extern "C" int bpc_predecoder_create(const bpc_predecoder_config* cfg, const int
       (e = copy_in(&h->check_type, check_type, c.n_checks))) {
     bpc_predecoder_destroy(h);
     return e;
+  }
+  if (check_order) {
+    std::vector<char> seen(c.n_checks, 0);
+    for (int i = 0; i < c.n_checks; ++i) {
+      if (check_order[i] < 0 || check_order[i] >= c.n_checks || seen[check_order[i]]) {
+        bpc_predecoder_destroy(h);
+        return fail(BPC_ERR_ARG, "check_order is not a permutation of the check nodes");
+      }
+      seen[check_order[i]] = 1;
+    }
+    if ((e = copy_in(&h->check_order, check_order, sizeof(int32_t) * c.n_checks))) {
+      bpc_predecoder_destroy(h);
+      return e;
+    }
   }
   int zero = 0;
   if ((e = copy_in(&h->status, &zero, sizeof(int)))) {
@@ -201,12 +225,12 @@ extern "C" int bpc_predecoder_forward(bpc_predecoder* h, const uint8_t* det, flo
   const auto& c = h->cfg;
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   // largest chunk (multiple of 128 shots, at most B rounded up) whose layout fits the workspace
-  int64_t chunk = ((B + 127) / 128) * 128;
-  const size_t per128 = layout_for(c, 128).total;
-  if (workspace_bytes < per128) return fail(BPC_ERR_SPACE, "workspace smaller than one 128-shot chunk");
-  while (chunk > 128 && layout_for(c, chunk).total > workspace_bytes) {
-    const int64_t fit = static_cast<int64_t>(workspace_bytes / per128) * 128;
-    chunk = std::max<int64_t>(128, std::min(chunk - 128, fit));
+  int64_t chunk = ((B + 255) / 256) * 256;
+  const size_t per256 = layout_for(c, 256).total;
+  if (workspace_bytes < per256) return fail(BPC_ERR_SPACE, "workspace smaller than one 256-shot pass");
+  while (chunk > 256 && layout_for(c, chunk).total > workspace_bytes) {
+    const int64_t fit = static_cast<int64_t>(workspace_bytes / per256) * 256;
+    chunk = std::max<int64_t>(256, std::min(chunk - 256, fit));
   }
   const Layout L = layout_for(c, chunk);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
@@ -220,18 +244,27 @@ extern "C" int bpc_predecoder_forward(bpc_predecoder* h, const uint8_t* det, flo
   const size_t wl = static_cast<size_t>(c.channels) * c.K * c.channels;
 
   // the two steps of layer l as bipartite-conv problems on the chunk's buffers
+  // tensor-core path: blocked (node, S / TM, C / 8, TM, 8) activations; CUDA-core path: node-major rows (node, S, C)
+  const int tm = tc ? gmm_tc_tile_shots(c.channels) : 0;
+  const int64_t shot_stride = c.channels;
+  const int64_t cg_stride = 8;
+  const int64_t node_stride = L.S * c.channels;
+  if (tc && L.S % tm != 0) return fail(BPC_ERR_ARG, "pass size is not a multiple of the tensor-core tile");
   GmmProblem c2d, d2c;
   c2d.x = hc;
-  c2d.x_shot_stride = c.channels;
-  c2d.x_node_stride = L.S * c.channels;
+  c2d.blocked = tc;
+  c2d.x_shot_stride = shot_stride;
+  c2d.x_node_stride = node_stride;
+  c2d.x_cg_stride = cg_stride;
   c2d.NS = c.n_checks;
   c2d.idx = h->c2d;
   c2d.NT = c.n_data;
   c2d.K = c.K;
   c2d.Ci = c2d.Co = c.channels;
   c2d.y = hd;
-  c2d.y_shot_stride = c.channels;
-  c2d.y_node_stride = L.S * c.channels;
+  c2d.y_shot_stride = shot_stride;
+  c2d.y_node_stride = node_stride;
+  c2d.y_cg_stride = cg_stride;
   c2d.n_wtypes = 1;
   c2d.type_split = c.n_data;
   d2c = c2d;
@@ -242,6 +275,7 @@ extern "C" int bpc_predecoder_forward(bpc_predecoder* h, const uint8_t* det, flo
   d2c.y = hc;
   d2c.n_wtypes = 2;
   d2c.type_split = c.z_check_begin;
+  d2c.order = h->check_order;
   d2c.epi = kEpiGeluResid;
 
   GmmMaps mc2d, md2c;
@@ -272,11 +306,13 @@ extern "C" int bpc_predecoder_forward(bpc_predecoder* h, const uint8_t* det, flo
       if (f32)
         embed_kernel<float><<<grid, 256, 0, stream>>>(det + b0 * c.n_checks, Sb, c.n_checks, c.channels,
                                                       h->check_type, static_cast<const float*>(h->embed),
-                                                      static_cast<float*>(hc), L.S, bits, words);
+                                                      static_cast<float*>(hc), node_stride, cg_stride, shot_stride,
+                                                      tm, bits, words);
       else
         embed_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
             det + b0 * c.n_checks, Sb, c.n_checks, c.channels, h->check_type,
-            static_cast<const __nv_bfloat16*>(h->embed), static_cast<__nv_bfloat16*>(hc), L.S, bits, words);
+            static_cast<const __nv_bfloat16*>(h->embed), static_cast<__nv_bfloat16*>(hc), node_stride, cg_stride,
+            shot_stride, tm, bits, words);
       cudaError_t e = cudaGetLastError();
       if (e != cudaSuccess) return fail(BPC_ERR_LAUNCH, std::string("embed_kernel: ") + cudaGetErrorString(e));
     }
@@ -350,6 +386,7 @@ extern "C" int bpc_predecoder_status(bpc_predecoder* h, bpc_stream_t stream, int
 extern "C" void bpc_predecoder_destroy(bpc_predecoder* h) {
   if (!h) return;
   for (void* p : {static_cast<void*>(h->c2d), static_cast<void*>(h->d2c), static_cast<void*>(h->xor_nbr),
+                  static_cast<void*>(h->check_order),
                   static_cast<void*>(h->check_type), h->embed, h->w_c2d, h->w_d2c, static_cast<void*>(h->head_w),
                   static_cast<void*>(h->head_b), static_cast<void*>(h->status)})
     if (p) cudaFree(p);

@@ -135,6 +135,9 @@ class RotatedSurface:
         # node attributes
         self.check_type = np.repeat(np.arange(2), T * nh).astype(np.int64)
         self.check_t = np.tile(np.repeat(np.arange(T), nh), 2).astype(np.int64)
+        # the checks round by round, X then Z within a round: the order a data -> check step visits them so the data
+        # nodes of a round are swept once for both check types (node order keeps the types apart)
+        self.check_round_order = np.lexsort((np.arange(N_c), self.check_type, self.check_t)).astype(np.int64)
         self.check_place = np.array([places[ty][s] for ty in range(2) for _ in range(T) for s in range(nh)], np.int64)
 
         # syndrome cancellation: a predicted X flip of data (t, q) flips the Z checks around q at round t,

@@ -69,6 +69,7 @@ class PreDecoder:
             "d2c": np.ascontiguousarray(geo.d2c_all, np.int32),
             "xor": np.ascontiguousarray(geo.xor_nbr, np.int32),
             "ctype": np.ascontiguousarray(geo.check_type, np.uint8),
+            "order": np.ascontiguousarray(geo.check_round_order, np.int32),
         }
         h = ctypes.c_void_p()
         with torch.cuda.device(self.device):

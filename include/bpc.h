@@ -45,7 +45,7 @@ BPC_API int bpc_last_error(char* buf, int len);
  *   y[b, n, :] = sum_r x[b, idx[n, r], :] W_r^T,   W (Co, K*Ci) row-major, W_r = W[:, r*Ci:(r+1)*Ci]
  * x (B, NS, Ci), y (B, NT, Co), idx (NT, K) int32 with NS (or any value outside [0, NS)) reading a zero row.
  * dtype BPC_DTYPE_BF16: bf16 x / w / y, fp32 accumulation (tcgen05 tensor cores when Ci >= 64, Co % 32 == 0,
- * Co <= 256; CUDA cores otherwise); BPC_DTYPE_F32: fp32 throughout on the CUDA cores.
+ * Co <= 256, K <= 16; CUDA cores otherwise); BPC_DTYPE_F32: fp32 throughout on the CUDA cores.
  * Replaces: training/bb/ising_compare/bb/cascade_net.py:140-153,174-175 (_GatherMM.forward / gather_mm) and
  * cascade_triton.py:100-117,139-148 (gmm with transposed=False, the op cascade::gmm). */
 BPC_API int bpc_gather_mm_fwd(const void* x, const void* w, const int32_t* idx, void* y, int64_t B, int32_t NS, int32_t NT,
@@ -71,9 +71,12 @@ typedef struct {
 
 /* Tables (host memory, copied): c2d (N_d, K) int32 source check per data node (N_c = pad), d2c (N_c, K) int32 source
  * data node per check (N_d = pad), xor_nbr (N_d, 2, 2) int32 checks flipped by a predicted X / Z flip (-1 = none),
- * check_type (N_c) uint8 0 X / 1 Z.  Allocates the handle's device tables and weights. */
+ * check_type (N_c) uint8 0 X / 1 Z, check_order (N_c) int32 the order in which a data -> check step visits the checks
+ * (a permutation; NULL = node order; visiting X and Z checks of one round together lets each data block be read
+ * from HBM once per step).  Allocates the handle's device tables and weights. */
 BPC_API int bpc_predecoder_create(const bpc_predecoder_config* cfg, const int32_t* c2d, const int32_t* d2c,
-                          const int32_t* xor_nbr, const uint8_t* check_type, bpc_predecoder** out);
+                          const int32_t* xor_nbr, const uint8_t* check_type, const int32_t* check_order,
+                          bpc_predecoder** out);
 
 /* Weights (host memory, copied; element type = cfg.dtype except head_w / head_b which are fp32):
  * embed (4, C); w_c2d (L, C, K*C); w_d2c (L, 2, C, K*C) (X then Z checks); head_w (2, C); head_b (2). */

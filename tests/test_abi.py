@@ -53,7 +53,7 @@ def test_predecoder_argument_checks(lib):
     cfg = _lib.PredecoderConfig(0, 64, 8, 1, 10, 10, 5)
     h = ctypes.c_void_p()
     z = (ctypes.c_int32 * 100)()
-    rc = lib.bpc_predecoder_create(ctypes.byref(cfg), z, z, z, z, ctypes.byref(h))
+    rc = lib.bpc_predecoder_create(ctypes.byref(cfg), z, z, z, z, None, ctypes.byref(h))
     assert rc == 2 and "configuration" in _lib.last_error()
     assert lib.bpc_predecoder_forward(None, None, None, None, 1, None, 0, None) == 2
     assert lib.bpc_predecoder_workspace_size(None, 128) == 0
