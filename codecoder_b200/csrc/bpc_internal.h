@@ -50,6 +50,9 @@ struct GmmProblem {
   int64_t y_shot_stride = 0, y_node_stride = 0, y_cg_stride = 8;
   int epi = kEpiStore;
   HeadEpilogue head;
+  // tensor-core path: a device counter that is zero when the kernel starts hands out tiles dynamically (null:
+  // static striding)
+  unsigned long long* tile_counter = nullptr;
 };
 
 // Tensor maps a caller may prepare once and reuse across launches (the pre-decoder does).

@@ -68,6 +68,7 @@ struct TcArgs {
   int* status;
   uint64_t timeout_ns;
   uint32_t tmem_cols;
+  unsigned long long* tile_counter;       // dynamic scheduling (zero at launch), or null
 };
 
 __device__ __forceinline__ int target_of(const TcArgs& a, int64_t tile) {
@@ -77,24 +78,33 @@ __device__ __forceinline__ int target_of(const TcArgs& a, int64_t tile) {
 
 constexpr int kMaxK = 16;   // relations per target on the tensor-core path
 
-// A tile's target node and index row.  The K index loads are independent (unrolled, predicated), and every role
-// loads the next tile's row while it works on the current one, so no role waits on a chain of table loads.
+// A tile's target node and index row.  The loads are independent (unrolled, predicated) and every role issues the
+// next tile's loads one tile ahead; the valid mask is formed only when the tile starts (finish_row), so no role
+// stalls on table loads in the middle of its pipeline.
 struct TileRow {
   int n;
   uint32_t vm;              // relations whose source is in [0, NS)
   int src[kMaxK];
 };
 
-__device__ __forceinline__ TileRow load_row(const TcArgs& a, int64_t tile) {
-  TileRow t;
+__device__ __forceinline__ void issue_row(const TcArgs& a, int64_t tile, TileRow& t) {
   t.n = target_of(a, tile);
   const int32_t* row = a.idx + static_cast<int64_t>(t.n) * a.K;
 #pragma unroll
   for (int r = 0; r < kMaxK; ++r) t.src[r] = r < a.K ? __ldg(row + r) : -1;
+}
+
+__device__ __forceinline__ void finish_row(const TcArgs& a, TileRow& t) {
   t.vm = 0;
 #pragma unroll
   for (int r = 0; r < kMaxK; ++r)
     if (t.src[r] >= 0 && t.src[r] < a.NS) t.vm |= 1u << r;
+}
+
+__device__ __forceinline__ TileRow load_row(const TcArgs& a, int64_t tile) {
+  TileRow t;
+  issue_row(a, tile, t);
+  finish_row(a, t);
   return t;
 }
 
@@ -103,6 +113,16 @@ __device__ __forceinline__ void ld_chunk(const __nv_bfloat16* base, int64_t cg_s
 #pragma unroll
   for (int j = 0; j < 4; ++j) r[j] = *reinterpret_cast<const uint4*>(base + (4 * c + j) * cg_stride);
 }
+
+// Tiles reach the MMA and epilogue warps through a small ring in shared memory written by the producer thread,
+// which is the only role that picks tiles: from a global counter (dynamic scheduling: all CTAs stay within a
+// window of consecutive tiles, so the sources they share stay in L2) or, without a counter, by striding.
+constexpr int kRing = 4;
+struct RingEntry {
+  long long tile;           // -1: no more tiles
+  int n;                    // target node
+  uint32_t vm;              // relations with a source in [0, NS)
+};
 
 template <int MT, int NCH, bool BLOCKED, int EPI, bool HEAD>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -122,7 +142,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* accf = bars + 2 * S;
   uint64_t* acce = bars + 2 * S + 2;
   uint64_t* drain = bars + 2 * S + 4;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
+  uint64_t* tfull = bars + 2 * S + 5;
+  uint64_t* tempty = bars + 2 * S + 5 + kRing;
+  volatile RingEntry* ring = reinterpret_cast<volatile RingEntry*>(bars + 2 * S + 5 + 2 * kRing);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5 + 2 * kRing + 2 * kRing);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -136,6 +159,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(smem_u32(&accf[i]), 1);
       mbar_init(smem_u32(&acce[i]), kEpiWarps);
+    }
+    for (int i = 0; i < kRing; ++i) {
+      mbar_init(smem_u32(&tfull[i]), 1);
+      mbar_init(smem_u32(&tempty[i]), 1 + kEpiWarps);
     }
     mbar_init(smem_u32(drain), 1);
     *abort_flag = 0;
@@ -158,27 +185,35 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       uint32_t armed = 0, armed_parity = 0;   // stages with a load in flight and the parity it completes
+      int rslot = 0;
+      uint32_t rphase = 0;
       bool ok = true;
-      TileRow cur = load_row(a, blockIdx.x < a.num_tiles ? blockIdx.x : 0);
-      for (int64_t tile = blockIdx.x; tile < a.num_tiles && ok; tile += gridDim.x) {
+      long long next = a.tile_counter ? atomicAdd(a.tile_counter, 1ull) : static_cast<long long>(blockIdx.x);
+      TileRow nrow;
+      issue_row(a, next < a.num_tiles ? next : 0, nrow);
+      while (ok) {
+        const long long tile = next;
+        finish_row(a, nrow);
+        const TileRow cur = nrow;
+        // publish the tile (or the end) to the MMA and epilogue warps
+        if (!mbar_wait(smem_u32(&tempty[rslot]), rphase ^ 1u, abort_flag, a.status, a.timeout_ns)) break;
+        ring[rslot].tile = tile < a.num_tiles ? tile : -1;
+        ring[rslot].n = cur.n;
+        ring[rslot].vm = cur.vm;
+        mbar_arrive(smem_u32(&tfull[rslot]));
+        if (++rslot == kRing) {
+          rslot = 0;
+          rphase ^= 1u;
+        }
+        if (tile >= a.num_tiles) break;
+        // the next tile: picked now so its index row and its source / residual blocks are on their way (to L2)
+        // while this tile is loaded and computed
+        next = a.tile_counter ? atomicAdd(a.tile_counter, 1ull) : tile + gridDim.x;
+        const bool has_next = next < a.num_tiles;
+        issue_row(a, has_next ? next : tile, nrow);
         const int n = cur.n;
         const int64_t s0 = (tile / a.NT) * kTileM;
         const int wrow = (n >= a.type_split) ? Co : 0;
-        const int64_t nt = tile + gridDim.x;
-        const TileRow nxt = load_row(a, nt < a.num_tiles ? nt : tile);
-        if (BLOCKED && nt < a.num_tiles) {
-          // ask L2 for the next tile's source blocks (and residual block) while this tile is loaded and computed
-          const int64_t ns0 = (nt / a.NT) * kTileM;
-#pragma unroll
-          for (int r = 0; r < kMaxK; ++r)
-            if (nxt.vm & (1u << r))
-              bulk_prefetch_l2(a.x + static_cast<int64_t>(nxt.src[r]) * a.x_node_stride + ns0 * a.Ci,
-                               a.Ci * kTileM * 2);
-          if (EPI == kEpiGeluResid)
-            bulk_prefetch_l2(reinterpret_cast<const __nv_bfloat16*>(a.y) + static_cast<int64_t>(nxt.n) * a.y_node_stride +
-                                 ns0 * Co,
-                             Co * kTileM * 2);
-        }
 #pragma unroll 1
         for (int r = 0; r < a.K && ok; ++r) {
           if (!(cur.vm & (1u << r))) continue;
@@ -208,8 +243,22 @@ __global__ void __launch_bounds__(kThreads, 1)
               phase ^= 1u;
             }
           }
+          if (BLOCKED && has_next && r == 0) {
+            // after the first stage of this tile is on its way: the next tile's blocks towards L2
+            TileRow pn = nrow;
+            finish_row(a, pn);
+            const int64_t ns0 = (next / a.NT) * kTileM;
+#pragma unroll
+            for (int q = 0; q < kMaxK; ++q)
+              if (pn.vm & (1u << q))
+                bulk_prefetch_l2(a.x + static_cast<int64_t>(pn.src[q]) * a.x_node_stride + ns0 * a.Ci,
+                                 a.Ci * kTileM * 2);
+            if (EPI == kEpiGeluResid)
+              bulk_prefetch_l2(reinterpret_cast<const __nv_bfloat16*>(a.y) +
+                                   static_cast<int64_t>(pn.n) * a.y_node_stride + ns0 * Co,
+                               Co * kTileM * 2);
+          }
         }
-        cur = nxt;
       }
       if (!ok) {
         // drain: wait (bounded) for every load this thread issued before leaving the CTA's shared memory
@@ -230,12 +279,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
+      int rslot = 0;
+      uint32_t rphase = 0;
       bool ok = true;
-      TileRow cur = load_row(a, blockIdx.x < a.num_tiles ? blockIdx.x : 0);
-      for (int64_t tile = blockIdx.x; tile < a.num_tiles && ok; tile += gridDim.x) {
-        const uint32_t vm = cur.vm;
-        const int64_t nt = tile + gridDim.x;
-        cur = load_row(a, nt < a.num_tiles ? nt : tile);     // next tile's row, loaded while this one is issued
+      while (ok) {
+        if (!mbar_wait(smem_u32(&tfull[rslot]), rphase, abort_flag, a.status, a.timeout_ns)) break;
+        const long long tile = ring[rslot].tile;
+        const uint32_t vm = ring[rslot].vm;
+        mbar_arrive(smem_u32(&tempty[rslot]));
+        if (++rslot == kRing) {
+          rslot = 0;
+          rphase ^= 1u;
+        }
+        if (tile < 0) break;
         if (!mbar_wait(smem_u32(&acce[acc]), acc_phase ^ 1u, abort_flag, a.status, a.timeout_ns)) {
           ok = false;
           break;
@@ -301,14 +357,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int64_t cgs = BLOCKED ? kTileM * 8 : a.y_cg_stride;
     int acc = 0;
     uint32_t acc_phase = 0;
-    TileRow cur = load_row(a, blockIdx.x < a.num_tiles ? blockIdx.x : 0);
-    for (int64_t tile = blockIdx.x; tile < a.num_tiles; tile += gridDim.x) {
-      const int n = cur.n;
-      const uint32_t vm = active ? cur.vm : 0u;
-      {
-        const int64_t nt = tile + gridDim.x;
-        cur = load_row(a, nt < a.num_tiles ? nt : tile);
+    int rslot = 0;
+    uint32_t rphase = 0;
+    while (true) {
+      if (!mbar_wait(smem_u32(&tfull[rslot]), rphase, abort_flag, a.status, a.timeout_ns)) break;
+      const long long tile = ring[rslot].tile;
+      const int n = ring[rslot].n;
+      const uint32_t vm = active ? ring[rslot].vm : 0u;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&tempty[rslot]));
+      if (++rslot == kRing) {
+        rslot = 0;
+        rphase ^= 1u;
       }
+      if (tile < 0) break;
       const int64_t s0 = (tile / a.NT) * kTileM + m * kBlockM;
       const int64_t shot = s0 + row;
       const bool ok = active && shot < a.shots;
@@ -416,7 +478,9 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
 
 int item_bytes_for(int Co) { return kSubBytes * mt_for(Co) + Co * 128; }
 
-int smem_bytes_for(int Co, int stages) { return 1024 + stages * item_bytes_for(Co) + (2 * stages + 5) * 8 + 8; }
+int smem_bytes_for(int Co, int stages) {
+  return 1024 + stages * item_bytes_for(Co) + (2 * stages + 5 + 2 * kRing) * 8 + kRing * 16 + 8;
+}
 
 int stages_for(int Co) {
   int s = kMaxStages;
@@ -548,6 +612,7 @@ int gmm_tc_launch(const GmmProblem& p, const GmmMaps& maps, int* status, uint64_
   a.head = p.head;
   a.status = status;
   a.timeout_ns = timeout_ns;
+  a.tile_counter = p.tile_counter;
   uint32_t cols = 32;
   while (cols < static_cast<uint32_t>(2 * mt_for(p.Co) * p.Co)) cols <<= 1;
   a.tmem_cols = cols;

@@ -30,6 +30,7 @@ struct bpc_predecoder {
   float* head_w = nullptr;       // (2, C)
   float* head_b = nullptr;       // (2)
   int* status = nullptr;         // device watchdog status word
+  unsigned long long* tile_counter = nullptr;   // dynamic tile scheduling of the tensor-core steps
   bool weights_set = false;
   uint64_t timeout_ns = 2000000000ull;
   std::vector<cudaEvent_t> step_events;   // optional (before, after) pairs around each bipartite-step launch
@@ -183,6 +184,11 @@ extern "C" int bpc_predecoder_create(const bpc_predecoder_config* cfg, const int
       return e;
     }
   }
+  const unsigned long long zero64 = 0;
+  if ((e = copy_in(&h->tile_counter, &zero64, sizeof(zero64)))) {
+    bpc_predecoder_destroy(h);
+    return e;
+  }
   int zero = 0;
   if ((e = copy_in(&h->status, &zero, sizeof(int)))) {
     bpc_predecoder_destroy(h);
@@ -335,12 +341,18 @@ extern "C" int bpc_predecoder_forward(bpc_predecoder* h, const uint8_t* det, flo
       for (int step = 0; step < 2; ++step) {
         const GmmProblem& p = step == 0 ? c2d : d2c;
         const bool rec = 2 * n_rec + 1 < h->step_events.size();
+        if (tc) {   // the tile counter of the dynamic scheduler starts at zero
+          cudaError_t me = cudaMemsetAsync(h->tile_counter, 0, sizeof(unsigned long long), stream);
+          if (me != cudaSuccess) return fail(BPC_ERR_LAUNCH, std::string("cudaMemsetAsync: ") + cudaGetErrorString(me));
+        }
         if (rec) cudaEventRecord(h->step_events[2 * n_rec], stream);
         int e;
         if (tc) {
           GmmMaps m = step == 0 ? mc2d : md2c;
           m.w = step == 0 ? wm_c2d[l] : wm_d2c[l];
-          e = gmm_tc_launch(p, m, h->status, h->timeout_ns, stream);
+          GmmProblem pc = p;
+          pc.tile_counter = h->tile_counter;
+          e = gmm_tc_launch(pc, m, h->status, h->timeout_ns, stream);
         } else {
           e = gmm_fma_launch(p, f32, stream);
         }
@@ -388,7 +400,7 @@ extern "C" void bpc_predecoder_destroy(bpc_predecoder* h) {
   for (void* p : {static_cast<void*>(h->c2d), static_cast<void*>(h->d2c), static_cast<void*>(h->xor_nbr),
                   static_cast<void*>(h->check_order),
                   static_cast<void*>(h->check_type), h->embed, h->w_c2d, h->w_d2c, static_cast<void*>(h->head_w),
-                  static_cast<void*>(h->head_b), static_cast<void*>(h->status)})
+                  static_cast<void*>(h->head_b), static_cast<void*>(h->status), static_cast<void*>(h->tile_counter)})
     if (p) cudaFree(p);
   delete h;
 }
