@@ -168,12 +168,6 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
                : "memory");
 }
 
-// Ask L2 to fetch [src, src + bytes) (16-byte aligned, size a multiple of 16) without waiting for it.
-__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
-               : "memory");
-}
-
 // Instruction descriptor for kind::f16: fp32 accumulator (bits 4-5 = 1), A and B bf16 (bits 7-9, 10-12 = 1),
 // both K-major (bits 15, 16 = 0), N >> 3 in bits 17-22, M >> 4 in bits 24-28.
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {

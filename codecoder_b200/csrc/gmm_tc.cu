@@ -10,9 +10,8 @@
 //            tensor (channel, shot, node); one TMA box per stage into the 128-byte-swizzled K-major layout.
 //   blocked  the pre-decoder's (node, shots / TM, C / 8, TM, 8) layout, TM = 128 MT: a tile's activations are one
 //            contiguous block, so a stage is one 1D bulk copy (8 channel groups x TM shots x 16 bytes) straight into
-//            the canonical no-swizzle K-major layout (8-row x 16-byte core matrices), the producer can ask L2 for
-//            the next tile's source and residual blocks one instruction each, and the epilogue's loads and stores
-//            cover 512 contiguous bytes per warp instruction.
+//            the canonical no-swizzle K-major layout (8-row x 16-byte core matrices), and the epilogue's loads and
+//            stores cover 512 contiguous bytes per warp instruction.
 // W_r (Co x 64 channels per stage) always comes by TMA in the 128-byte-swizzled K-major layout.
 //
 // Roles (320 threads, one CTA per SM):
@@ -101,12 +100,6 @@ __device__ __forceinline__ void finish_row(const TcArgs& a, TileRow& t) {
     if (t.src[r] >= 0 && t.src[r] < a.NS) t.vm |= 1u << r;
 }
 
-__device__ __forceinline__ TileRow load_row(const TcArgs& a, int64_t tile) {
-  TileRow t;
-  issue_row(a, tile, t);
-  finish_row(a, t);
-  return t;
-}
 
 // the 4 channel groups (32 channels) of chunk c of one shot's row
 __device__ __forceinline__ void ld_chunk(const __nv_bfloat16* base, int64_t cg_stride, int c, uint4 (&r)[4]) {
@@ -206,11 +199,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           rphase ^= 1u;
         }
         if (tile >= a.num_tiles) break;
-        // the next tile: picked now so its index row and its source / residual blocks are on their way (to L2)
-        // while this tile is loaded and computed
+        // the next tile: picked now so its index row is on its way while this tile is loaded
         next = a.tile_counter ? atomicAdd(a.tile_counter, 1ull) : tile + gridDim.x;
-        const bool has_next = next < a.num_tiles;
-        issue_row(a, has_next ? next : tile, nrow);
+        issue_row(a, next < a.num_tiles ? next : tile, nrow);
         const int n = cur.n;
         const int64_t s0 = (tile / a.NT) * kTileM;
         const int wrow = (n >= a.type_split) ? Co : 0;
@@ -242,21 +233,6 @@ __global__ void __launch_bounds__(kThreads, 1)
               stage = 0;
               phase ^= 1u;
             }
-          }
-          if (BLOCKED && has_next && r == 0) {
-            // after the first stage of this tile is on its way: the next tile's blocks towards L2
-            TileRow pn = nrow;
-            finish_row(a, pn);
-            const int64_t ns0 = (next / a.NT) * kTileM;
-#pragma unroll
-            for (int q = 0; q < kMaxK; ++q)
-              if (pn.vm & (1u << q))
-                bulk_prefetch_l2(a.x + static_cast<int64_t>(pn.src[q]) * a.x_node_stride + ns0 * a.Ci,
-                                 a.Ci * kTileM * 2);
-            if (EPI == kEpiGeluResid)
-              bulk_prefetch_l2(reinterpret_cast<const __nv_bfloat16*>(a.y) +
-                                   static_cast<int64_t>(pn.n) * a.y_node_stride + ns0 * Co,
-                               Co * kTileM * 2);
           }
         }
       }
