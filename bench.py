@@ -215,7 +215,8 @@ def main():
         dist.barrier()
         build()                                         # no-op once rank 0 built it
 
-    shots = args.shots // world
+    from codecoder_b200.shard import shard
+    _, shots = shard(args.shots, world, rank)
     det, _ = sample_torch(g, cfg.p, shots, SEED + 7919 * rank, device=dev)
     pd = PreDecoder(g, cfg, params, device=dev, chunk_shots=args.chunk)
     logits = torch.empty(shots, g.N_d, 2, dtype=torch.float32, device=dev)
@@ -225,10 +226,15 @@ def main():
     chunks = [min(S, shots - b) for b in range(0, shots, S)]
     launches_per_fwd = len(chunks) * (2 * cfg.layers + 2)
     step_flops = []                                     # algorithmic FLOPs of each bipartite-step launch in order
+    exec_flops = []                                     # the MMA work actually done (pad relations are skipped)
+    live_c2d = float((g.c2d[0] < g.N_c).sum()) / g.K
+    live_d2c = float((g.d2c_all < g.N_d).sum()) / g.K
     for sb in chunks:
         for _ in range(cfg.layers):
             step_flops.append(2.0 * cfg.K * cfg.channels ** 2 * g.N_d * sb)
             step_flops.append(2.0 * cfg.K * cfg.channels ** 2 * g.N_c * sb)
+            exec_flops.append(2.0 * cfg.K * cfg.channels ** 2 * live_c2d * sb)
+            exec_flops.append(2.0 * cfg.K * cfg.channels ** 2 * live_d2c * sb)
     ev_pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in step_flops]
 
     def barrier():
@@ -268,7 +274,7 @@ def main():
     if pd.status() != 0:
         raise RuntimeError("device watchdog fired in the timed region")
 
-    value = args.steps * shots * world / (ms / 1000.0)
+    value = args.steps * args.shots / (ms / 1000.0)
     pk = peaks()
     achieved = tc_flops / (tc_ms / 1000.0) / 1e12
     fps = flops_per_shot(cfg, g.N_c, g.N_d)
@@ -277,6 +283,7 @@ def main():
             "peak_kind": f"{pk['source']} sustained bf16 (cuBLAS)", "traffic": None,
             "avg_launch_ms": tc_ms / len(step_ms), "launches": len(step_ms),
             "flop_per_unit": 2 * cfg.K * cfg.channels ** 2, "unit_desc": "target node x shot",
+            "executed_tflops": sum(exec_flops) / (tc_ms / 1000.0) / 1e12,
             "whole_step_frac": value / world * fps / 1e12 / pk["bf16_tflops_sustained"]}
     tr_path = os.path.join(REPO, "profiles", "gmm_tc_d13_traffic.json")
     if os.path.exists(tr_path):
@@ -310,9 +317,9 @@ def main():
         e2.synchronize()
         barrier()
         ms2 = max_over_ranks(s2.elapsed_time(e2))
-        e2e = {"value": args.steps * shots * world / (ms2 / 1000.0), "unit": UNIT,
-               "h2d_bytes_per_step": det.numel() * world,
-               "d2h_bytes_per_step": (logits.numel() * 4 + resid.numel()) * world,
+        e2e = {"value": args.steps * args.shots / (ms2 / 1000.0), "unit": UNIT,
+               "h2d_bytes_per_step": args.shots * g.N_c,
+               "d2h_bytes_per_step": args.shots * (g.N_d * 2 * 4 + g.N_c),
                "api": "codecoder_b200.modules.PreDecoder.forward_into (C ABI bpc_predecoder_forward)"}
 
     cpu = None
