@@ -36,6 +36,8 @@ SIGNATURES = {
     "bpc_predecoder_record_step_events": (ctypes.c_int, [c_vp, ctypes.POINTER(c_vp), ctypes.c_int]),
     "bpc_predecoder_status": (ctypes.c_int, [c_vp, c_vp, ctypes.POINTER(ctypes.c_int)]),
     "bpc_predecoder_destroy": (None, [c_vp]),
+    "bpc_predecoder_forward_noalloc": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_vp]),
+    "bpc_noalloc_scratch_bytes": (ctypes.c_size_t, []),
 }
 
 _lib = None
