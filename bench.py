@@ -285,13 +285,20 @@ def main():
             "flop_per_unit": 2 * cfg.K * cfg.channels ** 2, "unit_desc": "target node x shot",
             "executed_tflops": sum(exec_flops) / (tc_ms / 1000.0) / 1e12,
             "whole_step_frac": value / world * fps / 1e12 / pk["bf16_tflops_sustained"]}
-    tr_path = os.path.join(REPO, "profiles", "gmm_tc_d13_traffic.json")
-    if os.path.exists(tr_path):
-        with open(tr_path) as f:
-            tr = json.load(f)
-        units_per_launch = (sum(step_flops) / len(step_flops)) / (2 * cfg.K * cfg.channels ** 2)
-        roof["traffic"] = tr["bytes_per_node_shot"] * units_per_launch
-        roof["traffic_source"] = tr.get("source", "")
+    tr_path = os.path.join(REPO, "profiles", "gmm_tc_d13_traffic.txt")
+    if os.path.exists(tr_path) and args.config == "d13_bf16":
+        per_unit = None
+        for line in open(tr_path):
+            if line.startswith("bytes_per_node_shot:"):
+                per_unit = float(line.split(":", 1)[1])
+        if per_unit:
+            units_per_launch = (sum(step_flops) / len(step_flops)) / (2 * cfg.K * cfg.channels ** 2)
+            roof["traffic"] = per_unit * units_per_launch
+            roof["traffic_unit"] = "bytes per launch (ncu capture scaled by shots)"
+            # sources read once + residual read + write, each 2C bytes per node and shot, averaged over the launches
+            roof["algorithmic_bytes_per_launch"] = sum(
+                (g.N_c + 2 * g.N_d if i % 2 == 0 else g.N_d + 2 * g.N_c) * sb * 2 * cfg.channels
+                for i, sb in enumerate(sb for sb in chunks for _ in range(2 * cfg.layers))) / len(step_flops)
 
     e2e = None
     if not args.no_e2e:
