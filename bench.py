@@ -46,6 +46,8 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-stream", action="store_true")
+    ap.add_argument("--stream-rounds", type=int, default=20000)
     return ap.parse_args()
 
 
@@ -302,24 +304,18 @@ def main():
 
     e2e = None
     if not args.no_e2e:
+        # the public API from pinned host memory: PreDecoder.forward_host copies slices in and out on a copy stream
+        # while the previous slice runs (C ABI bpc_predecoder_forward per slice)
         det_h = det.cpu().pin_memory()
         lg_h = torch.empty(logits.shape, dtype=logits.dtype, pin_memory=True)
         rs_h = torch.empty(resid.shape, dtype=resid.dtype, pin_memory=True)
-        d_in = torch.empty_like(det)
-        for _ in range(1):
-            d_in.copy_(det_h, non_blocking=True)
-            pd.forward_into(d_in, logits, resid)
-            lg_h.copy_(logits, non_blocking=True)
-            rs_h.copy_(resid, non_blocking=True)
-        torch.cuda.synchronize()
+        pd.forward_host(det_h, lg_h, rs_h)
         barrier()
+        torch.cuda.synchronize()
         s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s2.record()
         for _ in range(args.steps):
-            d_in.copy_(det_h, non_blocking=True)
-            pd.forward_into(d_in, logits, resid)
-            lg_h.copy_(logits, non_blocking=True)
-            rs_h.copy_(resid, non_blocking=True)
+            pd.forward_host(det_h, lg_h, rs_h)
         e2.record()
         e2.synchronize()
         barrier()
@@ -327,7 +323,7 @@ def main():
         e2e = {"value": args.steps * args.shots / (ms2 / 1000.0), "unit": UNIT,
                "h2d_bytes_per_step": args.shots * g.N_c,
                "d2h_bytes_per_step": args.shots * (g.N_d * 2 * 4 + g.N_c),
-               "api": "codecoder_b200.modules.PreDecoder.forward_into (C ABI bpc_predecoder_forward)"}
+               "api": "codecoder_b200.modules.PreDecoder.forward_host (C ABI bpc_predecoder_forward per slice)"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -337,6 +333,24 @@ def main():
                "sample": f"{n_shots} shots of the d={cfg.d} workload through the CPU oracle (fp32 torch "
                          f"index_select + matmul, the reference's gather_mm path), {threads} threads"}
 
+    stream = None
+    if rank == 0 and world == 1 and not args.no_stream:
+        # d = 17 streaming: sliding window of 3 rounds, batch 1, one new round per step, one graph replay per round
+        from codecoder_b200.sampler import sample_stream
+        from codecoder_b200.streaming import StreamingDecoder
+        scfg = CONFIGS["d17_stream"]
+        sd = StreamingDecoder(scfg.d, scfg.rounds, scfg, init_params(scfg, SEED), device=dev)
+        rounds = sample_stream(RotatedSurface(scfg.d, 1), scfg.p, args.stream_rounds + 200, SEED + 17)
+        lat = sd.latency(rounds, warmup=200)
+        sg = sd.geo
+        sflop = flops_per_shot(scfg, sg.N_c, sg.N_d)
+        stream = {"config": f"d={scfg.d}, window {scfg.rounds} rounds, batch 1, {scfg.layers} layers, C={scfg.channels},"
+                            f" {scfg.dtype}, p={scfg.p}; full-window forward per new round (CUDA graph replay)",
+                  "rounds": int(len(lat)), "p50_us": float(np.percentile(lat, 50)),
+                  "p99_us": float(np.percentile(lat, 99)), "mean_us": float(lat.mean()),
+                  "clock": "host wall clock from handing a round over to its results in pinned host memory",
+                  "flop_per_round": sflop, "roofline_us_all_sms": sflop / (pk["bf16_tflops"] * 1e12) * 1e6}
+
     if world > 1:
         dist.barrier()
     if rank == 0:
@@ -345,7 +359,7 @@ def main():
                 "scaling": "strong", "vs_baseline": None, "dtype": cfg.dtype, "data": "synthetic",
                 "config": workload(cfg, g, shots, world), "per_gpu": value / world, "roofline": roof,
                 "cpu_baseline": cpu, "e2e": e2e, "clocks": clk.summary(),
-                "gpu_launches": launches_per_fwd * args.steps, "flop_per_shot": fps}
+                "gpu_launches": launches_per_fwd * args.steps, "flop_per_shot": fps, "streaming": stream}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

@@ -134,6 +134,55 @@ class PreDecoder:
 
     __call__ = forward
 
+    def forward_host(self, det_host: torch.Tensor, logits_host: torch.Tensor, residual_host: torch.Tensor,
+                     slice_shots: int | None = None) -> None:
+        """Host buffers in, host buffers out (pinned memory): det (B, N_c) uint8 -> logits (B, N_d, 2) fp32,
+        residual (B, N_c) uint8.  The batch goes through in slices of `slice_shots` (default: the pass size), with
+        the copies of one slice on a copy stream overlapping the forward pass of the previous one (two device buffer
+        sets).  Synchronises before returning."""
+        B = det_host.shape[0]
+        if B == 0:
+            return
+        for t in (det_host, logits_host, residual_host):
+            if t.device.type != "cpu" or not t.is_contiguous():
+                raise ValueError("forward_host takes contiguous host tensors (pinned for overlap)")
+        S = int(slice_shots or self.chunk_shots)
+        S = max(256, (S // 256) * 256)
+        dev = self.device
+        bufs = getattr(self, "_host_bufs", None)
+        if bufs is None or bufs[0][0].shape[0] < S:
+            bufs = [(torch.empty(S, self.geo.N_c, dtype=torch.uint8, device=dev),
+                     torch.empty(S, self.geo.N_d, 2, dtype=torch.float32, device=dev),
+                     torch.empty(S, self.geo.N_c, dtype=torch.uint8, device=dev)) for _ in range(2)]
+            self._host_bufs = bufs
+            self._copy_stream = torch.cuda.Stream(device=dev)
+        comp = torch.cuda.current_stream(dev)
+        copy = self._copy_stream
+        done = [None, None]                     # event: slice buffers free again (outputs copied out)
+        with torch.cuda.device(dev):
+            for i, b0 in enumerate(range(0, B, S)):
+                n = min(S, B - b0)
+                k = i % 2
+                d_det, d_lg, d_rs = (t[:n] for t in bufs[k])
+                with torch.cuda.stream(copy):
+                    if done[k] is not None:
+                        copy.wait_event(done[k])
+                    d_det.copy_(det_host[b0:b0 + n], non_blocking=True)
+                    ready = torch.cuda.Event()
+                    ready.record(copy)
+                comp.wait_event(ready)
+                self.forward_into(d_det, d_lg, d_rs)
+                computed = torch.cuda.Event()
+                computed.record(comp)
+                with torch.cuda.stream(copy):
+                    copy.wait_event(computed)
+                    logits_host[b0:b0 + n].copy_(d_lg, non_blocking=True)
+                    residual_host[b0:b0 + n].copy_(d_rs, non_blocking=True)
+                    done[k] = torch.cuda.Event()
+                    done[k].record(copy)
+            comp.wait_stream(copy)
+        torch.cuda.synchronize(dev)
+
     def record_step_events(self, pairs) -> None:
         """pairs: list of (start, end) torch.cuda.Event(enable_timing=True); the next forward calls record them
         around their bipartite-step launches in launch order (empty list: off)."""

@@ -89,3 +89,20 @@ def sample_torch(geo: RotatedSurface, p: float, shots: int, seed: int, device="c
         det[s0:s0 + S] = d_
         err[s0:s0 + S] = e_
     return det, err
+
+
+def sample_stream(geo: RotatedSurface, p: float, rounds: int, seed: int, q: float | None = None) -> np.ndarray:
+    """A continuous phenomenological stream of `rounds` rounds for one memory experiment -> (rounds, 2 nh) uint8:
+    per round the X checks' detectors then the Z checks' (the per-round order of RotatedSurface's check nodes)."""
+    q = p if q is None else q
+    rng = np.random.default_rng(seed)
+    nq, nh = geo.n_data_round, geo.nh
+    xf = (rng.random((rounds, nq), dtype=np.float32) < p).astype(np.float32)
+    zf = (rng.random((rounds, nq), dtype=np.float32) < p).astype(np.float32)
+    mx = (rng.random((rounds, nh), dtype=np.float32) < q).astype(np.int64)
+    mz = (rng.random((rounds, nh), dtype=np.float32) < q).astype(np.int64)
+    sz = (xf @ geo.hz.T.astype(np.float32)).astype(np.int64) & 1
+    sx = (zf @ geo.hx.T.astype(np.float32)).astype(np.int64) & 1
+    mxp = np.concatenate([np.zeros((1, nh), np.int64), mx[:-1]], 0)
+    mzp = np.concatenate([np.zeros((1, nh), np.int64), mz[:-1]], 0)
+    return np.concatenate([sx ^ mx ^ mxp, sz ^ mz ^ mzp], 1).astype(np.uint8)

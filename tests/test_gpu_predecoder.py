@@ -109,3 +109,17 @@ def test_predecoder_empty_and_single_shot():
     lg, rs = pd(torch.as_tensor(det).to(DEV))
     ref_lg, ref_rs = orc.predecoder(g, cfg, storage_params(cfg, params), det)
     check_parity(g, cfg, det, lg.cpu().numpy(), rs.cpu().numpy(), ref_lg, ref_rs)
+
+
+def test_predecoder_forward_host_matches_device_forward():
+    cfg = replace(CONFIGS["d9_bf16"], layers=2)
+    g = RotatedSurface(cfg.d, cfg.rounds)
+    params = init_params(cfg, 707)
+    det, _ = sample(g, 0.02, 1100, 708)
+    pd = PreDecoder(g, cfg, params, device=DEV, chunk_shots=256)
+    ref_lg, ref_rs = pd(torch.as_tensor(det).to(DEV))
+    det_h = torch.as_tensor(det).pin_memory()
+    lg_h = torch.empty(len(det), g.N_d, 2, dtype=torch.float32).pin_memory()
+    rs_h = torch.empty(len(det), g.N_c, dtype=torch.uint8).pin_memory()
+    pd.forward_host(det_h, lg_h, rs_h, slice_shots=256)        # 5 slices, copies overlapping compute
+    assert torch.equal(lg_h, ref_lg.cpu()) and torch.equal(rs_h, ref_rs.cpu())

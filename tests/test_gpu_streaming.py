@@ -1,0 +1,40 @@
+"""Streaming (sliding window, batch 1, CUDA-graph replay) against the batch forward on the same windows."""
+import numpy as np
+import pytest
+import torch
+from dataclasses import replace
+
+from codecoder_b200.geometry import RotatedSurface
+from codecoder_b200.modules import PreDecoder
+from codecoder_b200.params import CONFIGS, init_params
+from codecoder_b200.sampler import sample_stream
+from codecoder_b200.streaming import StreamingDecoder
+
+pytestmark = pytest.mark.gpu
+
+
+def test_streaming_matches_batch_windows():
+    cfg = replace(CONFIGS["d17_stream"], d=9, layers=3)
+    W = cfg.rounds
+    params = init_params(cfg, 31)
+    sd = StreamingDecoder(cfg.d, W, cfg, params, device="cuda")
+    g = RotatedSurface(cfg.d, W)
+    stream = sample_stream(g, 0.05, 8, 32)
+    batch = PreDecoder(g, cfg, params, device="cuda")
+    nh = g.nh
+    win = np.zeros((2, W, nh), np.uint8)
+    for t in range(len(stream)):
+        res, lg_new = sd.step(stream[t])
+        win[:, :-1] = win[:, 1:].copy()
+        win[0, -1], win[1, -1] = stream[t][:nh], stream[t][nh:]
+        ref_lg, ref_rs = batch(torch.as_tensor(win.reshape(1, -1)).cuda())
+        assert torch.equal(res.clone(), ref_rs[0].cpu())
+        assert torch.equal(lg_new.clone(), ref_lg[0, (W - 1) * g.n_data_round:].cpu())
+
+
+def test_streaming_latency_is_measured():
+    cfg = CONFIGS["d17_stream"]
+    sd = StreamingDecoder(cfg.d, cfg.rounds, cfg, init_params(cfg, 33), device="cuda")
+    lat = sd.latency(sample_stream(RotatedSurface(cfg.d, 1), cfg.p, 300, 34), warmup=50)
+    assert len(lat) == 250 and np.all(lat > 0)
+    print("d17 window-3 per-round latency us p50 %.1f p99 %.1f" % (np.percentile(lat, 50), np.percentile(lat, 99)))
