@@ -28,6 +28,12 @@ SIGNATURES = {
     "bpc_last_error": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_int]),
     "bpc_gather_mm_fwd": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32,
                                          c_vp]),
+    "bpc_gather_mm_dgrad": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_i32, c_i32, c_i32,
+                                           c_i32, c_vp]),
+    "bpc_gather_mm_wgrad": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, ctypes.c_size_t, c_i64, c_i32, c_i32, c_i32,
+                                           c_i32, c_i32, c_i32, c_vp]),
+    "bpc_gather_mm_wgrad_workspace_size": (ctypes.c_size_t, [c_i64, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32]),
+    "bpc_gather_mm_status": (ctypes.c_int, [c_vp, ctypes.POINTER(ctypes.c_int)]),
     "bpc_predecoder_create": (ctypes.c_int, [ctypes.POINTER(PredecoderConfig), c_vp, c_vp, c_vp, c_vp, c_vp,
                                              ctypes.POINTER(c_vp)]),
     "bpc_predecoder_set_weights": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),

@@ -160,6 +160,18 @@ __device__ __forceinline__ uint64_t sdesc_k_none(uint32_t saddr, uint32_t lbo, u
   d |= static_cast<uint64_t>(1) << 46;
   return d;
 }
+// Descriptor of an MN-major operand (the M or N index contiguous) in the 128-byte swizzled canonical layout, as a
+// TMA box of rows of 64 bf16 with SWIZZLE_128B writes it: each 128-byte row holds 64 consecutive M (or N) elements
+// at one K index, K rows 128 bytes apart, 8-row groups (K) `sbo` bytes apart, 64-element M/N groups `lbo` bytes apart.
+__device__ __forceinline__ uint64_t sdesc_mn_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(2) << 61;
+  return d;
+}
 // 1D bulk copy global -> this CTA's shared memory (both 16-byte aligned, size a multiple of 16), counted on an
 // mbarrier in bytes.
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
@@ -173,6 +185,10 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
   return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
          (static_cast<uint32_t>(M >> 4) << 24);
+}
+// The same with A and B MN-major (bits 15 and 16 set): A (M x K) stored M-contiguous, B (N x K) N-contiguous.
+__host__ __device__ constexpr uint32_t idesc_bf16_f32_mn(int M, int N) {
+  return idesc_bf16_f32(M, N) | (1u << 15) | (1u << 16);
 }
 
 // GELU in its tanh form (Hendrycks & Gimpel 2016): 0.5 x (1 + tanh(sqrt(2 / pi) (x + 0.044715 x^3))).

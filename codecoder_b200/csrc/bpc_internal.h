@@ -5,6 +5,7 @@
 #include <string>
 
 #include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 namespace bpc {
@@ -76,5 +77,21 @@ int gmm_tc_tile_shots(int Co);
 int gmm_fma_launch(const GmmProblem& p, bool f32, cudaStream_t stream);
 
 int num_sms();
+// Opt a kernel in to `bytes` of dynamic shared memory on the current device (once per device and kernel).
+int allow_smem(const void* fn, int bytes);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (null when the driver lacks it).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
+
+// Backward (gmm_bwd.cu).  W (Co, K, Ci) -> W' (Ci, K, Co).
+int transpose_w_launch(const void* w, void* wt, int K, int Ci, int Co, int32_t dtype, cudaStream_t stream);
+// dw (Co, K Ci) fp32 = sum over rows of gy^T gather(x); ws holds the per-split partial sums.
+int gmm_wgrad_launch(const void* x, const void* gy, const int32_t* idx, float* dw, void* ws, size_t ws_bytes,
+                     int64_t B, int32_t NS, int32_t NT, int32_t K, int32_t Ci, int32_t Co, int32_t dtype,
+                     int* status, cudaStream_t stream);
+size_t gmm_wgrad_workspace(int64_t B, int32_t NT, int32_t K, int32_t Ci, int32_t Co, int32_t dtype);
+
+// Device status word of the stand-alone op entry points (bpc_gather_mm_*), one per device.
+int* op_status_ptr();
 
 }  // namespace bpc

@@ -28,7 +28,8 @@
 #include <cstdio>
 #include <mutex>
 #include <string>
-#include <unordered_set>
+#include <set>
+#include <utility>
 
 #include <cudaTypedefs.h>
 
@@ -496,6 +497,20 @@ KernelFn select_kernel(int Co, bool blocked, int epi, bool head) {
 
 }  // namespace
 
+int allow_smem(const void* fn, int bytes) {
+  // the attribute is per device: remember (device, kernel) pairs
+  static std::mutex mu;
+  static std::set<std::pair<int, const void*>> configured;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(mu);
+  if (configured.count({dev, fn})) return 0;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return fail(4, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+  configured.insert({dev, fn});
+  return 0;
+}
+
 int num_sms() {
   static int n = 0;
   if (n == 0) {
@@ -596,17 +611,7 @@ int gmm_tc_launch(const GmmProblem& p, const GmmMaps& maps, int* status, uint64_
   const bool head = p.head.head_w != nullptr;
   KernelFn fn = select_kernel(p.Co, p.blocked, p.epi, head);
   if (!fn) return fail(2, "unsupported C_out / layout / epilogue combination for the tcgen05 path");
-  static std::mutex mu;
-  static std::unordered_set<const void*> configured;
-  {
-    std::lock_guard<std::mutex> lk(mu);
-    if (!configured.count(reinterpret_cast<const void*>(fn))) {
-      cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
-      if (e != cudaSuccess) return fail(4, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
-      configured.insert(reinterpret_cast<const void*>(fn));
-    }
-  }
+  if (int e = allow_smem(reinterpret_cast<const void*>(fn), kSmemLimit)) return e;
   const int64_t grid = std::min<int64_t>(a.num_tiles, num_sms());
   void* args[] = {const_cast<CUtensorMap*>(&maps.x), const_cast<CUtensorMap*>(&maps.w), &a};
   cudaError_t le = cudaLaunchKernel(reinterpret_cast<const void*>(fn), dim3(static_cast<unsigned>(grid)),
@@ -616,5 +621,7 @@ int gmm_tc_launch(const GmmProblem& p, const GmmMaps& maps, int* status, uint64_
 }
 
 int gmm_tc_tile_shots(int Co) { return kBlockM * mt_for(Co); }
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() { return get_encode(); }
 
 }  // namespace bpc

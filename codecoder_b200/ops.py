@@ -2,10 +2,13 @@
 
 Drop-ins (training/bb/ising_compare/bb/cascade_net.py and cascade_triton.py):
   gather_mm(x, w, idx, inv)                  cascade_net.py:174-175
-  GatherMMB200.apply(x, w, idx, inv)         the autograd Function, as GatherMMTriton (cascade_triton.py:161-171)
-  torch.ops.cascade.gmm(a, idx, w, transposed)   cascade_triton.py:139-148 (transposed=False)
+  GatherMMB200.apply(x, w, idx, inv)         the autograd Function, as GatherMMTriton (cascade_triton.py:161-186)
+  torch.ops.cascade.gmm(a, idx, w, transposed)   cascade_triton.py:100-117,139-148
+  torch.ops.cascade.gmm_wgrad(x, gy, idx)        cascade_triton.py:120-136,151-158 (fp32 result)
 Everything runs on the GPU: a CPU tensor raises, there is no CPU path.  bf16 inputs run on the tcgen05 tensor
-cores (C_in >= 64, C_out % 32 == 0, C_out <= 256) or the CUDA-core kernel; fp32 inputs on the CUDA-core kernel.
+cores (forward: C_in >= 64, C_out % 32 == 0, C_out <= 256; weight gradient: C_in % 16 == 0, C_out % 8 == 0) or
+the CUDA-core kernels; fp32 inputs on the CUDA-core kernels.  The weight gradient is deterministic (fixed split of
+the rows, partial sums added in a fixed order), as the reference's is.
 """
 from __future__ import annotations
 
@@ -20,32 +23,83 @@ def _stream_ptr(device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+def _check_cuda(*ts):
+    if not all(t.is_cuda for t in ts):
+        raise RuntimeError("codecoder_b200 ops run on CUDA tensors only (no CPU path)")
+
+
 def gmm(a: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, transposed: bool = False) -> torch.Tensor:
-    """a (B, NS, C_in), idx (NT, K) int32, w (C_out, K C_in) -> y (B, NT, C_out), y[b, n] = sum_r a[b, idx[n, r]] W_r^T
-    (idx outside [0, NS) reads zeros).  Same contract as cascade_triton.gmm with transposed=False."""
-    if transposed:
-        raise NotImplementedError("the input-gradient form (transposed=True) of cascade::gmm is not built yet")
-    if not (a.is_cuda and idx.is_cuda and w.is_cuda):
-        raise RuntimeError("codecoder_b200.gmm runs on CUDA tensors only (no CPU path)")
+    """Same contract as cascade_triton.gmm (cascade_triton.py:100-117).
+    transposed=False: a (B, NS, C_in), idx (NT, K), w (C_out, K C_in) -> (B, NT, C_out),
+                      y[b, n] = sum_r a[b, idx[n, r]] W_r^T (idx outside [0, NS) reads zeros).
+    transposed=True:  a = gy (B, NT, C_out), idx = the target table tgt (NS, K) -> gx (B, NS, C_in),
+                      gx[b, s] = sum_r gy[b, tgt[s, r]] W_r (tgt outside [0, NT) = none)."""
+    _check_cuda(a, idx, w)
     if a.dtype not in _DTYPES or w.dtype != a.dtype:
         raise TypeError(f"gmm needs bf16 or fp32 a and w of the same dtype, got {a.dtype} / {w.dtype}")
     if a.dim() != 3 or idx.dim() != 2 or w.dim() != 2:
-        raise ValueError("gmm expects a (B, NS, C), idx (NT, K), w (C_out, K C_in)")
-    B, NS, Ci = a.shape
-    NT, K = idx.shape
+        raise ValueError("gmm expects a (B, N, C), idx (N_out, K), w (C_out, K C_in)")
+    B, NA, CA = a.shape
+    NY, K = idx.shape
     Co, KC = w.shape
-    if KC != K * Ci:
-        raise ValueError(f"w has {KC} columns, expected K * C_in = {K * Ci}")
+    if KC % K:
+        raise ValueError(f"w has {KC} columns, not a multiple of K = {K}")
+    Ci = KC // K
+    if CA != (Co if transposed else Ci):
+        raise ValueError(f"a has {CA} channels, expected {Co if transposed else Ci}")
     a = a.contiguous()
     w = w.contiguous()
     idx = idx.to(torch.int32).contiguous()
-    y = torch.empty(B, NT, Co, device=a.device, dtype=a.dtype)
-    if B == 0 or NT == 0:
+    CY = Ci if transposed else Co
+    y = torch.empty(B, NY, CY, device=a.device, dtype=a.dtype)
+    if B == 0 or NY == 0:
         return y
-    rc = _lib.lib().bpc_gather_mm_fwd(a.data_ptr(), w.data_ptr(), idx.data_ptr(), y.data_ptr(), B, NS, NT, K, Ci,
-                                      Co, _DTYPES[a.dtype], _stream_ptr(a.device))
-    _lib.check(rc, "bpc_gather_mm_fwd")
+    L = _lib.lib()
+    if transposed:
+        w_t = torch.empty_like(w)
+        rc = L.bpc_gather_mm_dgrad(a.data_ptr(), w.data_ptr(), idx.data_ptr(), y.data_ptr(), w_t.data_ptr(), B, NA,
+                                   NY, K, Ci, Co, _DTYPES[a.dtype], _stream_ptr(a.device))
+        _lib.check(rc, "bpc_gather_mm_dgrad")
+    else:
+        rc = L.bpc_gather_mm_fwd(a.data_ptr(), w.data_ptr(), idx.data_ptr(), y.data_ptr(), B, NA, NY, K, Ci, Co,
+                                 _DTYPES[a.dtype], _stream_ptr(a.device))
+        _lib.check(rc, "bpc_gather_mm_fwd")
     return y
+
+
+def gmm_wgrad(x: torch.Tensor, gy: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
+    """x (B, NS, C_in), gy (B, NT, C_out), idx (NT, K) -> dW (C_out, K C_in) fp32,
+    dW[o, r C_in + i] = sum_{b, n} gy[b, n, o] x[b, idx[n, r], i] (cascade_triton.py:120-136)."""
+    _check_cuda(x, gy, idx)
+    if x.dtype not in _DTYPES or gy.dtype != x.dtype:
+        raise TypeError(f"gmm_wgrad needs bf16 or fp32 x and gy of the same dtype, got {x.dtype} / {gy.dtype}")
+    B, NS, Ci = x.shape
+    B2, NT, Co = gy.shape
+    NT2, K = idx.shape
+    if B2 != B or NT2 != NT:
+        raise ValueError("gmm_wgrad: x, gy and idx disagree on B or NT")
+    x = x.contiguous()
+    gy = gy.contiguous()
+    idx = idx.to(torch.int32).contiguous()
+    dw = torch.empty(Co, K * Ci, device=x.device, dtype=torch.float32)
+    L = _lib.lib()
+    dt = _DTYPES[x.dtype]
+    nbytes = int(L.bpc_gather_mm_wgrad_workspace_size(B, NS, NT, K, Ci, Co, dt))
+    ws = torch.empty(max(nbytes, 16), device=x.device, dtype=torch.uint8)
+    rc = L.bpc_gather_mm_wgrad(x.data_ptr(), gy.data_ptr(), idx.data_ptr(), dw.data_ptr(), ws.data_ptr(), ws.numel(),
+                               B, NS, NT, K, Ci, Co, dt, _stream_ptr(x.device))
+    _lib.check(rc, "bpc_gather_mm_wgrad")
+    return dw
+
+
+def op_status(device=None) -> int:
+    """Synchronise the current stream and read (and clear) the gather_mm kernels' watchdog word; raises if set."""
+    import ctypes
+    s = ctypes.c_int(0)
+    with torch.cuda.device(device if device is not None else torch.cuda.current_device()):
+        rc = _lib.lib().bpc_gather_mm_status(_stream_ptr(torch.cuda.current_device()), ctypes.byref(s))
+    _lib.check(rc, "bpc_gather_mm_status")
+    return s.value
 
 
 @torch.library.custom_op("cascade::gmm", mutates_args=())
@@ -60,19 +114,48 @@ def _(a, idx, w, transposed):
     return a.new_empty(a.shape[0], idx.shape[0], w.shape[1] // K if transposed else w.shape[0])
 
 
+@torch.library.custom_op("cascade::gmm_wgrad", mutates_args=())
+def gmm_wgrad_op(x: torch.Tensor, gy: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
+    """gmm_wgrad as an opaque operator (cascade_triton.py:151-153)."""
+    return gmm_wgrad(x, gy, idx)
+
+
+@gmm_wgrad_op.register_fake
+def _(x, gy, idx):
+    return x.new_empty(gy.shape[2], idx.shape[1] * x.shape[2], dtype=torch.float32)
+
+
+def target_table(inv: torch.Tensor, NT: int, K: int) -> torch.Tensor:
+    """Inverse table (NS, K), value n K + r or NT K = none -> int32 target table, NT = none
+    (cascade_triton.py:182)."""
+    return torch.where(inv < NT * K, inv // K, torch.full_like(inv, NT)).to(torch.int32)
+
+
 class GatherMMB200(torch.autograd.Function):
     """Drop-in for cascade_net._GatherMM / cascade_triton.GatherMMTriton (same signature; idx and the inverse table
-    as int64 on the device).  Forward only: the backward kernels are not built yet and raise."""
+    as int64 on the device).  Forward and backward on the B200 kernels (cascade_triton.py:161-186)."""
 
     @staticmethod
     @torch.amp.custom_fwd(device_type="cuda", cast_inputs=torch.bfloat16)
     def forward(ctx, x, w, idx, inv):
-        return gmm_op(x.contiguous(), idx.to(torch.int32), w.contiguous(), False)
+        x = x.contiguous()
+        w = w.contiguous()
+        idx32 = idx.to(torch.int32)
+        ctx.save_for_backward(x, w, idx32, inv)
+        return gmm_op(x, idx32, w, False)
 
     @staticmethod
     @torch.amp.custom_bwd(device_type="cuda")
     def backward(ctx, gy):
-        raise NotImplementedError("backward of the B200 gather_mm (dgrad / wgrad kernels) is not built yet")
+        x, w, idx32, inv = ctx.saved_tensors
+        gy = gy.contiguous().to(x.dtype)
+        NT, K = idx32.shape
+        gx = gw = None
+        if ctx.needs_input_grad[0]:
+            gx = gmm_op(gy, target_table(inv, NT, K), w, True)
+        if ctx.needs_input_grad[1]:
+            gw = gmm_wgrad_op(x, gy, idx32).to(w.dtype)
+        return gx, gw, None, None
 
 
 def gather_mm(x, w, idx, inv):

@@ -1,0 +1,132 @@
+"""Training step of the rotated-surface pre-decoder on the B200 gather_mm op (forward and backward kernels).
+
+PreDecoderNet is the network of params.py as an nn.Module over (B, N, C) row-layout features:
+  h_c = E[2 type + det];  per layer  h_d (+)= GELU(gather_mm(h_c, Wc2d[l], c2d, inv_c2d))
+                                     h_c += GELU(cat_type gather_mm(h_d, Wd2c[l, type], d2c[type], inv_d2c[type]))
+  logits = h_d Wh^T + bh  (B, N_d, 2): predicted X / Z flip of every data node
+with gather_mm the autograd Function of ops.py (cascade_net.py:140-175 / cascade_triton.py:161-186): its forward,
+input gradient and weight gradient all run on the tcgen05 kernels under bf16 autocast.
+
+Trainer.step is the reference's optimisation step (training/bb/ising_compare/bb/cascade_train.py:292-320), with the
+optimiser of the training workload (Adam) in place of the reference's Muon / Lion pair: bf16 autocast forward,
+binary cross-entropy with logits against the sampled data-qubit error labels, backward, gradient-norm clipping,
+optimiser step.  With world > 1 the model is wrapped in DistributedDataParallel(broadcast_buffers=False) (NCCL
+all-reduce of the gradients, cascade_train.py:243-245), and Trainer.agree takes the MAX of the per-rank
+stop / non-finite flags so that every rank takes the same decision (cascade_train.py:387-391).
+"""
+from __future__ import annotations
+
+import math
+from contextlib import nullcontext
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from .ops import gather_mm
+from .params import N_TOKENS
+
+
+class PreDecoderNet(nn.Module):
+    """geo: geometry.RotatedSurface; cfg: params.PreDecoderConfig; params: optional init_params-style dict (fp32
+    numpy) to start from, else a seeded init with the same bounds.  `gmm` is the bipartite-conv op with the
+    reference's signature gmm(x, w, idx, inv) (default: the B200 op)."""
+
+    def __init__(self, geo, cfg, params: dict | None = None, gmm=gather_mm, seed: int = 0):
+        super().__init__()
+        if cfg.K != geo.K or cfg.d != geo.d or cfg.rounds != geo.R:
+            raise ValueError("configuration and geometry disagree")
+        self.cfg, self.gmm = cfg, gmm
+        C, K, L = cfg.channels, cfg.K, cfg.layers
+        if params is None:
+            from .params import init_params
+            params = init_params(cfg, seed)
+        self.embed = nn.Parameter(torch.as_tensor(np.asarray(params["embed"], np.float32)).clone())
+        self.w_c2d = nn.ParameterList([nn.Parameter(torch.as_tensor(params["w_c2d"][l][0]).clone()) for l in range(L)])
+        self.w_d2c = nn.ParameterList([nn.Parameter(torch.as_tensor(params["w_d2c"][l][c]).clone())
+                                       for l in range(L) for c in range(2)])
+        self.head_w = nn.Parameter(torch.as_tensor(params["head_w"]).clone())
+        self.head_b = nn.Parameter(torch.as_tensor(params["head_b"]).clone())
+        assert self.embed.shape == (N_TOKENS, C) and self.w_c2d[0].shape == (C, K * C)
+        buf = {"check_type": geo.check_type.astype(np.int64), "c2d": geo.c2d[0],
+               "inv_c2d": geo.inverse(geo.c2d[0], geo.N_c)}
+        for c in range(2):
+            buf[f"d2c{c}"] = geo.d2c[c]
+            buf[f"inv_d2c{c}"] = geo.inverse(geo.d2c[c], geo.N_d)
+        for k, v in buf.items():
+            self.register_buffer(k, torch.as_tensor(np.asarray(v, np.int64)), persistent=False)
+        # the logits read h_d after the last check -> data step: the last data -> check step does not reach the
+        # loss, so its weights take no gradient (kept for the inference weight set)
+        for c in range(2):
+            self.w_d2c[2 * (L - 1) + c].requires_grad_(False)
+
+    def forward(self, det: torch.Tensor) -> torch.Tensor:
+        """det (B, N_c) uint8 -> logits (B, N_d, 2) (bf16 under autocast)."""
+        tok = 2 * self.check_type + det.long()
+        hc = F.embedding(tok, self.embed)
+        hd = None
+        for l in range(self.cfg.layers):
+            u = F.gelu(self.gmm(hc, self.w_c2d[l], self.c2d, self.inv_c2d), approximate="tanh")
+            hd = u if hd is None else hd + u
+            if l == self.cfg.layers - 1:
+                break
+            a = torch.cat([self.gmm(hd, self.w_d2c[2 * l + c], getattr(self, f"d2c{c}"), getattr(self, f"inv_d2c{c}"))
+                           for c in range(2)], 1)
+            hc = hc + F.gelu(a, approximate="tanh")
+        return F.linear(hd, self.head_w, self.head_b)
+
+
+class Trainer:
+    """One process per GPU.  model: PreDecoderNet on `device`; with an initialised process group of world > 1 the
+    model is wrapped in DDP (NCCL on GPUs, gloo on CPU)."""
+
+    def __init__(self, model: PreDecoderNet, lr: float = 1e-3, clip: float = 1.0, autocast: bool = True):
+        import torch.distributed as dist
+        self.model = model
+        self.device = next(model.parameters()).device
+        self.world = dist.get_world_size() if dist.is_available() and dist.is_initialized() else 1
+        self.net = model
+        if self.world > 1:
+            from torch.nn.parallel import DistributedDataParallel as DDP
+            ids = [self.device.index] if self.device.type == "cuda" else None
+            self.net = DDP(model, device_ids=ids, broadcast_buffers=False)
+        self.params = [p for p in model.parameters() if p.requires_grad]
+        self.opt = torch.optim.Adam(self.params, lr=lr)
+        self.clip = clip
+        self.autocast = autocast and self.device.type == "cuda"
+
+    def step(self, det: torch.Tensor, err: torch.Tensor) -> torch.Tensor:
+        """det (B, N_c) uint8, err (B, N_d, 2) 0/1 labels -> the batch loss (a device scalar, not synchronised)."""
+        ctx = torch.autocast("cuda", dtype=torch.bfloat16) if self.autocast else nullcontext()
+        with ctx:
+            z = self.net(det)
+        loss = F.binary_cross_entropy_with_logits(z.float(), err.float())
+        loss.backward()
+        torch.nn.utils.clip_grad_norm_(self.params, self.clip)
+        self.opt.step()
+        self.opt.zero_grad(set_to_none=True)
+        return loss.detach()
+
+    def agree(self, stop: bool, bad: bool) -> tuple[bool, bool]:
+        """Every rank takes the same decision: MAX over ranks of the stop / non-finite flags."""
+        if self.world == 1:
+            return stop, bad
+        import torch.distributed as dist
+        fl = torch.tensor([float(stop), float(bad)], device=self.device)
+        dist.all_reduce(fl, op=dist.ReduceOp.MAX)
+        return bool(fl[0].item()), bool(fl[1].item())
+
+
+def train_flops_per_shot(geo, cfg) -> float:
+    """Algorithmic FLOPs of one training shot: forward + input gradient + weight gradient of every bipartite step
+    that reaches the loss (3 x 2 K C^2 per target node and step, all K slots counted; L check -> data steps and
+    L - 1 data -> check steps) plus the head."""
+    C, K, L = cfg.channels, cfg.K, cfg.layers
+    return 3.0 * 2 * K * C * C * (L * geo.N_d + (L - 1) * geo.N_c) + 3.0 * 2 * 2 * C * geo.N_d
+
+
+def bce_at_init(err_rate: float) -> float:
+    """Loss of a predictor that outputs the label frequency (a reference point for the loss curve)."""
+    p = min(max(err_rate, 1e-12), 1 - 1e-12)
+    return -(p * math.log(p) + (1 - p) * math.log(1 - p))

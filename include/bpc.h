@@ -51,6 +51,35 @@ BPC_API int bpc_last_error(char* buf, int len);
 BPC_API int bpc_gather_mm_fwd(const void* x, const void* w, const int32_t* idx, void* y, int64_t B, int32_t NS, int32_t NT,
                       int32_t K, int32_t Ci, int32_t Co, int32_t dtype, bpc_stream_t stream);
 
+/* Input gradient of bpc_gather_mm_fwd through the target table:
+ *   gx[b, s, :] = sum_r gy[b, tgt[s, r], :] W_r,   tgt (NS, K) int32, NT (or any value outside [0, NT)) = none
+ * gy (B, NT, Co), gx (B, NS, Ci), W (Co, K*Ci) as in the forward.  tgt[s, r] is the target that reads source s
+ * through relation r, the reference's where(inv < NT*K, inv // K, NT).  w_t is caller scratch of K*Ci*Co elements
+ * of dtype that receives W rearranged as (Ci, K*Co), so the forward kernels compute the sum (tensor cores when
+ * Co >= 64, Ci % 32 == 0, Ci <= 256, K <= 16 and bf16).
+ * Replaces: cascade_triton.py:100-117 (gmm with transposed=True), cascade_net.py:155-171 (_GatherMM.backward, gx). */
+BPC_API int bpc_gather_mm_dgrad(const void* gy, const void* w, const int32_t* tgt, void* gx, void* w_t, int64_t B,
+                                int32_t NT, int32_t NS, int32_t K, int32_t Ci, int32_t Co, int32_t dtype,
+                                bpc_stream_t stream);
+
+/* Weight gradient of bpc_gather_mm_fwd, fp32 and deterministic (fixed split of the rows, fixed-order sum):
+ *   dw[o, r*Ci + i] = sum_{b, n} gy[b, n, o] x[b, idx[n, r], i]      (pads contribute nothing)
+ * x (B, NS, Ci), gy (B, NT, Co), idx (NT, K) int32, dw (Co, K*Ci) fp32.  workspace: caller scratch of at least
+ * bpc_gather_mm_wgrad_workspace_size() bytes (per-split fp32 partial sums), 16-byte aligned.
+ * Replaces: cascade_triton.py:64-93,120-136,151-158 (_gmm_wgrad, gmm_wgrad, the op cascade::gmm_wgrad). */
+BPC_API int bpc_gather_mm_wgrad(const void* x, const void* gy, const int32_t* idx, float* dw, void* workspace,
+                                size_t workspace_bytes, int64_t B, int32_t NS, int32_t NT, int32_t K, int32_t Ci,
+                                int32_t Co, int32_t dtype, bpc_stream_t stream);
+
+/* Workspace bytes bpc_gather_mm_wgrad needs for these shapes on the current device. */
+BPC_API size_t bpc_gather_mm_wgrad_workspace_size(int64_t B, int32_t NS, int32_t NT, int32_t K, int32_t Ci, int32_t Co,
+                                                  int32_t dtype);
+
+/* Synchronises `stream`, reads and clears the current device's watchdog status word of the three gather_mm entry
+ * points (0 = every bounded wait completed).  Returns BPC_ERR_DEVICE when a tensor-core kernel gave up a wait, in
+ * which case that launch's output is not valid. */
+BPC_API int bpc_gather_mm_status(bpc_stream_t stream, int* status);
+
 /* ------------------------------------------------------------------------------------------------------------
  * Pre-decoder: detectors (B, N_c) uint8 -> per-data-node X/Z logits (B, N_d, 2) fp32 and the residual syndrome
  * (B, N_c) uint8, through `layers` x [check -> data, data -> check] bipartite convolutions of width `channels`.

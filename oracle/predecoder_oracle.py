@@ -8,6 +8,10 @@ What it restates:
                  sources with a zero row, index_select by the (NT, K) table, one matmul with W^T (C_out, K C_in).
                  gather_mm_loop is the literal per-relation sum y = sum_r x[idx[:, r]] W_r^T of the Triton kernel's
                  docstring (cascade_triton.py:5,40) for small cases.
+  gather_mm_dgrad / gather_mm_wgrad
+                 the reference's _GatherMM.backward (cascade_net.py:155-171): the input gradient as the per-relation
+                 sum gx[b, s] = sum_r gy[b, tgt[s, r]] W_r over the target table of the Triton backward
+                 (cascade_triton.py:173-186), and the weight gradient gy^T gather(x) (cascade_triton.py:64-93).
   bipartite_conv BipartiteConv.forward (cascade_net.py:228-233): check -> data for every data type, concatenated,
                  then data -> check for every check type.
   predecoder     the rotated-surface pre-decoder of codecoder_b200.params (embed, L x [c2d, GELU, residual;
@@ -48,6 +52,42 @@ def gather_mm_loop(x: np.ndarray, w: np.ndarray, idx: np.ndarray) -> np.ndarray:
         ok = src < N
         y[:, ok] += x64[:, src[ok]] @ w64[:, r].T
     return y
+
+
+def target_table(inv, NT: int, K: int) -> np.ndarray:
+    """Inverse table (NS, K) of flat positions n K + r (NT K = none) -> target table, NT = none
+    (cascade_triton.py:182)."""
+    inv = np.asarray(inv, np.int64)
+    return np.where(inv < NT * K, inv // K, NT)
+
+
+def gather_mm_dgrad(gy: np.ndarray, w: np.ndarray, tgt: np.ndarray, Ci: int) -> np.ndarray:
+    """gx (B, NS, Ci) float64 = sum_r gy[b, tgt[s, r]] W_r, tgt outside [0, NT) = none."""
+    B, NT, Co = gy.shape
+    NS, K = tgt.shape
+    gy64 = np.asarray(gy, np.float64)
+    w64 = np.asarray(w, np.float64).reshape(Co, K, Ci)
+    gx = np.zeros((B, NS, Ci))
+    for r in range(K):
+        t = tgt[:, r]
+        ok = (t >= 0) & (t < NT)
+        gx[:, ok] += gy64[:, t[ok]] @ w64[:, r]
+    return gx
+
+
+def gather_mm_wgrad(x: np.ndarray, gy: np.ndarray, idx: np.ndarray) -> np.ndarray:
+    """dW (Co, K Ci) float64 = sum_{b, n} gy[b, n]^T x[b, idx[n, r]] per relation r (pads contribute nothing)."""
+    B, NS, Ci = x.shape
+    _, NT, Co = gy.shape
+    K = idx.shape[1]
+    x64 = np.asarray(x, np.float64)
+    gy64 = np.asarray(gy, np.float64)
+    dw = np.zeros((Co, K, Ci))
+    for r in range(K):
+        src = idx[:, r]
+        ok = (src >= 0) & (src < NS)
+        dw[:, r] = np.tensordot(gy64[:, ok], x64[:, src[ok]], axes=([0, 1], [0, 1]))
+    return dw.reshape(Co, K * Ci)
 
 
 def bipartite_conv(x, w_c2d, w_d2c, c2d, d2c):

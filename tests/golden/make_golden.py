@@ -11,6 +11,10 @@ It imports the reference's bb.cascade_net (training/bb/ising_compare/bb/cascade_
                          (several channel widths, including C_in != C_out)
   predecoder_<cfg>.npz   the pre-decoder composed from the reference's gather_mm on seeded shots: det, logits,
                          residual (weights regenerate from the stored seed with codecoder_b200.params.init_params)
+  gather_mm_bwd.npz      input and weight gradients from the reference's _GatherMM.backward (autograd through
+                         cn.gather_mm, fp32, CPU) for seeded upstream gradients: rotated-surface steps at several
+                         widths and BipartiteConv(128, Geometry('bb72')) with the C14 relation matrices (its
+                         input gradient and two of its four weight gradients)
 The fixtures are small; the device never reads the reference tree.
 """
 import hashlib
@@ -152,8 +156,52 @@ def make_predecoder():
         print("predecoder", name, det.shape, logits.shape, float(np.abs(logits).mean()))
 
 
+def make_backward():
+    out = {}
+    rng = np.random.default_rng(1403)
+    cases = [("d5_c64_c2d", 5, 64, 64, 3, "c2d"), ("d3_c96_d2c", 3, 96, 96, 4, "d2c"),
+             ("d3_ci64_co128_c2d", 3, 64, 128, 3, "c2d"), ("d5_c32_c2d", 5, 32, 32, 4, "c2d")]
+    for name, d, ci, co, B, step in cases:
+        geo = RotatedSurface(d, d)
+        idx, ns = (geo.c2d[0], geo.N_c) if step == "c2d" else (geo.d2c_all, geo.N_d)
+        inv = geo.inverse(idx, ns)
+        x = torch.as_tensor(round_bf16(rng.standard_normal((B, ns, ci)).astype(np.float32))).requires_grad_()
+        w = torch.as_tensor(round_bf16((rng.standard_normal((co, geo.K * ci)) / np.sqrt(geo.K * ci))
+                                       .astype(np.float32))).requires_grad_()
+        gy = round_bf16(rng.standard_normal((B, idx.shape[0], co)).astype(np.float32))
+        y = cn.gather_mm(x, w, torch.as_tensor(idx), torch.as_tensor(inv))
+        y.backward(torch.as_tensor(gy))
+        out[name + "_x"] = bf16_bits(x.detach().numpy())
+        out[name + "_w"] = bf16_bits(w.detach().numpy())
+        out[name + "_gy"] = bf16_bits(gy)
+        out[name + "_idx"] = idx.astype(np.int32)
+        out[name + "_inv"] = inv.astype(np.int64)
+        out[name + "_gx"] = x.grad.numpy()
+        out[name + "_gw"] = w.grad.numpy()
+    # the reference module with the C14 relation matrices on Geometry('bb72'), one shot
+    geo = cn.Geometry("bb72")
+    z = np.load(os.path.join(HERE, "bb72_c14_conv.npz"))
+    C = int(z["C"])
+    conv = cn.BipartiteConv(C, geo, impl="torch")
+    with torch.no_grad():
+        for k in range(2):
+            conv.w_c2d[k].copy_(torch.as_tensor((z[f"w_c2d_{k}_bf16"].astype(np.uint32) << 16).view(np.float32)))
+            conv.w_d2c[k].copy_(torch.as_tensor((z[f"w_d2c_{k}_bf16"].astype(np.uint32) << 16).view(np.float32)))
+    x = torch.as_tensor(round_bf16(rng.standard_normal((1, geo.N, C)).astype(np.float32))).requires_grad_()
+    gy = round_bf16(rng.standard_normal((1, geo.N, C)).astype(np.float32))
+    conv(x).backward(torch.as_tensor(gy))
+    out["bb72_x"] = bf16_bits(x.detach().numpy())
+    out["bb72_gy"] = bf16_bits(gy)
+    out["bb72_gx"] = x.grad.numpy()
+    out["bb72_gw_c2d0"] = conv.w_c2d[0].grad.numpy()     # two of the four weight gradients keep the file small
+    out["bb72_gw_d2c1"] = conv.w_d2c[1].grad.numpy()
+    np.savez_compressed(os.path.join(HERE, "gather_mm_bwd.npz"), **out)
+    print("gather_mm_bwd", len(cases), "op cases + bb72 module")
+
+
 if __name__ == "__main__":
     torch.manual_seed(0)
     make_bb72()
     make_surface_gmm()
     make_predecoder()
+    make_backward()

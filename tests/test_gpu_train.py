@@ -1,0 +1,73 @@
+"""The training step on the GPU: PreDecoderNet on the B200 op against the same network on the CPU oracle's
+gather_mm (float64 autograd), and a short training run that lowers the loss.
+
+Tolerances: fp32 network (CUDA-core kernels) 1e-4 relative to max |ref|; bf16 autocast (tensor cores) 5e-2 on the
+gradients (every stored activation and gradient is rounded to bf16 along the way)."""
+from dataclasses import replace
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from codecoder_b200.geometry import RotatedSurface
+from codecoder_b200.params import CONFIGS, init_params
+from codecoder_b200.sampler import sample, sample_torch
+from codecoder_b200.train import PreDecoderNet, Trainer
+from oracle import predecoder_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+
+def oracle_gmm(x, w, idx, inv):
+    return orc.gather_mm(x, w, idx.cpu())
+
+
+def rel(a, b):
+    a, b = a.detach().double().cpu(), b.detach().double().cpu()
+    return float((a - b).abs().max() / b.abs().max().clamp_min(1e-30))
+
+
+def grads(cfg, seed, B, autocast):
+    g = RotatedSurface(cfg.d, cfg.rounds)
+    params = init_params(cfg, seed)
+    det, err = sample(g, 0.03, B, seed + 1)
+    dev_net = PreDecoderNet(g, cfg, params).cuda()
+    ref_net = PreDecoderNet(g, cfg, params, gmm=oracle_gmm).double()
+    with torch.autocast("cuda", dtype=torch.bfloat16, enabled=autocast):
+        z = dev_net(torch.as_tensor(det).cuda())
+    F.binary_cross_entropy_with_logits(z.float(), torch.as_tensor(err).cuda().float()).backward()
+    zr = ref_net(torch.as_tensor(det))
+    F.binary_cross_entropy_with_logits(zr, torch.as_tensor(err).double()).backward()
+    return z, zr, dict(dev_net.named_parameters()), dict(ref_net.named_parameters())
+
+
+def test_train_gradients_fp32_match_oracle():
+    cfg = replace(CONFIGS["d5_fp32"], d=3, rounds=3, layers=2)
+    z, zr, pd, pr = grads(cfg, 31, 24, autocast=False)
+    assert rel(z, zr) < 1e-4
+    for k in pr:
+        if pr[k].requires_grad:
+            assert rel(pd[k].grad, pr[k].grad) < 1e-4, k
+
+
+def test_train_gradients_bf16_match_oracle():
+    cfg = replace(CONFIGS["d11_train"], d=5, rounds=5, layers=2)          # C = 96: tensor-core kernels
+    z, zr, pd, pr = grads(cfg, 32, 40, autocast=True)
+    assert rel(z, zr) < 3e-2
+    for k in pr:
+        if pr[k].requires_grad:
+            assert rel(pd[k].grad, pr[k].grad) < 5e-2, (k, rel(pd[k].grad, pr[k].grad))
+
+
+def test_training_lowers_the_loss():
+    cfg = replace(CONFIGS["d11_train"], d=5, rounds=5, layers=3, channels=64)
+    g = RotatedSurface(cfg.d, cfg.rounds)
+    torch.manual_seed(0)
+    tr = Trainer(PreDecoderNet(g, cfg, init_params(cfg, 41)).cuda(), lr=1e-3)
+    losses = []
+    for step in range(60):
+        det, err = sample_torch(g, 0.01, 1024, 1000 + step, device="cuda")
+        losses.append(float(tr.step(det, err)))
+    assert np.isfinite(losses).all()
+    assert np.mean(losses[-10:]) < 0.7 * np.mean(losses[:5]), losses

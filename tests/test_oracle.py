@@ -78,3 +78,38 @@ def test_band_helpers():
     ref = np.array([[[1.0, -2.0], [1e-6, 0.5]]])
     assert orc.band_mask(ref, 1e-3).sum() == 1
     assert orc.logit_error(ref, ref) == 0.0
+
+
+def _rel(a, b):
+    return float(np.max(np.abs(a - b)) / max(np.max(np.abs(b)), 1e-30))
+
+
+@pytest.fixture(scope="module")
+def bwd(golden_dir):
+    return dict(np.load(os.path.join(golden_dir, "gather_mm_bwd.npz")))
+
+
+def test_oracle_backward_matches_reference_op(bwd):
+    names = sorted({k.rsplit("_", 1)[0] for k in bwd if not k.startswith("bb72")})
+    assert len(names) == 4
+    for nm in names:
+        x = bf16_to_f32(bwd[nm + "_x"])
+        w = bf16_to_f32(bwd[nm + "_w"])
+        gy = bf16_to_f32(bwd[nm + "_gy"])
+        idx = bwd[nm + "_idx"].astype(np.int64)
+        NT, K = idx.shape
+        Ci = x.shape[2]
+        tgt = orc.target_table(bwd[nm + "_inv"], NT, K)
+        assert _rel(orc.gather_mm_dgrad(gy, w, tgt, Ci), bwd[nm + "_gx"]) < 1e-5, nm
+        assert _rel(orc.gather_mm_wgrad(x, gy, idx), bwd[nm + "_gw"]) < 1e-5, nm
+
+
+def test_oracle_backward_matches_reference_module(bb72, bwd):
+    w = [torch.as_tensor(bf16_to_f32(bb72[k + "_bf16"]), dtype=torch.float64).requires_grad_()
+         for k in ("w_c2d_0", "w_c2d_1", "w_d2c_0", "w_d2c_1")]
+    x = torch.as_tensor(bf16_to_f32(bwd["bb72_x"]), dtype=torch.float64).requires_grad_()
+    y = orc.bipartite_conv(x, w[:2], w[2:], [bb72["c2d0"], bb72["c2d1"]], [bb72["d2c0"], bb72["d2c1"]])
+    y.backward(torch.as_tensor(bf16_to_f32(bwd["bb72_gy"]), dtype=torch.float64))
+    assert _rel(x.grad.numpy(), bwd["bb72_gx"]) < 1e-5
+    assert _rel(w[0].grad.numpy(), bwd["bb72_gw_c2d0"]) < 1e-5
+    assert _rel(w[3].grad.numpy(), bwd["bb72_gw_d2c1"]) < 1e-5
