@@ -48,6 +48,9 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-stream", action="store_true")
     ap.add_argument("--stream-rounds", type=int, default=20000)
+    ap.add_argument("--no-train", action="store_true")
+    ap.add_argument("--train-steps", type=int, default=6)
+    ap.add_argument("--train-batch", type=int, default=8192, help="shots per GPU per training step")
     return ap.parse_args()
 
 
@@ -351,6 +354,45 @@ def main():
                   "clock": "host wall clock from handing a round over to its results in pinned host memory",
                   "flop_per_round": sflop, "roofline_us_all_sms": sflop / (pk["bf16_tflops"] * 1e12) * 1e6}
 
+    train = None
+    if not args.no_train:
+        # d = 11 training step (bf16 autocast, BCE, Adam 1e-3) with DDP over NCCL at world > 1: fixed shots per GPU
+        del det, logits, resid, pd
+        if not args.no_e2e:
+            del det_h, lg_h, rs_h
+        torch.cuda.empty_cache()
+        from codecoder_b200.train import PreDecoderNet, Trainer, train_flops_per_shot
+        tcfg = CONFIGS["d11_train"]
+        tg = RotatedSurface(tcfg.d, tcfg.rounds)
+        torch.manual_seed(SEED)
+        trn = Trainer(PreDecoderNet(tg, tcfg, init_params(tcfg, SEED)).to(dev), lr=1e-3)
+        batches = [sample_torch(tg, tcfg.p, args.train_batch, SEED + 1000 * rank + i, device=dev) for i in range(4)]
+        losses = []
+        for i in range(args.warmup):
+            losses.append(trn.step(*batches[i % 4]))
+        torch.cuda.synchronize()
+        barrier()
+        s3, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s3.record()
+        for i in range(args.train_steps):
+            losses.append(trn.step(*batches[(args.warmup + i) % 4]))
+        e3.record()
+        e3.synchronize()
+        barrier()
+        ms3 = max_over_ranks(s3.elapsed_time(e3))
+        losses = [float(l) for l in losses]
+        tfps = train_flops_per_shot(tg, tcfg)
+        train = {"config": f"d={tcfg.d}, {tcfg.rounds} rounds, p={tcfg.p}, {tcfg.layers} layers, C={tcfg.channels}, "
+                           f"bf16 autocast, BCE vs sampled data-qubit errors, Adam lr 1e-3, grad-norm clip 1, "
+                           f"{'DDP over NCCL' if world > 1 else 'one GPU'}",
+                 "shots_per_gpu": args.train_batch, "steps": args.train_steps, "warmup": args.warmup,
+                 "ms_per_step": ms3 / args.train_steps,
+                 "shots_per_s": args.train_steps * args.train_batch * world / (ms3 / 1000.0),
+                 "flop_per_shot": tfps,
+                 "tflops_per_gpu": args.train_steps * args.train_batch * tfps / (ms3 / 1000.0) / 1e12,
+                 "loss_first": losses[0], "loss_last": losses[-1], "scaling": "weak",
+                 "peak_mem_gb": torch.cuda.max_memory_allocated(dev) / 1e9}
+
     if world > 1:
         dist.barrier()
     if rank == 0:
@@ -359,7 +401,7 @@ def main():
                 "scaling": "strong", "vs_baseline": None, "dtype": cfg.dtype, "data": "synthetic",
                 "config": workload(cfg, g, shots, world), "per_gpu": value / world, "roofline": roof,
                 "cpu_baseline": cpu, "e2e": e2e, "clocks": clk.summary(),
-                "gpu_launches": launches_per_fwd * args.steps, "flop_per_shot": fps, "streaming": stream}
+                "gpu_launches": launches_per_fwd * args.steps, "flop_per_shot": fps, "streaming": stream, "train": train}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

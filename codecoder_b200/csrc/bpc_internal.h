@@ -73,6 +73,11 @@ int gmm_tc_launch(const GmmProblem& p, const GmmMaps& maps, int* status, uint64_
 // Shots per tensor-core tile (TM of the blocked layout) for C_out.
 int gmm_tc_tile_shots(int Co);
 
+// Node-tiled tcgen05 path for small batches (rows of the MMA = 128 target nodes of one shot): bf16, rows layouts
+// with contiguous channels, Ci and Co in {64, 128}.  Same bits as gmm_tc_launch for the same shot.
+bool gmm_nodes_supported(const GmmProblem& p);
+int gmm_nodes_launch(const GmmProblem& p, int* status, uint64_t timeout_ns, cudaStream_t stream);
+
 // CUDA-core path: fp32 (f32 = true) or bf16 storage, fp32 accumulation.  Any Ci, Co % 4 == 0, Co <= 256.
 int gmm_fma_launch(const GmmProblem& p, bool f32, cudaStream_t stream);
 

@@ -40,6 +40,9 @@ namespace bpc {
 namespace {
 
 constexpr int kEmbShots = 128;
+// Passes of at most this many shots run the node-tiled kernels (rows of the MMA = nodes), larger ones the
+// shot-tiled kernels (rows = shots): below it a shot tile would be mostly empty.
+constexpr int64_t kNodePathMaxShots = 64;
 constexpr int kEmbNodes = 32;
 
 size_t esize(int dtype) { return dtype == BPC_DTYPE_F32 ? 4 : 2; }
@@ -246,19 +249,22 @@ extern "C" int bpc_predecoder_forward(bpc_predecoder* h, const uint8_t* det, flo
   const int64_t words = L.S / 32;
   const bool f32 = c.dtype == BPC_DTYPE_F32;
   const bool tc = !f32 && c.channels >= 64 && c.channels % 32 == 0;
+  const bool nodes = tc && B <= kNodePathMaxShots && (c.channels == 64 || c.channels == 128);
+  const bool shot_tiles = tc && !nodes;
   const size_t es = esize(c.dtype);
   const size_t wl = static_cast<size_t>(c.channels) * c.K * c.channels;
 
   // the two steps of layer l as bipartite-conv problems on the chunk's buffers
-  // tensor-core path: blocked (node, S / TM, C / 8, TM, 8) activations; CUDA-core path: node-major rows (node, S, C)
-  const int tm = tc ? gmm_tc_tile_shots(c.channels) : 0;
+  // shot-tiled tensor-core path: blocked (node, S / TM, C / 8, TM, 8) activations; node-tiled tensor-core and
+  // CUDA-core paths: node-major rows (node, S, C)
+  const int tm = shot_tiles ? gmm_tc_tile_shots(c.channels) : 0;
   const int64_t shot_stride = c.channels;
   const int64_t cg_stride = 8;
   const int64_t node_stride = L.S * c.channels;
-  if (tc && L.S % tm != 0) return fail(BPC_ERR_ARG, "pass size is not a multiple of the tensor-core tile");
+  if (shot_tiles && L.S % tm != 0) return fail(BPC_ERR_ARG, "pass size is not a multiple of the tensor-core tile");
   GmmProblem c2d, d2c;
   c2d.x = hc;
-  c2d.blocked = tc;
+  c2d.blocked = shot_tiles;
   c2d.x_shot_stride = shot_stride;
   c2d.x_node_stride = node_stride;
   c2d.x_cg_stride = cg_stride;
@@ -286,7 +292,7 @@ extern "C" int bpc_predecoder_forward(bpc_predecoder* h, const uint8_t* det, flo
 
   GmmMaps mc2d, md2c;
   std::vector<CUtensorMap> wm_c2d, wm_d2c;
-  if (tc) {
+  if (shot_tiles) {
     c2d.shots = d2c.shots = L.S;
     c2d.w = h->w_c2d;
     d2c.w = h->w_d2c;
@@ -341,13 +347,15 @@ extern "C" int bpc_predecoder_forward(bpc_predecoder* h, const uint8_t* det, flo
       for (int step = 0; step < 2; ++step) {
         const GmmProblem& p = step == 0 ? c2d : d2c;
         const bool rec = 2 * n_rec + 1 < h->step_events.size();
-        if (tc) {   // the tile counter of the dynamic scheduler starts at zero
+        if (shot_tiles) {   // the tile counter of the dynamic scheduler starts at zero
           cudaError_t me = cudaMemsetAsync(h->tile_counter, 0, sizeof(unsigned long long), stream);
           if (me != cudaSuccess) return fail(BPC_ERR_LAUNCH, std::string("cudaMemsetAsync: ") + cudaGetErrorString(me));
         }
         if (rec) cudaEventRecord(h->step_events[2 * n_rec], stream);
         int e;
-        if (tc) {
+        if (nodes) {
+          e = gmm_nodes_launch(p, h->status, h->timeout_ns, stream);
+        } else if (tc) {
           GmmMaps m = step == 0 ? mc2d : md2c;
           m.w = step == 0 ? wm_c2d[l] : wm_d2c[l];
           GmmProblem pc = p;

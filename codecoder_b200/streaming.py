@@ -5,8 +5,10 @@ Each step is one CUDA-graph replay on the decoder's stream:
   2. copy the new round's detectors in from pinned host memory (nh X detectors, nh Z detectors),
   3. run the pre-decoder forward on the window (bpc_predecoder_forward: embed, 2L bipartite steps, head, residual),
   4. copy the window's residual syndrome and the newest round's X/Z logits out to pinned host memory.
-The graph is captured once after a warm-up step, so a step costs one graph launch plus the device work.  The window
-keeps the model's time boundary: the oldest round is t = 0 and the newest t = W - 1 (RotatedSurface(d, W)).
+The graph is captured once after a warm-up step, so a step costs one graph launch plus the device work.  A batch of
+one shot runs the node-tiled kernels (the MMA rows are 128 target nodes, gmm_nodes.cu), which give the same bits as
+the shot-tiled kernels of large batches.  The window keeps the model's time boundary: the oldest round is t = 0 and
+the newest t = W - 1 (RotatedSurface(d, W)).
 """
 from __future__ import annotations
 

@@ -123,3 +123,23 @@ def test_predecoder_forward_host_matches_device_forward():
     rs_h = torch.empty(len(det), g.N_c, dtype=torch.uint8).pin_memory()
     pd.forward_host(det_h, lg_h, rs_h, slice_shots=256)        # 5 slices, copies overlapping compute
     assert torch.equal(lg_h, ref_lg.cpu()) and torch.equal(rs_h, ref_rs.cpu())
+
+
+@pytest.mark.parametrize("name,layers", [("d17_stream", 3), ("d13_bf16", 2)])
+def test_small_batch_node_tiles_match_shot_tiles(name, layers):
+    """Passes of <= 64 shots run the node-tiled kernels (MMA rows = nodes), larger ones the shot-tiled kernels (MMA
+    rows = shots): the same shots give the same bits either way, and the small batch matches the oracle."""
+    cfg = replace(CONFIGS[name], layers=layers)
+    g = RotatedSurface(cfg.d, cfg.rounds)
+    params = init_params(cfg, 808)
+    det, _ = sample(g, 0.02, 100, 809)
+    pd = PreDecoder(g, cfg, params, device=DEV)
+    big_lg, big_rs = pd(torch.as_tensor(det).to(DEV))
+    small_lg, small_rs = pd(torch.as_tensor(det[:40]).to(DEV))
+    one_lg, one_rs = pd(torch.as_tensor(det[7:8]).to(DEV))
+    torch.cuda.synchronize()
+    assert pd.status() == 0
+    assert torch.equal(small_lg, big_lg[:40]) and torch.equal(small_rs, big_rs[:40])
+    assert torch.equal(one_lg[0], big_lg[7]) and torch.equal(one_rs[0], big_rs[7])
+    ref_lg, ref_rs = orc.predecoder(g, cfg, storage_params(cfg, params), det[:40], dtype=torch.float32)
+    check_parity(g, cfg, det[:40], small_lg.cpu().numpy(), small_rs.cpu().numpy(), ref_lg, ref_rs)
