@@ -59,9 +59,11 @@ __global__ void __launch_bounds__(256) embed_kernel(const uint8_t* __restrict__ 
                                                    int64_t words) {
   __shared__ uint8_t tile[kEmbNodes][kEmbShots + 4];
   __shared__ __align__(16) T emb[4 * 256];
+  __shared__ uint8_t types[kEmbNodes];
   const int64_t s0 = static_cast<int64_t>(blockIdx.x) * kEmbShots;
   const int n0 = blockIdx.y * kEmbNodes;
   for (int e = threadIdx.x; e < 4 * C; e += blockDim.x) emb[e] = embed[e];
+  if (threadIdx.x < kEmbNodes) types[threadIdx.x] = n0 + threadIdx.x < N_c ? ctype[n0 + threadIdx.x] : 0;
   for (int e = threadIdx.x; e < kEmbNodes * kEmbShots; e += blockDim.x) {
     const int s = e / kEmbNodes, j = e - s * kEmbNodes;
     const int64_t shot = s0 + s;
@@ -80,24 +82,25 @@ __global__ void __launch_bounds__(256) embed_kernel(const uint8_t* __restrict__ 
       if (lane == 0 && word < words) bits[static_cast<int64_t>(n) * words + word] = m;
     }
   }
-  // features in 8-element groups (16 bytes of bf16, 32 of fp32: two 16-byte vectors)
+  // features in 8-element groups (16 bytes of bf16, 32 of fp32: two 16-byte vectors), one (node, group, shot)
+  // element per thread and iteration, shots fastest (contiguous in the chunked layout)
   constexpr int kVec = 16 / sizeof(T);
   const int groups = C / 8;
-  const int64_t smax = (shots - s0) < kEmbShots ? (shots - s0) : kEmbShots;
-  for (int j = 0; j < kEmbNodes; ++j) {
+  const int smax = static_cast<int>((shots - s0) < kEmbShots ? (shots - s0) : kEmbShots);
+  const int per_node = groups * smax;
+  for (int e = threadIdx.x; e < kEmbNodes * per_node; e += blockDim.x) {
+    const int j = e / per_node;
+    const int rem = e - j * per_node;
+    const int g = rem / smax, s = rem - g * smax;
     const int n = n0 + j;
-    if (n >= N_c) break;
-    const int tb = 2 * ctype[n];
+    if (n >= N_c) continue;
+    const int tok = 2 * types[j] + tile[j][s];
+    const int64_t shot = s0 + s;
     T* base = hc + static_cast<int64_t>(n) * node_stride;
-    for (int e = threadIdx.x; e < groups * smax; e += blockDim.x) {
-      const int g = e / smax, s = e - g * smax;              // shots fastest: contiguous in the chunked layout
-      const int tok = tb + tile[j][s];
-      const int64_t shot = s0 + s;
-      T* dst = tm ? base + (shot / tm) * C * tm + g * tm * 8 + (shot % tm) * 8 : base + g * cg_stride + shot * shot_stride;
-      const uint4* src = reinterpret_cast<const uint4*>(emb + tok * C + g * 8);
+    T* dst = tm ? base + (shot / tm) * C * tm + g * tm * 8 + (shot % tm) * 8 : base + g * cg_stride + shot * shot_stride;
+    const uint4* src = reinterpret_cast<const uint4*>(emb + tok * C + g * 8);
 #pragma unroll
-      for (int v = 0; v < 8 / kVec; ++v) reinterpret_cast<uint4*>(dst)[v] = src[v];
-    }
+    for (int v = 0; v < 8 / kVec; ++v) reinterpret_cast<uint4*>(dst)[v] = src[v];
   }
 }
 

@@ -128,7 +128,9 @@ def test_predecoder_forward_host_matches_device_forward():
 @pytest.mark.parametrize("name,layers", [("d17_stream", 3), ("d13_bf16", 2)])
 def test_small_batch_node_tiles_match_shot_tiles(name, layers):
     """Passes of <= 64 shots run the node-tiled kernels (MMA rows = nodes), larger ones the shot-tiled kernels (MMA
-    rows = shots): the same shots give the same bits either way, and the small batch matches the oracle."""
+    rows = shots).  At C = 128 the node-tiled kernel accumulates in the shot-tiled kernel's order: the same bits.  At
+    C = 64 the relation-split kernel adds the 8 relations' fp32 partials across a CTA cluster: the same sum up to
+    the association of the additions, held to the oracle like every other path."""
     cfg = replace(CONFIGS[name], layers=layers)
     g = RotatedSurface(cfg.d, cfg.rounds)
     params = init_params(cfg, 808)
@@ -139,7 +141,10 @@ def test_small_batch_node_tiles_match_shot_tiles(name, layers):
     one_lg, one_rs = pd(torch.as_tensor(det[7:8]).to(DEV))
     torch.cuda.synchronize()
     assert pd.status() == 0
-    assert torch.equal(small_lg, big_lg[:40]) and torch.equal(small_rs, big_rs[:40])
-    assert torch.equal(one_lg[0], big_lg[7]) and torch.equal(one_rs[0], big_rs[7])
+    assert torch.equal(one_lg[0], small_lg[7]) and torch.equal(one_rs[0], small_rs[7])
     ref_lg, ref_rs = orc.predecoder(g, cfg, storage_params(cfg, params), det[:40], dtype=torch.float32)
     check_parity(g, cfg, det[:40], small_lg.cpu().numpy(), small_rs.cpu().numpy(), ref_lg, ref_rs)
+    if cfg.channels == 128:
+        assert torch.equal(small_lg, big_lg[:40]) and torch.equal(small_rs, big_rs[:40])
+    else:
+        assert orc.logit_error(small_lg.cpu().numpy(), big_lg[:40].cpu().numpy()) < 1e-2
