@@ -25,6 +25,15 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 }
 
 // ---------------------------------------------------------------------------------------------------------------
+// Programmatic dependent launch: a kernel launched with programmatic stream serialization may start while the
+// previous kernel of the stream still runs.  pdl_launch_dependents lets the next kernel start; pdl_wait blocks the
+// calling thread until the previous kernel has completed and its memory is visible (a no-op without the launch
+// attribute).  Everything before pdl_wait may touch only shared memory, tensor memory and inputs no kernel of the
+// stream writes.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------------------------------------------
 // mbarrier
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");

@@ -84,6 +84,10 @@ int gmm_fma_launch(const GmmProblem& p, bool f32, cudaStream_t stream);
 int num_sms();
 // Opt a kernel in to `bytes` of dynamic shared memory on the current device (once per device and kernel).
 int allow_smem(const void* fn, int bytes);
+// Launch with programmatic stream serialization (the kernel's prologue may overlap the previous kernel; the kernel
+// calls pdl_wait before it reads what earlier kernels wrote), optionally as clusters of cluster_x CTAs.
+int launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, void** args, int cluster_x,
+               const char* what);
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (null when the driver lacks it).
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();

@@ -108,6 +108,7 @@ __global__ void __launch_bounds__(kNodeThreads, 1)
   const bool second = tile >= a.tiles_a;
   const int n_begin = second ? a.type_split + (tile - a.tiles_a) * kNodeRows : tile * kNodeRows;
   const int n_end = second ? a.NT : min(a.type_split, n_begin + kNodeRows);
+  pdl_launch_dependents();
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
@@ -141,6 +142,7 @@ __global__ void __launch_bounds__(kNodeThreads, 1)
       sidx[e] = n < n_end ? __ldg(a.idx + static_cast<int64_t>(n_begin) * a.K + e) : -1;
     }
     named_bar_sync(1, kNodeRows);
+    pdl_wait();                           // the activations are the previous kernels' outputs
     const int row = t;                    // = 32 warp + lane
     const int q4 = lane & ~3;             // first row (within the warp) of this lane's 4-row group
     bool ok = true;
@@ -422,6 +424,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
 
   const int t = threadIdx.x;
   const int warp = t >> 5, lane = t & 31;
+  pdl_launch_dependents();
   const int r = static_cast<int>(cluster_ctarank());
   const int tile = blockIdx.x / kSplitK;
   const int64_t shot = blockIdx.y;
@@ -434,10 +437,6 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
   const int orow = t >> 3;                      // output row 16 r + orow, channels 8 (t % 8) .. + 7
   const int on = n_begin + r * 16 + orow;
   const bool o_ok = on < n_end;
-  uint4 res = make_uint4(0, 0, 0, 0);
-  if (EPI == kEpiGeluResid && o_ok)
-    res = *reinterpret_cast<const uint4*>(a.y + shot * a.y_shot_stride + static_cast<int64_t>(on) * a.y_node_stride +
-                                          (t & 7) * 8);
 
   if (t == 0) {
     mbar_init(smem_u32(full), 4 + 1);          // one expect_tx arrival per gathering warp + W_r's
@@ -463,6 +462,11 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
     mbar_arrive_expect_tx(smem_u32(full), kW);
     tma_load_3d(smem_u32(sW), &tmW, 0, r, second ? C : 0, smem_u32(full));
   }
+  pdl_wait();                                   // the activations are the previous kernels' outputs
+  uint4 res = make_uint4(0, 0, 0, 0);
+  if (EPI == kEpiGeluResid && o_ok)
+    res = *reinterpret_cast<const uint4*>(a.y + shot * a.y_shot_stride + static_cast<int64_t>(on) * a.y_node_stride +
+                                          (t & 7) * 8);
   {
     // relation r's source rows, 4 per TMA gather (lanes 0, 4, .., 28 of every warp), pads read zeros
     const int32_t xr = (src >= 0 && src < a.NS) ? static_cast<int32_t>(src * a.x_row_node + shot * a.x_row_shot)
@@ -722,22 +726,12 @@ int gmm_nodes_launch(const GmmProblem& p, int* status, uint64_t timeout_ns, cuda
     if (!sf) return fail(BPC_ERR_ARG, "node-tiled path: unsupported epilogue");
     const int ssmem = 1024 + kNodeRows * 128 + 64 * 128 + 2 * kSplitK * 16 * 64 * 4 + 64;
     if (int e = allow_smem(reinterpret_cast<const void*>(sf), ssmem)) return e;
-    cudaLaunchConfig_t lc = {};
-    lc.gridDim = dim3(static_cast<unsigned>(a.tiles * kSplitK), static_cast<unsigned>(p.shots));
-    lc.blockDim = dim3(kSplitThreads);
-    lc.dynamicSmemBytes = static_cast<size_t>(ssmem);
-    lc.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = kSplitK;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    lc.attrs = attr;
-    lc.numAttrs = 1;
     void* sargs[] = {&tmW, &tmX, &a};
-    cudaError_t le = cudaLaunchKernelExC(&lc, reinterpret_cast<const void*>(sf), sargs);
-    if (le != cudaSuccess)
-      return fail(BPC_ERR_LAUNCH, std::string("gmm_nodes_split_kernel launch: ") + cudaGetErrorString(le));
+    if (int e = launch_pdl(reinterpret_cast<const void*>(sf), dim3(static_cast<unsigned>(a.tiles * kSplitK),
+                                                                   static_cast<unsigned>(p.shots)),
+                           dim3(kSplitThreads), static_cast<size_t>(ssmem), stream, sargs, kSplitK,
+                           "gmm_nodes_split_kernel"))
+      return e;
     return 0;
   }
   const int nkb = p.Ci / 64;
@@ -751,9 +745,9 @@ int gmm_nodes_launch(const GmmProblem& p, int* status, uint64_t timeout_ns, cuda
   if (!fn) return fail(BPC_ERR_ARG, "node-tiled path: unsupported epilogue");
   if (int e = allow_smem(reinterpret_cast<const void*>(fn), kNodeSmemLimit)) return e;
   void* args[] = {&tmW, &tmX, &tmY, &a};
-  cudaError_t le = cudaLaunchKernel(reinterpret_cast<const void*>(fn), dim3(a.tiles, static_cast<unsigned>(p.shots)),
-                                    dim3(kNodeThreads), args, static_cast<size_t>(smem), stream);
-  if (le != cudaSuccess) return fail(BPC_ERR_LAUNCH, std::string("gmm_nodes_kernel launch: ") + cudaGetErrorString(le));
+  if (int e = launch_pdl(reinterpret_cast<const void*>(fn), dim3(a.tiles, static_cast<unsigned>(p.shots)),
+                         dim3(kNodeThreads), static_cast<size_t>(smem), stream, args, 1, "gmm_nodes_kernel"))
+    return e;
   return 0;
 }
 

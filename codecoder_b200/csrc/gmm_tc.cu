@@ -511,6 +511,32 @@ int allow_smem(const void* fn, int bytes) {
   return 0;
 }
 
+int launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, void** args, int cluster_x,
+               const char* what) {
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = grid;
+  lc.blockDim = block;
+  lc.dynamicSmemBytes = smem;
+  lc.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[n].val.programmaticStreamSerializationAllowed = 1;
+  ++n;
+  if (cluster_x > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = static_cast<unsigned>(cluster_x);
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  lc.attrs = attr;
+  lc.numAttrs = n;
+  cudaError_t e = cudaLaunchKernelExC(&lc, fn, args);
+  if (e != cudaSuccess) return fail(4, std::string(what) + " launch: " + cudaGetErrorString(e));
+  return 0;
+}
+
 int num_sms() {
   static int n = 0;
   if (n == 0) {

@@ -62,8 +62,10 @@ __global__ void __launch_bounds__(256) embed_kernel(const uint8_t* __restrict__ 
   __shared__ uint8_t types[kEmbNodes];
   const int64_t s0 = static_cast<int64_t>(blockIdx.x) * kEmbShots;
   const int n0 = blockIdx.y * kEmbNodes;
+  pdl_launch_dependents();
   for (int e = threadIdx.x; e < 4 * C; e += blockDim.x) emb[e] = embed[e];
   if (threadIdx.x < kEmbNodes) types[threadIdx.x] = n0 + threadIdx.x < N_c ? ctype[n0 + threadIdx.x] : 0;
+  pdl_wait();                               // det, and the buffers earlier kernels still read, are shared
   for (int e = threadIdx.x; e < kEmbNodes * kEmbShots; e += blockDim.x) {
     const int s = e / kEmbNodes, j = e - s * kEmbNodes;
     const int64_t shot = s0 + s;
@@ -110,6 +112,8 @@ __global__ void __launch_bounds__(256) unpack_kernel(const uint32_t* __restrict_
   __shared__ uint32_t w[kEmbNodes][kEmbShots / 32];
   const int64_t s0 = static_cast<int64_t>(blockIdx.x) * kEmbShots;
   const int n0 = blockIdx.y * kEmbNodes;
+  pdl_launch_dependents();
+  pdl_wait();
   for (int e = threadIdx.x; e < kEmbNodes * (kEmbShots / 32); e += blockDim.x) {
     const int j = e / (kEmbShots / 32), k = e - j * (kEmbShots / 32);
     const int64_t word = (s0 >> 5) + k;
@@ -318,16 +322,22 @@ extern "C" int bpc_predecoder_forward(bpc_predecoder* h, const uint8_t* det, flo
     {
       dim3 grid(static_cast<unsigned>((Sb + kEmbShots - 1) / kEmbShots),
                 static_cast<unsigned>((c.n_checks + kEmbNodes - 1) / kEmbNodes));
-      if (f32)
-        embed_kernel<float><<<grid, 256, 0, stream>>>(det + b0 * c.n_checks, Sb, c.n_checks, c.channels,
-                                                      h->check_type, static_cast<const float*>(h->embed),
-                                                      static_cast<float*>(hc), node_stride, cg_stride, shot_stride,
-                                                      tm, bits, words);
-      else
-        embed_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
-            det + b0 * c.n_checks, Sb, c.n_checks, c.channels, h->check_type,
-            static_cast<const __nv_bfloat16*>(h->embed), static_cast<__nv_bfloat16*>(hc), node_stride, cg_stride,
-            shot_stride, tm, bits, words);
+      const uint8_t* det_b = det + b0 * c.n_checks;
+      int Nc = c.n_checks, Cc = c.channels;
+      int tm_i = tm;
+      int64_t Sb_i = Sb, ns = node_stride, cgs = cg_stride, ss = shot_stride, wd = words;
+      const uint8_t* ct = h->check_type;
+      const void* emb = h->embed;
+      void* hcp = hc;
+      uint32_t* bp = bits;
+      void* eargs[] = {&det_b, &Sb_i, &Nc, &Cc, &ct, &emb, &hcp, &ns, &cgs, &ss, &tm_i, &bp, &wd};
+      const void* efn = f32 ? reinterpret_cast<const void*>(&embed_kernel<float>)
+                            : reinterpret_cast<const void*>(&embed_kernel<__nv_bfloat16>);
+      if (nodes) {
+        if (int e = launch_pdl(efn, grid, dim3(256), 0, stream, eargs, 1, "embed_kernel")) return e;
+      } else if (cudaLaunchKernel(efn, grid, dim3(256), eargs, 0, stream) != cudaSuccess) {
+        return fail(BPC_ERR_LAUNCH, std::string("embed_kernel: ") + cudaGetErrorString(cudaGetLastError()));
+      }
       cudaError_t e = cudaGetLastError();
       if (e != cudaSuccess) return fail(BPC_ERR_LAUNCH, std::string("embed_kernel: ") + cudaGetErrorString(e));
     }
@@ -375,7 +385,18 @@ extern "C" int bpc_predecoder_forward(bpc_predecoder* h, const uint8_t* det, flo
     {
       dim3 grid(static_cast<unsigned>((Sb + kEmbShots - 1) / kEmbShots),
                 static_cast<unsigned>((c.n_checks + kEmbNodes - 1) / kEmbNodes));
-      unpack_kernel<<<grid, 256, 0, stream>>>(bits, words, Sb, c.n_checks, residual + b0 * c.n_checks);
+      const uint32_t* bp = bits;
+      int64_t wd = words, Sb_i = Sb;
+      int Nc = c.n_checks;
+      uint8_t* outp = residual + b0 * c.n_checks;
+      void* uargs[] = {&bp, &wd, &Sb_i, &Nc, &outp};
+      if (nodes) {
+        if (int e = launch_pdl(reinterpret_cast<const void*>(&unpack_kernel), grid, dim3(256), 0, stream, uargs, 1,
+                               "unpack_kernel"))
+          return e;
+      } else {
+        unpack_kernel<<<grid, 256, 0, stream>>>(bits, words, Sb, c.n_checks, residual + b0 * c.n_checks);
+      }
       cudaError_t e = cudaGetLastError();
       if (e != cudaSuccess) return fail(BPC_ERR_LAUNCH, std::string("unpack_kernel: ") + cudaGetErrorString(e));
     }
