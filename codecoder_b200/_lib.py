@@ -11,6 +11,8 @@ LIB_PATH = os.environ.get("BPC_LIB", os.path.join(_PKG, "libbpc.so"))
 
 BPC_DTYPE_F32 = 0
 BPC_DTYPE_BF16 = 1
+BPC_EPILOGUE_STORE = 0
+BPC_EPILOGUE_AFFINE_SILU = 1
 
 c_i32 = ctypes.c_int32
 c_i64 = ctypes.c_int64
@@ -28,6 +30,10 @@ SIGNATURES = {
     "bpc_last_error": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_int]),
     "bpc_gather_mm_fwd": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32,
                                          c_vp]),
+    "bpc_gather_mm_fwd_ex": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32,
+                                            c_i32, c_i32, c_vp, c_vp, c_i32, c_vp]),
+    "bpc_residual_affine_silu": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, ctypes.c_float, ctypes.c_float,
+                                                c_vp, c_vp, c_vp]),
     "bpc_gather_mm_dgrad": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_i32, c_i32, c_i32,
                                            c_i32, c_vp]),
     "bpc_gather_mm_wgrad": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, ctypes.c_size_t, c_i64, c_i32, c_i32, c_i32,

@@ -53,10 +53,15 @@ extern "C" int bpc_last_error(char* buf, int len) {
   return n;
 }
 
-extern "C" int bpc_gather_mm_fwd(const void* x, const void* w, const int32_t* idx, void* y, int64_t B, int32_t NS,
-                                 int32_t NT, int32_t K, int32_t Ci, int32_t Co, int32_t dtype, bpc_stream_t stream) {
+namespace {
+
+int run_gather_mm(const void* x, const void* w, const int32_t* idx, void* y, int64_t B, int32_t NS, int32_t NT,
+                  int32_t K, int32_t Ci, int32_t Co, int32_t n_wtypes, int32_t type_split, int epi,
+                  const float* scale, const float* shift, int32_t dtype, bpc_stream_t stream) {
   if (B < 0 || NS < 1 || NT < 0 || K < 1 || Ci < 1 || Co < 1) return fail(BPC_ERR_ARG, "invalid gather_mm shape");
   if (dtype != BPC_DTYPE_BF16 && dtype != BPC_DTYPE_F32) return fail(BPC_ERR_ARG, "dtype must be bf16 or f32");
+  if (n_wtypes < 1 || n_wtypes > 2 || type_split < 0 || type_split > NT)
+    return fail(BPC_ERR_ARG, "one or two weight sets, split inside [0, NT]");
   if (B == 0 || NT == 0) return 0;
   if (!x || !w || !idx || !y) return fail(BPC_ERR_ARG, "null buffer");
   GmmProblem p;
@@ -66,8 +71,8 @@ extern "C" int bpc_gather_mm_fwd(const void* x, const void* w, const int32_t* id
   p.shots = B;
   p.NS = NS;
   p.w = w;
-  p.n_wtypes = 1;
-  p.type_split = NT;
+  p.n_wtypes = n_wtypes;
+  p.type_split = n_wtypes > 1 ? type_split : NT;
   p.idx = idx;
   p.NT = NT;
   p.K = K;
@@ -76,7 +81,9 @@ extern "C" int bpc_gather_mm_fwd(const void* x, const void* w, const int32_t* id
   p.y = y;
   p.y_shot_stride = static_cast<int64_t>(NT) * Co;   // y (B, NT, Co)
   p.y_node_stride = Co;
-  p.epi = kEpiStore;
+  p.epi = epi;
+  p.epi_scale = scale;
+  p.epi_shift = shift;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (dtype == BPC_DTYPE_BF16 && Ci >= 64 && Ci % 8 == 0 && Co % 32 == 0 && Co <= 256 && K <= 16) {
     if (int e = gmm_tc_check(p)) return e;
@@ -85,6 +92,29 @@ extern "C" int bpc_gather_mm_fwd(const void* x, const void* w, const int32_t* id
     return gmm_tc_launch(p, maps, op_status_ptr(), 2000000000ull, s);
   }
   return gmm_fma_launch(p, dtype == BPC_DTYPE_F32, s);
+}
+
+}  // namespace
+
+extern "C" int bpc_gather_mm_fwd(const void* x, const void* w, const int32_t* idx, void* y, int64_t B, int32_t NS,
+                                 int32_t NT, int32_t K, int32_t Ci, int32_t Co, int32_t dtype, bpc_stream_t stream) {
+  return run_gather_mm(x, w, idx, y, B, NS, NT, K, Ci, Co, 1, NT, kEpiStore, nullptr, nullptr, dtype, stream);
+}
+
+extern "C" int bpc_gather_mm_fwd_ex(const void* x, const void* w, const int32_t* idx, void* y, int64_t B, int32_t NS,
+                                    int32_t NT, int32_t K, int32_t Ci, int32_t Co, int32_t n_wtypes,
+                                    int32_t type_split, int32_t epilogue, const float* scale, const float* shift,
+                                    int32_t dtype, bpc_stream_t stream) {
+  int epi;
+  if (epilogue == BPC_EPILOGUE_STORE) {
+    epi = kEpiStore;
+  } else if (epilogue == BPC_EPILOGUE_AFFINE_SILU) {
+    epi = kEpiAffineSilu;
+    if (!scale || !shift) return fail(BPC_ERR_ARG, "the affine + SiLU epilogue needs scale and shift");
+  } else {
+    return fail(BPC_ERR_ARG, "unknown epilogue");
+  }
+  return run_gather_mm(x, w, idx, y, B, NS, NT, K, Ci, Co, n_wtypes, type_split, epi, scale, shift, dtype, stream);
 }
 
 extern "C" int bpc_gather_mm_dgrad(const void* gy, const void* w, const int32_t* tgt, void* gx, void* w_t, int64_t B,

@@ -246,6 +246,17 @@ __device__ __forceinline__ uint64_t gelu_tanh_fast2(uint64_t x) {
   return f2_fma(hx, t, hx);
 }
 
+// SiLU of a packed pair: x sigmoid(x) = h + h tanh(h) with h = x / 2, tanh on the MUFU unit (used where the result
+// is rounded to bf16 right after).
+__device__ __forceinline__ uint64_t silu_tanh_fast2(uint64_t x) {
+  const uint64_t kHalf = f2_pack(0.5f, 0.5f);
+  const uint64_t h = f2_mul(x, kHalf);
+  const uint64_t t = f2_pack(tanh_approx(f2_lo(h)), tanh_approx(f2_hi(h)));
+  return f2_fma(h, t, h);
+}
+// SiLU with CUDA's expf (fp32 networks)
+__device__ __forceinline__ float silu_exact(float x) { return x / (1.0f + expf(-x)); }
+
 __device__ __forceinline__ float gelu_tanh(float x) {
   const float u = 0.7978845608028654f * fmaf(0.044715f * x, x * x, x);
   return 0.5f * x * (1.0f + tanhf(u));

@@ -14,6 +14,7 @@ enum EpiMode : int {
   kEpiStore = 0,      // y = acc
   kEpiGeluInit = 1,   // y = GELU(acc)
   kEpiGeluResid = 2,  // y = y + GELU(acc)
+  kEpiAffineSilu = 3, // y = SiLU(scale[c] acc + shift[c])  (an inference BatchNorm folded into scale / shift)
 };
 
 // Optional work fused into the epilogue of the last check -> data step of the pre-decoder.
@@ -50,6 +51,8 @@ struct GmmProblem {
   void* y = nullptr;
   int64_t y_shot_stride = 0, y_node_stride = 0, y_cg_stride = 8;
   int epi = kEpiStore;
+  const float* epi_scale = nullptr;   // kEpiAffineSilu: per output channel (Co,) fp32
+  const float* epi_shift = nullptr;
   HeadEpilogue head;
   // tensor-core path: a device counter that is zero when the kernel starts hands out tiles dynamically (null:
   // static striding)

@@ -43,6 +43,8 @@ struct FmaArgs {
   void* y;
   int64_t y_shot_stride, y_node_stride, y_cg_stride;
   int epi;
+  const float* epi_scale;
+  const float* epi_shift;
   HeadEpilogue head;
 };
 
@@ -100,6 +102,7 @@ __global__ void __launch_bounds__(kFmaThreads) gmm_fma_kernel(const FmaArgs a) {
         T* yp = yr + ch_off(o0 + j, a.y_cg_stride);
         if (a.epi == kEpiGeluInit) v = gelu_tanh(v);
         else if (a.epi == kEpiGeluResid) v = ld_elem(yp) + gelu_tanh(v);
+        else if (a.epi == kEpiAffineSilu) v = silu_exact(fmaf(v, __ldg(a.epi_scale + o0 + j), __ldg(a.epi_shift + o0 + j)));
         const T sv = st_conv<T>(v);
         *yp = sv;
         if (a.head.head_w) {
@@ -149,6 +152,8 @@ int gmm_fma_launch(const GmmProblem& p, bool f32, cudaStream_t stream) {
   if (p.Co < 4 || p.Co > 256 || p.Co % 4 != 0) return fail(2, "CUDA-core path needs C_out in 4..256, multiple of 4");
   if (p.Ci < 1) return fail(2, "C_in must be positive");
   if (p.K < 1 || p.NT < 1 || p.NS < 1) return fail(2, "empty problem");
+  if (p.epi == kEpiAffineSilu && (!p.epi_scale || !p.epi_shift))
+    return fail(2, "the affine + SiLU epilogue needs scale and shift vectors");
   if (p.shots <= 0) return 0;
   FmaArgs a;
   a.x = p.x;
@@ -169,6 +174,8 @@ int gmm_fma_launch(const GmmProblem& p, bool f32, cudaStream_t stream) {
   a.y_node_stride = p.y_node_stride;
   a.y_cg_stride = p.y_cg_stride;
   a.epi = p.epi;
+  a.epi_scale = p.epi_scale;
+  a.epi_shift = p.epi_shift;
   a.head = p.head;
   const int64_t tiles = static_cast<int64_t>(p.NT) * ((p.shots + kFmaShots - 1) / kFmaShots);
   if (tiles > 0x7fffffffLL) return fail(2, "too many tiles for one launch");

@@ -64,6 +64,8 @@ struct TcArgs {
   void* y;
   int64_t y_shot_stride, y_node_stride, y_cg_stride;
   int epi;
+  const float* epi_scale;
+  const float* epi_shift;
   HeadEpilogue head;
   int* status;
   uint64_t timeout_ns;
@@ -389,7 +391,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
                 uint64_t x = f2_pack(v[j * 8 + 2 * e], v[j * 8 + 2 * e + 1]);
-                if (EPI != kEpiStore) x = gelu_tanh_fast2(x);
+                if (EPI == kEpiAffineSilu) {
+                  const int colp = c * 32 + j * 8 + 2 * e;
+                  x = silu_tanh_fast2(f2_fma(x, *reinterpret_cast<const uint64_t*>(a.epi_scale + colp),
+                                             *reinterpret_cast<const uint64_t*>(a.epi_shift + colp)));
+                } else if (EPI != kEpiStore) {
+                  x = gelu_tanh_fast2(x);
+                }
                 if (kResid) x = f2_add(x, bf2_to_f2(h[e]));
                 o[e] = f2_to_bf2(x);
                 if (HEAD) {
@@ -472,7 +480,12 @@ using KernelFn = void (*)(CUtensorMap, CUtensorMap, TcArgs);
 template <int NCH>
 KernelFn kernel_for(bool blocked, int epi, bool head) {
   constexpr int MT = mt_for(NCH * 32);
-  if (!blocked) return (epi == kEpiStore && !head) ? &gmm_tc_kernel<MT, NCH, false, kEpiStore, false> : nullptr;
+  if (!blocked) {
+    if (head) return nullptr;
+    if (epi == kEpiStore) return &gmm_tc_kernel<MT, NCH, false, kEpiStore, false>;
+    if (epi == kEpiAffineSilu) return &gmm_tc_kernel<MT, NCH, false, kEpiAffineSilu, false>;
+    return nullptr;
+  }
   if (epi == kEpiGeluInit)
     return head ? &gmm_tc_kernel<MT, NCH, true, kEpiGeluInit, true> : &gmm_tc_kernel<MT, NCH, true, kEpiGeluInit, false>;
   if (epi == kEpiGeluResid)
@@ -569,6 +582,9 @@ int gmm_tc_check(const GmmProblem& p) {
   if (p.head.head_w && (!p.head.logits || (reinterpret_cast<uintptr_t>(p.head.logits) & 7) ||
                         ((p.head.lg_shot_stride | p.head.lg_node_stride) & 1)))
     return fail(2, "head logits must be 8-byte aligned with even strides");
+  if (p.epi == kEpiAffineSilu && (!p.epi_scale || !p.epi_shift ||
+                                  ((reinterpret_cast<uintptr_t>(p.epi_scale) | reinterpret_cast<uintptr_t>(p.epi_shift)) & 7)))
+    return fail(2, "the affine + SiLU epilogue needs 8-byte aligned scale and shift vectors");
   return 0;
 }
 
@@ -626,6 +642,8 @@ int gmm_tc_launch(const GmmProblem& p, const GmmMaps& maps, int* status, uint64_
   a.y_node_stride = p.y_node_stride;
   a.y_cg_stride = p.y_cg_stride;
   a.epi = p.epi;
+  a.epi_scale = p.epi_scale;
+  a.epi_shift = p.epi_shift;
   a.head = p.head;
   a.status = status;
   a.timeout_ns = timeout_ns;

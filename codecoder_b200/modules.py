@@ -1,5 +1,7 @@
 """Modules on the B200 kernels: BipartiteConv (drop-in for the reference's module) and PreDecoder.
 
+CascadeBlock(H, geo, L, res, impl) is the reference's bottleneck residual block (cascade_net.py:236-259) on the same op.
+
 BipartiteConv(C, geo, impl) keeps the reference's constructor, parameter names (w_c2d, w_d2c: one (C, K C) matrix per
 target type), registered tables (c2d{k}, inv_c2d{k}, d2c{k}, inv_d2c{k}) and forward (cascade_net.py:213-233).  It
 takes the reference's Geometry (BB codes, K = 12) or geometry.RotatedSurface (K = 8).
@@ -14,6 +16,7 @@ import math
 
 import numpy as np
 import torch
+import torch.nn.functional as F
 from torch import nn
 
 from . import _lib
@@ -213,3 +216,119 @@ class PreDecoder:
             self.close()
         except Exception:
             pass
+
+
+def _fold_bn(bn: nn.BatchNorm1d):
+    """Inference BatchNorm as a per-channel affine map: (scale, shift) fp32 with bn(x) = scale x + shift."""
+    scale = bn.weight.float() / torch.sqrt(bn.running_var.float() + bn.eps)
+    return scale, bn.bias.float() - bn.running_mean.float() * scale
+
+
+class CascadeBlock(nn.Module):
+    """The reference's bottleneck residual block (cascade_net.py:236-259) on the B200 op, with its parameter names
+    (bn1, bn2, bn3, down, conv, up) so its state_dicts load unchanged:
+        u = up(SiLU(BN3(conv(SiLU(BN2(down(SiLU(BN1(h)))))))));  h' = h + u / sqrt(2L) (res 'branch') or
+        h / sqrt(2L) + u (res 'skip'),  H -> H / 4 in the bottleneck.
+    Training: the reference's composition (batch statistics over every node of every shot, cascade_net.py:195-210),
+    the convolution through gather_mm (forward and backward on the B200 kernels).
+    Eval: the fused inference path on the folded BatchNorms --
+        BN1 + SiLU: one elementwise pass;  down + BN2 + SiLU: the op with K = 1 (identity table) and the affine + SiLU
+        epilogue;  conv: two launches, each covering both target types (stacked relation matrices, the targets are
+        type-major);  BN3 + SiLU: the epilogue of the second;  up and the residual: one bf16 GEMM and one fp32 add.
+    The bottleneck activations are bf16 (the reference's bf16 autocast), the residual stream keeps h's dtype."""
+
+    def __init__(self, H, geo, L, res="branch", impl="b200"):
+        super().__init__()
+        Hb = H // 4
+        self.bn1, self.bn2, self.bn3 = nn.BatchNorm1d(H), nn.BatchNorm1d(Hb), nn.BatchNorm1d(Hb)
+        self.down = nn.Linear(H, Hb, bias=False)
+        self.conv = BipartiteConv(Hb, geo, impl)
+        self.up = nn.Linear(Hb, H, bias=False)
+        for lin in (self.down, self.up):
+            nn.init.normal_(lin.weight, std=1 / math.sqrt(lin.in_features))
+        self.res, self.scale = res, 1 / math.sqrt(2 * L)
+        n_data = int(np.asarray(geo.c2d[0]).shape[0])
+        n_chk = int(np.asarray(geo.d2c[0]).shape[0])
+        self._splits = (n_data, n_chk)
+        self.register_buffer("c2d_all", torch.as_tensor(np.concatenate([np.asarray(t) for t in geo.c2d]), dtype=torch.int32),
+                             persistent=False)
+        self.register_buffer("d2c_all", torch.as_tensor(np.concatenate([np.asarray(t) for t in geo.d2c]), dtype=torch.int32),
+                             persistent=False)
+        self._cache = None
+
+    def _bn(self, mod, x):
+        C = x.shape[-1]
+        return mod(x.reshape(-1, C)).view(x.shape)
+
+    def branch(self, h):
+        u = self.down(F.silu(self._bn(self.bn1, h)))
+        u = self.conv(F.silu(self._bn(self.bn2, u)))
+        return self.up(F.silu(self._bn(self.bn3, u)))
+
+    def prepare_inference(self):
+        """Fold the BatchNorms and cast the weights once (call again after changing weights or statistics)."""
+        with torch.no_grad():
+            a1, b1 = _fold_bn(self.bn1)
+            a2, b2 = _fold_bn(self.bn2)
+            a3, b3 = _fold_bn(self.bn3)
+            bf = torch.bfloat16
+            self._cache = dict(a1=a1, b1=b1, a2=a2, b2=b2, a3=a3, b3=b3,
+                               down=self.down.weight.to(bf).contiguous(), up=self.up.weight.to(bf).contiguous(),
+                               wc=torch.stack([w.to(bf) for w in self.conv.w_c2d]).contiguous(),
+                               wd=torch.stack([w.to(bf) for w in self.conv.w_d2c]).contiguous(),
+                               ident=torch.zeros(0, dtype=torch.int32))
+        return self
+
+    def _fused(self, h, x1=None, nxt=None):
+        """h (B, N, H) fp32 -> (h', SiLU(BN1 of `nxt`)(h') bf16 or None).  x1: this block's SiLU(BN1(h)) if the
+        previous block already produced it."""
+        from .ops import gmm_ex, residual_affine_silu
+        c = self._cache
+        B, N, H = h.shape
+        if c["ident"].numel() != N or c["ident"].device != h.device:
+            c["ident"] = torch.arange(N, dtype=torch.int32, device=h.device).view(N, 1)
+        if x1 is None:
+            _, x1 = residual_affine_silu(h, None, 1.0, 0.0, c["a1"], c["b1"], want_out=False)
+        x2 = gmm_ex(x1, c["ident"], c["down"], scale=c["a2"], shift=c["b2"])
+        d = gmm_ex(x2, self.c2d_all, c["wc"], type_split=self._splits[0])
+        x3 = gmm_ex(d, self.d2c_all, c["wd"], type_split=self._splits[1], scale=c["a3"], shift=c["b3"])
+        u = torch.matmul(x3, c["up"].t())
+        sh, su = (1.0, self.scale) if self.res == "branch" else (self.scale, 1.0)
+        a_n = b_n = None
+        if nxt is not None:
+            if nxt._cache is None or nxt._cache["a1"].device != h.device:
+                nxt.prepare_inference()
+            a_n, b_n = nxt._cache["a1"], nxt._cache["b1"]
+        return residual_affine_silu(h, u, sh, su, a_n, b_n)
+
+    def forward(self, h):
+        if not self.training and h.is_cuda and h.dtype == torch.float32:
+            if self._cache is None or self._cache["a1"].device != h.device:
+                self.prepare_inference()
+            return self._fused(h)[0]
+        u = self.branch(h)
+        if self.res == "branch":
+            return h + self.scale * u
+        return self.scale * h + u
+
+
+class CascadeStack(nn.Module):
+    """A sequence of CascadeBlocks (the reference CascadeBB's `blocks`, cascade_net.py:319-343).  In eval mode on the
+    GPU the blocks hand over their fp32 residual stream and the next block's SiLU(BN1(.)) input in one pass each."""
+
+    def __init__(self, blocks):
+        super().__init__()
+        self.blocks = nn.ModuleList(blocks)
+
+    def forward(self, h):
+        if self.training or not h.is_cuda or h.dtype != torch.float32:
+            for b in self.blocks:
+                h = b(h)
+            return h
+        x = None
+        for i, b in enumerate(self.blocks):
+            if b._cache is None or b._cache["a1"].device != h.device:
+                b.prepare_inference()
+            nxt = self.blocks[i + 1] if i + 1 < len(self.blocks) else None
+            h, x = b._fused(h, x, nxt)
+        return h

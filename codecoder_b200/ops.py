@@ -67,6 +67,63 @@ def gmm(a: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, transposed: bool = 
     return y
 
 
+def gmm_ex(a: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, type_split: int | None = None,
+           scale: torch.Tensor | None = None, shift: torch.Tensor | None = None) -> torch.Tensor:
+    """Forward with one or two weight sets and an optional affine + SiLU epilogue (C ABI bpc_gather_mm_fwd_ex).
+    a (B, NS, C_in); idx (NT, K); w (C_out, K C_in) or (2, C_out, K C_in) with targets >= type_split using w[1];
+    scale / shift fp32 (C_out,): y = SiLU(scale * acc + shift) per output channel (an inference BatchNorm + SiLU)."""
+    _check_cuda(a, idx, w)
+    if a.dtype not in _DTYPES or w.dtype != a.dtype:
+        raise TypeError(f"gmm_ex needs bf16 or fp32 a and w of the same dtype, got {a.dtype} / {w.dtype}")
+    B, NS, Ci = a.shape
+    NT, K = idx.shape
+    n_w = 1 if w.dim() == 2 else w.shape[0]
+    Co, KC = w.shape[-2:]
+    if KC != K * Ci or n_w not in (1, 2):
+        raise ValueError("gmm_ex: w must be (C_out, K C_in) or (2, C_out, K C_in)")
+    split = NT if type_split is None else int(type_split)
+    if (scale is None) != (shift is None):
+        raise ValueError("gmm_ex: give both scale and shift, or neither")
+    a = a.contiguous()
+    w = w.contiguous()
+    idx = idx.to(torch.int32).contiguous()
+    y = torch.empty(B, NT, Co, device=a.device, dtype=a.dtype)
+    if B == 0 or NT == 0:
+        return y
+    epi = _lib.BPC_EPILOGUE_STORE
+    sp = hp = None
+    if scale is not None:
+        epi = _lib.BPC_EPILOGUE_AFFINE_SILU
+        scale = scale.to(a.device, torch.float32).contiguous()
+        shift = shift.to(a.device, torch.float32).contiguous()
+        sp, hp = scale.data_ptr(), shift.data_ptr()
+    rc = _lib.lib().bpc_gather_mm_fwd_ex(a.data_ptr(), w.data_ptr(), idx.data_ptr(), y.data_ptr(), B, NS, NT, K, Ci,
+                                         Co, n_w, split, epi, sp, hp, _DTYPES[a.dtype], _stream_ptr(a.device))
+    _lib.check(rc, "bpc_gather_mm_fwd_ex")
+    return y
+
+
+def residual_affine_silu(h: torch.Tensor, u: torch.Tensor | None, scale_h: float, scale_u: float,
+                         a: torch.Tensor | None = None, b: torch.Tensor | None = None, want_out: bool = True):
+    """One pass over an fp32 (..., H) stream (C ABI bpc_residual_affine_silu): v = scale_h h + scale_u u (u bf16 or
+    None) -> (v fp32 or None, SiLU(a v + b) bf16 or None)."""
+    _check_cuda(h)
+    if h.dtype != torch.float32 or (u is not None and (u.dtype != torch.bfloat16 or u.shape != h.shape)):
+        raise TypeError("residual_affine_silu: h fp32, u bf16 of h's shape")
+    h = h.contiguous()
+    H = h.shape[-1]
+    rows = h.numel() // H
+    out = torch.empty_like(h) if want_out else None
+    x = torch.empty(h.shape, dtype=torch.bfloat16, device=h.device) if a is not None else None
+    u = u.contiguous() if u is not None else None
+    rc = _lib.lib().bpc_residual_affine_silu(
+        h.data_ptr(), u.data_ptr() if u is not None else None, out.data_ptr() if out is not None else None,
+        x.data_ptr() if x is not None else None, rows, H, float(scale_h), float(scale_u),
+        a.data_ptr() if a is not None else None, b.data_ptr() if b is not None else None, _stream_ptr(h.device))
+    _lib.check(rc, "bpc_residual_affine_silu")
+    return out, x
+
+
 def gmm_wgrad(x: torch.Tensor, gy: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
     """x (B, NS, C_in), gy (B, NT, C_out), idx (NT, K) -> dW (C_out, K C_in) fp32,
     dW[o, r C_in + i] = sum_{b, n} gy[b, n, o] x[b, idx[n, r], i] (cascade_triton.py:120-136)."""

@@ -51,6 +51,30 @@ BPC_API int bpc_last_error(char* buf, int len);
 BPC_API int bpc_gather_mm_fwd(const void* x, const void* w, const int32_t* idx, void* y, int64_t B, int32_t NS, int32_t NT,
                       int32_t K, int32_t Ci, int32_t Co, int32_t dtype, bpc_stream_t stream);
 
+/* Epilogues of bpc_gather_mm_fwd_ex. */
+enum { BPC_EPILOGUE_STORE = 0, BPC_EPILOGUE_AFFINE_SILU = 1 };
+
+/* bpc_gather_mm_fwd with two weight sets and an epilogue, for the layers around the op (no reference counterpart as
+ * one call; it computes what the reference's BipartiteConv / Block compose from several calls):
+ *   y[b, n, :] = epi( sum_r x[b, idx[n, r], :] W_{t(n), r}^T ),  t(n) = (n >= type_split), W = n_wtypes stacked
+ *   (Co, K*Ci) matrices; epi = identity (BPC_EPILOGUE_STORE) or c -> SiLU(scale[c] v + shift[c])
+ *   (BPC_EPILOGUE_AFFINE_SILU: an inference BatchNorm + SiLU; scale / shift fp32 (Co,) device vectors).
+ * The concatenation of the reference's per-type calls (cascade_net.py:228-233) is one call with n_wtypes = 2 when
+ * the targets are ordered by type. */
+BPC_API int bpc_gather_mm_fwd_ex(const void* x, const void* w, const int32_t* idx, void* y, int64_t B, int32_t NS,
+                                 int32_t NT, int32_t K, int32_t Ci, int32_t Co, int32_t n_wtypes, int32_t type_split,
+                                 int32_t epilogue, const float* scale, const float* shift, int32_t dtype,
+                                 bpc_stream_t stream);
+
+/* One memory-bound pass over a (rows, H) fp32 residual stream of the Cascade bottleneck block (no reference
+ * counterpart as one call; it replaces the casts, scale, add and activation torch runs between the reference Block's
+ * up projection and the next block's first BatchNorm, cascade_net.py:236-259):
+ *   v = scale_h h + scale_u u (u bf16 (rows, H), may be NULL);  out = v (fp32, may be NULL);
+ *   x = SiLU(a[c] v + b[c]) (bf16, may be NULL; a, b fp32 (H,): an inference BatchNorm folded to scale and shift).
+ * H % 8 == 0; every pointer 16-byte aligned. */
+BPC_API int bpc_residual_affine_silu(const float* h, const void* u, float* out, void* x, int64_t rows, int32_t H,
+                                     float scale_h, float scale_u, const float* a, const float* b, bpc_stream_t stream);
+
 /* Input gradient of bpc_gather_mm_fwd through the target table:
  *   gx[b, s, :] = sum_r gy[b, tgt[s, r], :] W_r,   tgt (NS, K) int32, NT (or any value outside [0, NT)) = none
  * gy (B, NT, Co), gx (B, NS, Ci), W (Co, K*Ci) as in the forward.  tgt[s, r] is the target that reads source s

@@ -12,6 +12,8 @@ What it restates:
                  the reference's _GatherMM.backward (cascade_net.py:155-171): the input gradient as the per-relation
                  sum gx[b, s] = sum_r gy[b, tgt[s, r]] W_r over the target table of the Triton backward
                  (cascade_triton.py:173-186), and the weight gradient gy^T gather(x) (cascade_triton.py:64-93).
+  cascade_block  the reference's bottleneck residual Block in eval mode (cascade_net.py:195-210,236-259): BatchNorm
+                 with running statistics, SiLU, bias-free down / up projections, the bipartite convolution, residual.
   bipartite_conv BipartiteConv.forward (cascade_net.py:228-233): check -> data for every data type, concatenated,
                  then data -> check for every check type.
   predecoder     the rotated-surface pre-decoder of codecoder_b200.params (embed, L x [c2d, GELU, residual;
@@ -94,6 +96,24 @@ def bipartite_conv(x, w_c2d, w_d2c, c2d, d2c):
     """check features (B, N_c, C) -> check features (B, N_c, C), linear (cascade_net.py:228-233)."""
     data = torch.cat([gather_mm(x, w, t) for w, t in zip(w_c2d, c2d)], 1)
     return torch.cat([gather_mm(data, w, t) for w, t in zip(w_d2c, d2c)], 1)
+
+
+def cascade_block(h, p: dict, c2d, d2c, L: int, res: str, eps: float = 1e-5, dtype=torch.float64):
+    """h (B, N, H) -> h' in eval mode.  p: bn{1,2,3}_{weight,bias,mean,var}, down (H/4, H), up (H, H/4), w_c2d
+    [(H/4, K H/4)] per data type, w_d2c [...] per check type (cascade_net.py:236-259)."""
+    t = {k: torch.as_tensor(np.asarray(v)).to(dtype) for k, v in p.items() if not k.startswith("w_")}
+    h = torch.as_tensor(np.asarray(h)).to(dtype)
+
+    def bn(x, i):
+        return (x - t[f"bn{i}_mean"]) / torch.sqrt(t[f"bn{i}_var"] + eps) * t[f"bn{i}_weight"] + t[f"bn{i}_bias"]
+
+    u = F.silu(bn(h, 1)) @ t["down"].t()
+    wc = [torch.as_tensor(np.asarray(w)).to(dtype) for w in p["w_c2d"]]
+    wd = [torch.as_tensor(np.asarray(w)).to(dtype) for w in p["w_d2c"]]
+    u = bipartite_conv(F.silu(bn(u, 2)), wc, wd, c2d, d2c)
+    u = F.silu(bn(u, 3)) @ t["up"].t()
+    scale = 1.0 / np.sqrt(2 * L)
+    return h + scale * u if res == "branch" else scale * h + u
 
 
 def _store(a: torch.Tensor, bf16: bool) -> torch.Tensor:

@@ -11,6 +11,9 @@ It imports the reference's bb.cascade_net (training/bb/ising_compare/bb/cascade_
                          (several channel widths, including C_in != C_out)
   predecoder_<cfg>.npz   the pre-decoder composed from the reference's gather_mm on seeded shots: det, logits,
                          residual (weights regenerate from the stored seed with codecoder_b200.params.init_params)
+  cascade_block_c14.npz  the reference's Block(512, Geometry('bb72'), L=14, res='skip') in eval mode with the C14
+                         network's block-0 weights (relation, down and up matrices rounded to bf16; BatchNorm in
+                         fp32) on a seeded bf16-valued input, and its output (fp32, CPU)
   gather_mm_bwd.npz      input and weight gradients from the reference's _GatherMM.backward (autograd through
                          cn.gather_mm, fp32, CPU) for seeded upstream gradients: rotated-surface steps at several
                          widths and BipartiteConv(128, Geometry('bb72')) with the C14 relation matrices (its
@@ -199,9 +202,34 @@ def make_backward():
     print("gather_mm_bwd", len(cases), "op cases + bb72 module")
 
 
+def make_cascade_block():
+    geo = cn.Geometry("bb72")
+    ck = torch.load(os.path.join(REF, "weights/cascade_bb72/C14.pt"), map_location="cpu", weights_only=False)
+    ema, cfg = ck["ema"], ck["cfg"]
+    blk = cn.Block(cfg["H"], geo, cfg["L"], res=cfg["res"], impl="torch")
+    sd = {k[len("blocks.0."):]: v for k, v in ema.items() if k.startswith("blocks.0.")}
+    for k in list(sd):
+        if k.startswith(("conv.", "down.", "up.")):
+            sd[k] = torch.as_tensor(round_bf16(sd[k].float().numpy()))
+    blk.load_state_dict(sd)
+    blk.eval()
+    rng = np.random.default_rng(1404)
+    h = torch.as_tensor(round_bf16(rng.standard_normal((1, geo.N, cfg["H"])).astype(np.float32)))
+    with torch.no_grad():
+        out = blk(h)
+    o = {"h_bf16": bf16_bits(h.numpy()), "out": out.numpy(), "H": cfg["H"], "L": cfg["L"], "res": cfg["res"],
+         "eps": blk.bn1.eps, "down_bf16": bf16_bits(sd["down.weight"].numpy()), "up_bf16": bf16_bits(sd["up.weight"].numpy())}
+    for i in (1, 2, 3):
+        for a, b in (("weight", "weight"), ("bias", "bias"), ("mean", "running_mean"), ("var", "running_var")):
+            o[f"bn{i}_{a}"] = sd[f"bn{i}.{b}"].float().numpy()
+    np.savez_compressed(os.path.join(HERE, "cascade_block_c14.npz"), **o)
+    print("cascade_block_c14", h.shape, float(out.abs().mean()))
+
+
 if __name__ == "__main__":
     torch.manual_seed(0)
     make_bb72()
     make_surface_gmm()
     make_predecoder()
     make_backward()
+    make_cascade_block()

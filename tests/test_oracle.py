@@ -113,3 +113,15 @@ def test_oracle_backward_matches_reference_module(bb72, bwd):
     assert _rel(x.grad.numpy(), bwd["bb72_gx"]) < 1e-5
     assert _rel(w[0].grad.numpy(), bwd["bb72_gw_c2d0"]) < 1e-5
     assert _rel(w[3].grad.numpy(), bwd["bb72_gw_d2c1"]) < 1e-5
+
+
+def test_oracle_cascade_block_matches_reference_c14(bb72, golden_dir):
+    z = dict(np.load(os.path.join(golden_dir, "cascade_block_c14.npz")))
+    p = {k: z[k] for k in z if k.startswith("bn")}
+    p["down"] = bf16_to_f32(z["down_bf16"])
+    p["up"] = bf16_to_f32(z["up_bf16"])
+    p["w_c2d"] = [bf16_to_f32(bb72["w_c2d_0_bf16"]), bf16_to_f32(bb72["w_c2d_1_bf16"])]
+    p["w_d2c"] = [bf16_to_f32(bb72["w_d2c_0_bf16"]), bf16_to_f32(bb72["w_d2c_1_bf16"])]
+    out = orc.cascade_block(bf16_to_f32(z["h_bf16"]), p, [bb72["c2d0"], bb72["c2d1"]], [bb72["d2c0"], bb72["d2c1"]],
+                            int(z["L"]), str(z["res"]), float(z["eps"]))
+    assert _rel(out.numpy(), z["out"]) < 1e-5
