@@ -8,6 +8,8 @@
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
+#include "bpc.h"
+
 namespace bpc {
 
 enum EpiMode : int {
@@ -102,6 +104,11 @@ int gmm_wgrad_launch(const void* x, const void* gy, const int32_t* idx, float* d
                      int64_t B, int32_t NS, int32_t NT, int32_t K, int32_t Ci, int32_t Co, int32_t dtype,
                      int* status, cudaStream_t stream);
 size_t gmm_wgrad_workspace(int64_t B, int32_t NT, int32_t K, int32_t Ci, int32_t Co, int32_t dtype);
+
+// The device tables and weights of a pre-decoder handle (predecoder.cu), for kernels built on the same model.
+int predecoder_internals(const struct bpc_predecoder* h, bpc_predecoder_config* cfg, const void** embed,
+                         const void** w_c2d, const void** w_d2c, const float** head_w, const float** head_b,
+                         const int32_t** c2d, const int32_t** d2c, const int32_t** xor_nbr);
 
 // Device status word of the stand-alone op entry points (bpc_gather_mm_*), one per device.
 int* op_status_ptr();

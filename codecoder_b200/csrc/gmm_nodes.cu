@@ -55,19 +55,6 @@ struct NodeArgs {
   uint32_t tmem_cols;
 };
 
-// TMA gather of 4 rows (row indices r0..r3, channels c0 .. c0 + 63 of a 2D tensor map with a one-row box) into 512
-// consecutive bytes of shared memory, in the map's swizzled layout; completion counted in bytes on `bar`.
-__device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap* map, int32_t c0, int32_t r0, int32_t r1,
-                                            int32_t r2, int32_t r3, uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(bar)
-      : "memory");
-}
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
 // barrier among the first `count` threads (warps 0-3) only
 __device__ __forceinline__ void named_bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
@@ -353,52 +340,6 @@ __global__ void __launch_bounds__(kNodeThreads, 1)
 constexpr int kSplitThreads = 128;
 constexpr int kSplitK = 8;
 
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ void cluster_arrive_release() {
-  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void cluster_wait_acquire() {
-  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-__device__ __forceinline__ uint32_t map_to_cta(uint32_t saddr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
-  return r;
-}
-// bulk copy of `bytes` (a multiple of 16) from this CTA's shared memory to another CTA's of the cluster, the bytes
-// counted on an mbarrier of the destination CTA
-__device__ __forceinline__ void bulk_s2cluster(uint32_t dst_cluster, uint32_t src, uint32_t bytes,
-                                               uint32_t bar_cluster) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          dst_cluster),
-      "r"(src), "r"(bytes), "r"(bar_cluster)
-      : "memory");
-}
-__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-// wait until the bulk copies this thread issued have finished reading their source
-__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
-// acquire side of the remote arrivals (cluster scope): a bounded wait like mbar_wait
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// byte offset of float4 chunk c (channels 4c .. 4c + 3) of row m (0..15) in receive slot r: rows of 16 chunks,
-// XOR-swizzled by row
-__device__ __forceinline__ uint32_t recv_off(int r, int m, int c) {
-  return static_cast<uint32_t>(r * (16 * 256) + m * 256 + ((c ^ (m & 15)) << 4));
-}
 
 template <int EPI, bool HEAD>
 __global__ void __launch_bounds__(kSplitThreads, 1)

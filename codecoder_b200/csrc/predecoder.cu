@@ -404,6 +404,25 @@ extern "C" int bpc_predecoder_forward(bpc_predecoder* h, const uint8_t* det, flo
   return 0;
 }
 
+namespace bpc {
+int predecoder_internals(const bpc_predecoder* h, bpc_predecoder_config* cfg, const void** embed, const void** w_c2d,
+                         const void** w_d2c, const float** head_w, const float** head_b, const int32_t** c2d,
+                         const int32_t** d2c, const int32_t** xor_nbr) {
+  if (!h) return fail(BPC_ERR_ARG, "null pre-decoder");
+  if (!h->weights_set) return fail(BPC_ERR_ARG, "pre-decoder without weights");
+  *cfg = h->cfg;
+  *embed = h->embed;
+  *w_c2d = h->w_c2d;
+  *w_d2c = h->w_d2c;
+  *head_w = h->head_w;
+  *head_b = h->head_b;
+  *c2d = h->c2d;
+  *d2c = h->d2c;
+  *xor_nbr = h->xor_nbr;
+  return 0;
+}
+}  // namespace bpc
+
 extern "C" int bpc_predecoder_record_step_events(bpc_predecoder* h, void* const* events, int n_pairs) {
   if (!h || n_pairs < 0 || (n_pairs > 0 && !events)) return fail(BPC_ERR_ARG, "invalid event list");
   h->step_events.assign(reinterpret_cast<cudaEvent_t const*>(events),

@@ -74,8 +74,8 @@ class StreamingDecoder:
                 with torch.cuda.graph(g, stream=self.stream):
                     self._work(src)
                 self.graphs.append(g)
+            self.stream.synchronize()            # this stream only: a resident kernel may run on another
         self.cur = 0
-        torch.cuda.synchronize(self.device)
 
     def reset(self):
         with torch.cuda.device(self.device):
@@ -107,3 +107,82 @@ class StreamingDecoder:
             if i >= warmup:
                 out.append((time.perf_counter() - t0) * 1e6)
         return np.asarray(out)
+
+
+class PersistentStreamingDecoder:
+    """The same sliding-window decoder served by one resident kernel (C ABI bpc_stream_*): rounds go in and results
+    come out through a request line in mapped host memory, no launch per round.  bf16 networks with C = 64 and K = 8
+    (the d = 17 streaming workload); the kernel occupies 64 SMs while it runs and leaves after `idle_timeout_ms`
+    without a request, on stop(), or when a wait inside a round exceeds its watchdog.  Same bits as StreamingDecoder
+    (whose small-batch steps run the same relation-split arithmetic).  While it runs nothing may synchronise the
+    whole device (torch.cuda.synchronize() would wait for the resident kernel until its idle limit): synchronise
+    streams or events instead."""
+
+    def __init__(self, d: int, window: int, cfg, params, device="cuda", idle_timeout_ms: int = 5000):
+        import ctypes
+        from . import _lib
+        self.geo = g = RotatedSurface(d, window)
+        self.pd = PreDecoder(g, cfg, params, device=device, chunk_shots=256)
+        self.device = self.pd.device
+        self.W, self.nh, self.nq = window, g.nh, g.n_data_round
+        h = ctypes.c_void_p()
+        _lib.check(_lib.lib().bpc_stream_create(self.pd._h, window, g.nh, g.n_data_round, int(idle_timeout_ms),
+                                                ctypes.byref(h)), "bpc_stream_create")
+        self._s = h
+        self.residual = np.zeros(g.N_c, np.uint8)
+        self.logits = np.zeros((self.nq, 2), np.float32)
+        self.running = False
+
+    def start(self):
+        from . import _lib
+        with torch.cuda.device(self.device):
+            _lib.check(_lib.lib().bpc_stream_start(self._s), "bpc_stream_start")
+        self.running = True
+
+    def step(self, new_round: np.ndarray, timeout_us: int = 2_000_000):
+        """new_round (2 nh,) uint8 -> (residual (N_c,) uint8, newest-round logits (nq, 2) fp32), host arrays valid
+        until the next step."""
+        from . import _lib
+        if not self.running:
+            self.start()
+        r = np.ascontiguousarray(new_round, np.uint8)
+        _lib.check(_lib.lib().bpc_stream_round(self._s, r.ctypes.data, self.residual.ctypes.data,
+                                               self.logits.ctypes.data, int(timeout_us)), "bpc_stream_round")
+        return self.residual, self.logits
+
+    def latency(self, rounds: np.ndarray, warmup: int = 100, timeout_us: int = 2_000_000):
+        """Per-round latency in microseconds (host wall clock in the library's own loop, from writing the request to
+        reading the response) for rounds (R, 2 nh) uint8 -> np.ndarray (R - warmup,)."""
+        from . import _lib
+        if not self.running:
+            self.start()
+        rounds = np.ascontiguousarray(rounds, np.uint8)
+        lat = np.zeros(len(rounds), np.int64)
+        _lib.check(_lib.lib().bpc_stream_run(self._s, rounds.ctypes.data, len(rounds), None, None, lat.ctypes.data,
+                                             int(timeout_us)), "bpc_stream_run")
+        return lat[warmup:] / 1000.0
+
+    def status(self) -> int:
+        from . import _lib
+        return int(_lib.lib().bpc_stream_status(self._s))
+
+    def stop(self):
+        from . import _lib
+        if self.running:
+            self.running = False
+            _lib.check(_lib.lib().bpc_stream_stop(self._s), "bpc_stream_stop")
+
+    def close(self):
+        from . import _lib
+        if getattr(self, "_s", None):
+            try:
+                self.stop()
+            finally:
+                _lib.lib().bpc_stream_destroy(self._s)
+                self._s = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

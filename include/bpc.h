@@ -168,6 +168,37 @@ BPC_API void bpc_predecoder_destroy(bpc_predecoder* h);
 BPC_API int bpc_predecoder_forward_noalloc(bpc_predecoder* h, const uint8_t* det, float* logits, uint8_t* residual,
                                            int64_t B, bpc_stream_t stream);
 
+/* ------------------------------------------------------------------------------------------------------------
+ * Persistent streaming pre-decoder (sliding window of `window` rounds, batch 1): one resident kernel serves rounds
+ * through a request line in mapped host memory -- the reference's persistent-kernel protocol
+ * (evaluation/timing/d7/router.cc:170-223,576-650, kernel.cu:310-369,440-527; s9_pers_*): a tagged request with
+ * the round's detectors, a response with the same tag, a stop command, and watchdogs (an idle limit while waiting
+ * for requests, a step limit on every wait inside a round) that end the kernel with a status instead of a hang.
+ * Served networks: bf16, C = 64, K = 8, at most 8 layers, at most 8 tiles of 128 nodes per step (d = 17 with a
+ * window of 3 rounds is 7 and 8).  The kernel occupies 64 SMs while it runs. */
+typedef struct bpc_stream bpc_stream;
+
+/* The pre-decoder's tables and weights (device, not copied: keep h alive), the window and the detectors (nh per
+ * check type) and data qubits (nq) per round.  Allocates the device state and the mapped lines. */
+BPC_API int bpc_stream_create(const bpc_predecoder* h, int32_t window, int32_t nh, int32_t nq, int32_t idle_timeout_ms,
+                              bpc_stream** out);
+/* Launches the resident kernel on the handle's own non-blocking stream and waits for it to report ready. */
+BPC_API int bpc_stream_start(bpc_stream* s);
+/* One round: round_dets (2 nh) host bytes, this round's X then Z detectors -> residual (N_c bytes) of the window and
+ * logits (nq x 2 fp32) of the newest round, host buffers (either may be NULL).  Spins on the response tag for at most
+ * timeout_us (<= 0: no limit besides the kernel's own watchdogs). */
+BPC_API int bpc_stream_round(bpc_stream* s, const uint8_t* round_dets, uint8_t* residual, float* logits,
+                             int64_t timeout_us);
+/* n_rounds rounds in a row (rounds: n_rounds x 2 nh bytes); per-round results and the host wall-clock latency of
+ * each round in ns (each output may be NULL). */
+BPC_API int bpc_stream_run(bpc_stream* s, const uint8_t* rounds, int64_t n_rounds, uint8_t* residuals, float* logits,
+                           int64_t* latency_ns, int64_t timeout_us);
+/* Sends the stop command and waits (bounded) for the kernel to leave. */
+BPC_API int bpc_stream_stop(bpc_stream* s);
+/* The kernel's status word: 0 starting, 1 ready / serving, 2 stopped, 3 watchdog fired, 4 idle limit reached. */
+BPC_API int bpc_stream_status(const bpc_stream* s);
+BPC_API void bpc_stream_destroy(bpc_stream* s);
+
 /* Size in bytes of the scratch array bpc_predecoder_forward_noalloc runs on. */
 BPC_API size_t bpc_noalloc_scratch_bytes(void);
 

@@ -38,3 +38,29 @@ def test_streaming_latency_is_measured():
     lat = sd.latency(sample_stream(RotatedSurface(cfg.d, 1), cfg.p, 300, 34), warmup=50)
     assert len(lat) == 250 and np.all(lat > 0)
     print("d17 window-3 per-round latency us p50 %.1f p99 %.1f" % (np.percentile(lat, 50), np.percentile(lat, 99)))
+
+
+@pytest.mark.parametrize("d", [9, 17])
+def test_persistent_stream_matches_graph_stream(d):
+    """The resident kernel (mapped request line) gives the graph-replay decoder's bits round after round."""
+    from codecoder_b200.streaming import PersistentStreamingDecoder
+    cfg = replace(CONFIGS["d17_stream"], d=d)
+    params = init_params(cfg, 41)
+    stream = sample_stream(RotatedSurface(d, 1), 0.02, 12, 42)
+    ref = StreamingDecoder(d, cfg.rounds, cfg, params, device="cuda")
+    ref.capture()                          # before the resident kernel starts: capture synchronises
+    ps = PersistentStreamingDecoder(d, cfg.rounds, cfg, params, device="cuda")
+    try:
+        ps.start()
+        for t in range(len(stream)):
+            r_res, r_lg = ref.step(stream[t])
+            p_res, p_lg = ps.step(stream[t])
+            assert np.array_equal(p_res, r_res.numpy()), t
+            assert np.array_equal(p_lg, r_lg.numpy()), t
+        lat = ps.latency(sample_stream(RotatedSurface(d, 1), cfg.p, 400, 43), warmup=100)
+        print("persistent d%d window-3 per-round latency us p50 %.1f p99 %.1f" %
+              (d, np.percentile(lat, 50), np.percentile(lat, 99)))
+        ps.stop()
+        assert ps.status() == 2
+    finally:
+        ps.close()
