@@ -64,3 +64,27 @@ def test_persistent_stream_matches_graph_stream(d):
         assert ps.status() == 2
     finally:
         ps.close()
+
+
+def test_persistent_stream_idle_watchdog_leaves_a_usable_context():
+    """No request within the idle limit: the kernel leaves by itself with status 4; a round afterwards is an error,
+    not a hang, and the device keeps working."""
+    import time
+    from codecoder_b200.sampler import sample
+    from codecoder_b200.streaming import PersistentStreamingDecoder
+    cfg = replace(CONFIGS["d17_stream"], d=9)
+    params = init_params(cfg, 5)
+    ps = PersistentStreamingDecoder(9, cfg.rounds, cfg, params, device="cuda", idle_timeout_ms=200)
+    try:
+        ps.start()
+        time.sleep(1.0)
+        assert ps.status() == 4
+        with pytest.raises(RuntimeError):
+            ps.step(np.zeros(2 * ps.nh, np.uint8), timeout_us=200_000)
+    finally:
+        ps.close()
+    g = RotatedSurface(9, cfg.rounds)
+    det, _ = sample(g, 0.02, 8, 6)
+    lg, rs = PreDecoder(g, cfg, params, device="cuda")(torch.as_tensor(det).cuda())
+    torch.cuda.synchronize()
+    assert torch.isfinite(lg).all()
