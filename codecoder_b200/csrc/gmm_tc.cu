@@ -448,6 +448,357 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// Wide-tile kernel: blocked layout, C_in = C_out = 128 (the pre-decoder's hidden-128 networks).
+//
+// The MMA rows are the 128 output channels and its columns the tile's 256 shots: one tcgen05.mma M=128 N=256 K=16
+// per 16 input channels, W_r's 64-channel stage (the same TMA box as above) as the K-major 128-byte-swizzled A
+// operand and the blocked activation stage as the K-major no-swizzle B operand.  The tensor pipe takes a 256-column
+// MMA at its full rate, while 128-column MMAs cost more than their share per instruction (measured on B200 with
+// one issuing thread: M128 N128 K16 80-100 cycles each against 64, M128 N256 K16 at 128 when eight are committed
+// together, 143 when four are).  So the two stages of one relation are freed by one commit after its eight MMAs.
+//
+// The accumulator rows are channels.  Each epilogue warp owns one TMEM lane quarter (32 channels) and one half of
+// the tile's shots; it reads 16 shot columns at a time (tcgen05.ld 32x32b.x16), turns them around through a 2 KB
+// scratch of its own (row = channel, 16-byte chunks swizzled: conflict-free stores and loads) so that each thread
+// holds 16 channels of one shot, and then runs the row kernel's element arithmetic (same bits).  With the head,
+// the logits of a shot need all 128 channels: after every warp has stored its part of the tile (an mbarrier of
+// 256 arrivals, waited with the watchdog), each warp reads 32 shots' rows back and forms the logits, threshold and
+// residual XOR exactly as the row kernel does.
+constexpr int kWideShots = 256;                       // tile shots = MMA N
+constexpr int kWideC = 128;                           // C_in = C_out = MMA M
+constexpr uint32_t kWideXBytes = kWideShots * 64 * 2;   // one 64-channel activation stage (8 channel groups)
+constexpr uint32_t kWideWBytes = kWideC * 128;          // W_r rows x 64 channels
+constexpr uint32_t kWideStageBytes = kWideXBytes + kWideWBytes;
+constexpr int kWideStages = 4;                        // two relation slots of two 64-channel stages
+constexpr int kWideScratch = 2048;                    // per epilogue warp: 32 channels x 16 shots fp32
+constexpr int kWideBars = kWideStages + 2 + 2 + 2 + 1 + 2 * kRing + 2;
+
+__host__ __device__ constexpr int wide_smem_bytes() {
+  return 1024 + kWideStages * kWideStageBytes + kEpiWarps * kWideScratch + kWideBars * 8 + kRing * 16 + 16;
+}
+
+// fp32 scratch element (channel row c of the warp's quarter, shot column s of the 16-shot piece), in bytes
+__device__ __forceinline__ uint32_t wide_scr_off(int c, int s) {
+  return static_cast<uint32_t>((c ^ ((c >> 4) & 1)) * 64 + (((s >> 2) ^ ((c >> 1) & 3)) << 4) + (s & 3) * 4);
+}
+
+template <int EPI, bool HEAD>
+__global__ void __launch_bounds__(kThreads, 1)
+    gmm_wide_kernel(const __grid_constant__ CUtensorMap tmW, const TcArgs a) {
+  constexpr int kCgElems = kWideShots * 8;            // one channel group of a tile (elements)
+  constexpr bool kResid = EPI == kEpiGeluResid;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* scratch = smem + kWideStages * kWideStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(scratch + kEpiWarps * kWideScratch);
+  uint64_t* full = bars;                              // per stage
+  uint64_t* empty = bars + kWideStages;               // per relation slot
+  uint64_t* accf = empty + 2;
+  uint64_t* acce = accf + 2;
+  uint64_t* drain = acce + 2;
+  uint64_t* tfull = drain + 1;
+  uint64_t* tempty = tfull + kRing;
+  uint64_t* stored = tempty + kRing;                  // head: the tile's outputs are all stored (per accumulator)
+  volatile RingEntry* ring = reinterpret_cast<volatile RingEntry*>(bars + kWideBars);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(bars + kWideBars) + kRing * 16);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kWideStages; ++i) mbar_init(smem_u32(&full[i]), 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_u32(&empty[i]), 1);
+      mbar_init(smem_u32(&accf[i]), 1);
+      mbar_init(smem_u32(&acce[i]), kEpiWarps);
+      mbar_init(smem_u32(&stored[i]), kEpiWarps * 32);
+    }
+    for (int i = 0; i < kRing; ++i) {
+      mbar_init(smem_u32(&tfull[i]), 1);
+      mbar_init(smem_u32(&tempty[i]), 1 + kEpiWarps);
+    }
+    mbar_init(smem_u32(drain), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmW);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ producer
+    if (lane == 0) {
+      int slot = 0;
+      uint32_t sphase = 0;
+      uint32_t armed = 0, armed_parity = 0;
+      int rslot = 0;
+      uint32_t rphase = 0;
+      bool ok = true;
+      long long next = a.tile_counter ? atomicAdd(a.tile_counter, 1ull) : static_cast<long long>(blockIdx.x);
+      TileRow nrow;
+      issue_row(a, next < a.num_tiles ? next : 0, nrow);
+      while (ok) {
+        const long long tile = next;
+        finish_row(a, nrow);
+        const TileRow cur = nrow;
+        if (!mbar_wait(smem_u32(&tempty[rslot]), rphase ^ 1u, abort_flag, a.status, a.timeout_ns)) break;
+        ring[rslot].tile = tile < a.num_tiles ? tile : -1;
+        ring[rslot].n = cur.n;
+        ring[rslot].vm = cur.vm;
+        mbar_arrive(smem_u32(&tfull[rslot]));
+        if (++rslot == kRing) {
+          rslot = 0;
+          rphase ^= 1u;
+        }
+        if (tile >= a.num_tiles) break;
+        next = a.tile_counter ? atomicAdd(a.tile_counter, 1ull) : tile + gridDim.x;
+        issue_row(a, next < a.num_tiles ? next : tile, nrow);
+        const int64_t s0 = (tile / a.NT) * kWideShots;
+        const int wrow = (cur.n >= a.type_split) ? kWideC : 0;
+#pragma unroll 1
+        for (int r = 0; r < a.K; ++r) {
+          if (!(cur.vm & (1u << r))) continue;
+          if (!mbar_wait(smem_u32(&empty[slot]), sphase ^ 1u, abort_flag, a.status, a.timeout_ns)) {
+            ok = false;
+            break;
+          }
+          const __nv_bfloat16* xs = a.x + static_cast<int64_t>(cur.src[r]) * a.x_node_stride + s0 * kWideC;
+#pragma unroll
+          for (int kb = 0; kb < 2; ++kb) {
+            const int st = slot * 2 + kb;
+            const uint32_t sa = smem_u32(smem + st * kWideStageBytes);
+            const uint32_t fb = smem_u32(&full[st]);
+            mbar_arrive_expect_tx(fb, kWideStageBytes);
+            bulk_load(sa, xs + kb * 8 * kCgElems, kWideXBytes, fb);
+            tma_load_3d(sa + kWideXBytes, &tmW, kb * kKBlock, r, wrow, fb);
+            armed |= 1u << st;
+            armed_parity = (armed_parity & ~(1u << st)) | (sphase << st);
+          }
+          slot ^= 1;
+          if (slot == 0) sphase ^= 1u;
+        }
+      }
+      if (!ok) {
+        for (int i = 0; i < kWideStages; ++i)
+          if (armed & (1u << i)) {
+            const uint32_t par = (armed_parity >> i) & 1u;
+            const uint64_t t0 = globaltimer_ns();
+            while (!mbar_try_wait(smem_u32(&full[i]), par) && globaltimer_ns() - t0 < a.timeout_ns) {
+            }
+          }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(kWideC, kWideShots);
+      int slot = 0;
+      uint32_t sphase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      int rslot = 0;
+      uint32_t rphase = 0;
+      bool ok = true;
+      while (ok) {
+        if (!mbar_wait(smem_u32(&tfull[rslot]), rphase, abort_flag, a.status, a.timeout_ns)) break;
+        const long long tile = ring[rslot].tile;
+        const uint32_t vm = ring[rslot].vm;
+        mbar_arrive(smem_u32(&tempty[rslot]));
+        if (++rslot == kRing) {
+          rslot = 0;
+          rphase ^= 1u;
+        }
+        if (tile < 0) break;
+        if (!mbar_wait(smem_u32(&acce[acc]), acc_phase ^ 1u, abort_flag, a.status, a.timeout_ns)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kWideShots);
+        uint32_t accumulate = 0;
+#pragma unroll 1
+        for (int r = 0; r < a.K && ok; ++r) {
+          if (!(vm & (1u << r))) continue;
+#pragma unroll
+          for (int kb = 0; kb < 2; ++kb) {
+            const int st = slot * 2 + kb;
+            if (!mbar_wait(smem_u32(&full[st]), sphase, abort_flag, a.status, a.timeout_ns)) {
+              ok = false;
+              break;
+            }
+            const uint32_t sa = smem_u32(smem + st * kWideStageBytes);
+            const uint64_t ad0 = sdesc_k_sw128(sa + kWideXBytes);
+            const uint64_t bd0 = sdesc_k_none(sa, kCgElems * 2, 128);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              tc_mma_ss(d_tmem, ad0 + static_cast<uint64_t>((k * 32) >> 4),
+                        bd0 + static_cast<uint64_t>((2 * k * kCgElems * 2) >> 4), idesc, accumulate);
+              accumulate = 1;
+            }
+          }
+          if (!ok) break;
+          tc_commit(smem_u32(&empty[slot]));      // both stages of the relation, once its eight MMAs have read them
+          slot ^= 1;
+          if (slot == 0) sphase ^= 1u;
+        }
+        if (!ok) break;
+        tc_commit(smem_u32(&accf[acc]));
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      tc_commit(smem_u32(drain));
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(smem_u32(drain), 0) && globaltimer_ns() - t0 < a.timeout_ns) {
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (warps 2..9)
+    const int q = warp & 3;                   // TMEM lane quarter: channels 32 q .. 32 q + 31
+    const int e = warp - 2;
+    const int half = e >> 2;                  // tile shots 128 half .. 128 half + 127
+    const int s = lane & 15;                  // after the turn-around: shot s of the 16-shot piece ...
+    const int h = lane >> 4;                  // ... channels 32 q + 16 h .. + 15 (channel groups 4 q + 2 h, + 1)
+    const int cg0 = 4 * q + 2 * h;
+    uint8_t* scr = scratch + e * kWideScratch;
+    const uint32_t scr_u = smem_u32(scr);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    int rslot = 0;
+    uint32_t rphase = 0;
+    // every wait is decided for the whole warp (a watchdog timeout seen by some lanes ends the loop for all, so no
+    // lane is left in a warp-collective instruction)
+    while (true) {
+      if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&tfull[rslot]), rphase, abort_flag, a.status, a.timeout_ns)))
+        break;
+      const long long tile = ring[rslot].tile;
+      const int n = ring[rslot].n;
+      const uint32_t vm = ring[rslot].vm;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&tempty[rslot]));
+      if (++rslot == kRing) {
+        rslot = 0;
+        rphase ^= 1u;
+      }
+      if (tile < 0) break;
+      const int64_t s0 = (tile / a.NT) * kWideShots;
+      __nv_bfloat16* yt = reinterpret_cast<__nv_bfloat16*>(a.y) + static_cast<int64_t>(n) * a.y_node_stride + s0 * kWideC;
+      // this thread's two 16-byte chunks of piece j: shot 128 half + 16 j + s, channel groups cg0, cg0 + 1
+      __nv_bfloat16* yc = yt + cg0 * kCgElems + (128 * half + s) * 8;
+      uint4 rb[kResid ? 8 : 1][2];
+      if (kResid) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (s0 + 128 * half + 16 * j + s < a.shots) {
+            rb[j][0] = *reinterpret_cast<const uint4*>(yc + j * 128);
+            rb[j][1] = *reinterpret_cast<const uint4*>(yc + j * 128 + kCgElems);
+          }
+      }
+      if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&accf[acc]), acc_phase, abort_flag, a.status, a.timeout_ns)))
+        break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                             static_cast<uint32_t>(acc * kWideShots + 128 * half);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float v[16];
+        if (vm) {
+          tmem_ld16(taddr + 16 * j, v);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[i] = 0.f;
+        }
+        if (j == 7) {                         // the accumulator buffer is free for the next tile's MMAs
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_u32(&acce[acc]));
+        }
+        // turn around: row = channel (this lane), 16 shot columns -> this thread: shot s, 16 channels
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4)
+          asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(scr_u + wide_scr_off(lane, 4 * c4)),
+                       "f"(v[4 * c4]), "f"(v[4 * c4 + 1]), "f"(v[4 * c4 + 2]), "f"(v[4 * c4 + 3])
+                       : "memory");
+        __syncwarp();
+        float x[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k)
+          asm volatile("ld.shared.f32 %0, [%1];" : "=f"(x[k]) : "r"(scr_u + wide_scr_off(16 * h + k, s)) : "memory");
+        __syncwarp();
+        const bool ok = s0 + 128 * half + 16 * j + s < a.shots;
+        if (ok) {
+#pragma unroll
+          for (int g = 0; g < 2; ++g) {
+            uint4 u;
+            uint32_t* o = reinterpret_cast<uint32_t*>(&u);
+            const uint32_t* hr = reinterpret_cast<const uint32_t*>(&rb[kResid ? j : 0][g]);
+#pragma unroll
+            for (int e4 = 0; e4 < 4; ++e4) {
+              uint64_t xx = gelu_tanh_fast2(f2_pack(x[8 * g + 2 * e4], x[8 * g + 2 * e4 + 1]));
+              if (kResid) xx = f2_add(xx, bf2_to_f2(hr[e4]));
+              o[e4] = f2_to_bf2(xx);
+            }
+            *reinterpret_cast<uint4*>(yc + j * 128 + g * kCgElems) = u;
+          }
+        }
+      }
+      if (HEAD) {
+        // every warp's part of the tile is stored: read 32 shots' rows back and form the logits in the row kernel's
+        // order (channel pairs, four 32-channel chunks, stored bf16 values)
+        mbar_arrive(smem_u32(&stored[acc]));
+        if (!__all_sync(0xffffffffu,
+                        mbar_wait(smem_u32(&stored[acc]), acc_phase, abort_flag, a.status, a.timeout_ns)))
+          break;
+        const int sl = 32 * e + lane;
+        const bool ok = s0 + sl < a.shots;
+        uint64_t lg0 = 0, lg1 = 0;
+#pragma unroll
+        for (int cg = 0; cg < 16; ++cg) {
+          const uint4 u = *reinterpret_cast<const uint4*>(yt + cg * kCgElems + sl * 8);
+          const uint32_t* o = reinterpret_cast<const uint32_t*>(&u);
+#pragma unroll
+          for (int e4 = 0; e4 < 4; ++e4) {
+            const uint64_t f = bf2_to_f2(o[e4]);
+            const int col = cg * 8 + 2 * e4;
+            lg0 = f2_fma(f, *reinterpret_cast<const uint64_t*>(a.head.head_w + col), lg0);
+            lg1 = f2_fma(f, *reinterpret_cast<const uint64_t*>(a.head.head_w + kWideC + col), lg1);
+          }
+        }
+        const float l0 = f2_lo(lg0) + f2_hi(lg0) + __ldg(a.head.head_b);
+        const float l1 = f2_lo(lg1) + f2_hi(lg1) + __ldg(a.head.head_b + 1);
+        if (ok) {
+          float2* lp = reinterpret_cast<float2*>(a.head.logits + (s0 + sl) * a.head.lg_shot_stride +
+                                                 static_cast<int64_t>(n) * a.head.lg_node_stride);
+          *lp = make_float2(l0, l1);
+        }
+        if (a.head.res_bits) {
+          const uint32_t m0 = __ballot_sync(0xffffffffu, ok && l0 > 0.f);
+          const uint32_t m1 = __ballot_sync(0xffffffffu, ok && l1 > 0.f);
+          if (lane < 4) {
+            const int32_t c = __ldg(a.head.xor_nbr + static_cast<int64_t>(n) * 4 + lane);
+            const uint32_t msk = (lane >> 1) ? m1 : m0;
+            if (c >= 0 && msk)
+              atomicXor(a.head.res_bits + static_cast<int64_t>(c) * a.head.res_words + (s0 >> 5) + e, msk);
+          }
+        }
+      }
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
@@ -651,8 +1002,23 @@ int gmm_tc_launch(const GmmProblem& p, const GmmMaps& maps, int* status, uint64_
   uint32_t cols = 32;
   while (cols < static_cast<uint32_t>(2 * mt_for(p.Co) * p.Co)) cols <<= 1;
   a.tmem_cols = cols;
-  const int smem = smem_bytes_for(p.Co, a.stages);
   const bool head = p.head.head_w != nullptr;
+  if (p.blocked && p.Ci == kWideC && p.Co == kWideC && (p.epi == kEpiGeluInit || p.epi == kEpiGeluResid)) {
+    using WideFn = void (*)(CUtensorMap, TcArgs);
+    WideFn wf = p.epi == kEpiGeluInit ? (head ? &gmm_wide_kernel<kEpiGeluInit, true> : &gmm_wide_kernel<kEpiGeluInit, false>)
+                                      : (head ? &gmm_wide_kernel<kEpiGeluResid, true>
+                                              : &gmm_wide_kernel<kEpiGeluResid, false>);
+    constexpr int wsmem = wide_smem_bytes();
+    static_assert(wsmem <= kSmemLimit, "wide-tile kernel exceeds the shared memory per CTA");
+    if (int e = allow_smem(reinterpret_cast<const void*>(wf), wsmem)) return e;
+    const int64_t grid = std::min<int64_t>(a.num_tiles, num_sms());
+    void* args[] = {const_cast<CUtensorMap*>(&maps.w), &a};
+    cudaError_t le = cudaLaunchKernel(reinterpret_cast<const void*>(wf), dim3(static_cast<unsigned>(grid)),
+                                      dim3(kThreads), args, static_cast<size_t>(wsmem), stream);
+    if (le != cudaSuccess) return fail(4, std::string("gmm_wide_kernel launch: ") + cudaGetErrorString(le));
+    return 0;
+  }
+  const int smem = smem_bytes_for(p.Co, a.stages);
   KernelFn fn = select_kernel(p.Co, p.blocked, p.epi, head);
   if (!fn) return fail(2, "unsupported C_out / layout / epilogue combination for the tcgen05 path");
   if (int e = allow_smem(reinterpret_cast<const void*>(fn), kSmemLimit)) return e;

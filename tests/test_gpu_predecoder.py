@@ -148,3 +148,21 @@ def test_small_batch_node_tiles_match_shot_tiles(name, layers):
         assert torch.equal(small_lg, big_lg[:40]) and torch.equal(small_rs, big_rs[:40])
     else:
         assert orc.logit_error(small_lg.cpu().numpy(), big_lg[:40].cpu().numpy()) < 1e-2
+
+
+def test_d13_wide_tiles_match_node_tiles_bitwise():
+    """C = 128 passes of more than 64 shots run the wide-tile kernel (MMA rows = output channels, columns = the
+    tile's 256 shots); passes of at most 64 shots the node-tiled kernel.  Both use the same per-element arithmetic and
+    the same head order: every logit and residual bit agrees, over full and partial 256-shot tiles."""
+    cfg = replace(CONFIGS["d13_bf16"], layers=3)
+    g = RotatedSurface(cfg.d, cfg.rounds)
+    params = init_params(cfg, 909)
+    det, _ = sample(g, 0.02, 600, 910)
+    d = torch.as_tensor(det).to(DEV)
+    wide = PreDecoder(g, cfg, params, device=DEV, chunk_shots=16384)
+    node = PreDecoder(g, cfg, params, device=DEV, chunk_shots=64)
+    w_lg, w_rs = wide(d)
+    n_lg, n_rs = node(d)
+    torch.cuda.synchronize()
+    assert wide.status() == 0 and node.status() == 0
+    assert torch.equal(w_lg, n_lg) and torch.equal(w_rs, n_rs)
