@@ -472,7 +472,7 @@ constexpr uint32_t kWideWBytes = kWideC * 128;          // W_r rows x 64 channel
 constexpr uint32_t kWideStageBytes = kWideXBytes + kWideWBytes;
 constexpr int kWideStages = 4;                        // two relation slots of two 64-channel stages
 constexpr int kWideScratch = 2048;                    // per epilogue warp: 32 channels x 16 shots fp32
-constexpr int kWideBars = kWideStages + 2 + 2 + 2 + 1 + 2 * kRing + 2;
+constexpr int kWideBars = 2 * kWideStages + 2 + 2 + 1 + 2 * kRing + 2;
 
 __host__ __device__ constexpr int wide_smem_bytes() {
   return 1024 + kWideStages * kWideStageBytes + kEpiWarps * kWideScratch + kWideBars * 8 + kRing * 16 + 16;
@@ -493,8 +493,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* scratch = smem + kWideStages * kWideStageBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(scratch + kEpiWarps * kWideScratch);
   uint64_t* full = bars;                              // per stage
-  uint64_t* empty = bars + kWideStages;               // per relation slot
-  uint64_t* accf = empty + 2;
+  uint64_t* empty = bars + kWideStages;               // per stage
+  uint64_t* accf = empty + kWideStages;
   uint64_t* acce = accf + 2;
   uint64_t* drain = acce + 2;
   uint64_t* tfull = drain + 1;
@@ -508,9 +508,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kWideStages; ++i) mbar_init(smem_u32(&full[i]), 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kWideStages; ++i) {
+      mbar_init(smem_u32(&full[i]), 1);
       mbar_init(smem_u32(&empty[i]), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(smem_u32(&accf[i]), 1);
       mbar_init(smem_u32(&acce[i]), kEpiWarps);
       mbar_init(smem_u32(&stored[i]), kEpiWarps * 32);
@@ -566,14 +568,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
         for (int r = 0; r < a.K; ++r) {
           if (!(cur.vm & (1u << r))) continue;
-          if (!mbar_wait(smem_u32(&empty[slot]), sphase ^ 1u, abort_flag, a.status, a.timeout_ns)) {
-            ok = false;
-            break;
-          }
           const __nv_bfloat16* xs = a.x + static_cast<int64_t>(cur.src[r]) * a.x_node_stride + s0 * kWideC;
 #pragma unroll
           for (int kb = 0; kb < 2; ++kb) {
             const int st = slot * 2 + kb;
+            if (!mbar_wait(smem_u32(&empty[st]), sphase ^ 1u, abort_flag, a.status, a.timeout_ns)) {
+              ok = false;
+              break;
+            }
             const uint32_t sa = smem_u32(smem + st * kWideStageBytes);
             const uint32_t fb = smem_u32(&full[st]);
             mbar_arrive_expect_tx(fb, kWideStageBytes);
@@ -582,6 +584,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             armed |= 1u << st;
             armed_parity = (armed_parity & ~(1u << st)) | (sphase << st);
           }
+          if (!ok) break;
           slot ^= 1;
           if (slot == 0) sphase ^= 1u;
         }
@@ -640,9 +643,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         bd0 + static_cast<uint64_t>((2 * k * kCgElems * 2) >> 4), idesc, accumulate);
               accumulate = 1;
             }
+            tc_commit(smem_u32(&empty[st]));      // the stage is free once its four MMAs have read it
           }
           if (!ok) break;
-          tc_commit(smem_u32(&empty[slot]));      // both stages of the relation, once its eight MMAs have read them
           slot ^= 1;
           if (slot == 0) sphase ^= 1u;
         }
