@@ -283,7 +283,8 @@ def main():
     pk = peaks()
     achieved = tc_flops / (tc_ms / 1000.0) / 1e12
     fps = flops_per_shot(cfg, g.N_c, g.N_d)
-    roof = {"bound": "tensor", "kernel": "gmm_tc_kernel (bipartite step)", "achieved": achieved,
+    step_kernel = "gmm_wide_kernel" if cfg.channels == 128 else "gmm_tc_kernel"
+    roof = {"bound": "tensor", "kernel": f"{step_kernel} (bipartite step)", "achieved": achieved,
             "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s", "frac": achieved / pk["bf16_tflops_sustained"],
             "peak_kind": f"{pk['source']} sustained bf16 (cuBLAS)", "traffic": None,
             "avg_launch_ms": tc_ms / len(step_ms), "launches": len(step_ms),
