@@ -13,6 +13,7 @@ BPC_DTYPE_F32 = 0
 BPC_DTYPE_BF16 = 1
 BPC_EPILOGUE_STORE = 0
 BPC_EPILOGUE_AFFINE_SILU = 1
+BPC_EPILOGUE_ADD = 2
 
 c_i32 = ctypes.c_int32
 c_i64 = ctypes.c_int64
@@ -34,8 +35,12 @@ SIGNATURES = {
                                             c_i32, c_i32, c_vp, c_vp, c_i32, c_vp]),
     "bpc_residual_affine_silu": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, ctypes.c_float, ctypes.c_float,
                                                 c_vp, c_vp, c_vp]),
+    "bpc_gelu_residual_fwd": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_i32, c_i32, c_vp]),
+    "bpc_gelu_residual_bwd": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_i32, c_i32, c_vp]),
     "bpc_gather_mm_dgrad": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_i32, c_i32, c_i32,
                                            c_i32, c_vp]),
+    "bpc_gather_mm_dgrad_ex": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_i32, c_i32, c_i32,
+                                              c_i32, c_i32, c_vp]),
     "bpc_gather_mm_wgrad": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, ctypes.c_size_t, c_i64, c_i32, c_i32, c_i32,
                                            c_i32, c_i32, c_i32, c_vp]),
     "bpc_gather_mm_wgrad_workspace_size": (ctypes.c_size_t, [c_i64, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32]),

@@ -111,6 +111,8 @@ extern "C" int bpc_gather_mm_fwd_ex(const void* x, const void* w, const int32_t*
   } else if (epilogue == BPC_EPILOGUE_AFFINE_SILU) {
     epi = kEpiAffineSilu;
     if (!scale || !shift) return fail(BPC_ERR_ARG, "the affine + SiLU epilogue needs scale and shift");
+  } else if (epilogue == BPC_EPILOGUE_ADD) {
+    epi = kEpiAdd;
   } else {
     return fail(BPC_ERR_ARG, "unknown epilogue");
   }
@@ -128,6 +130,19 @@ extern "C" int bpc_gather_mm_dgrad(const void* gy, const void* w, const int32_t*
   if (int e = transpose_w_launch(w, w_t, K, Ci, Co, dtype, s)) return e;
   // gx = the forward over gy (B, NT, Co) with the target table and W' (Ci, K Co)
   return bpc_gather_mm_fwd(gy, w_t, tgt, gx, B, NT, NS, K, Co, Ci, dtype, stream);
+}
+
+extern "C" int bpc_gather_mm_dgrad_ex(const void* gy, const void* w, const int32_t* tgt, void* gx, void* w_t,
+                                      int64_t B, int32_t NT, int32_t NS, int32_t K, int32_t Ci, int32_t Co,
+                                      int32_t accumulate, int32_t dtype, bpc_stream_t stream) {
+  if (B < 0 || NS < 0 || NT < 1 || K < 1 || Ci < 1 || Co < 1) return fail(BPC_ERR_ARG, "invalid gather_mm shape");
+  if (dtype != BPC_DTYPE_BF16 && dtype != BPC_DTYPE_F32) return fail(BPC_ERR_ARG, "dtype must be bf16 or f32");
+  if (B == 0 || NS == 0) return 0;
+  if (!gy || !w || !tgt || !gx || !w_t) return fail(BPC_ERR_ARG, "null buffer");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (int e = transpose_w_launch(w, w_t, K, Ci, Co, dtype, s)) return e;
+  return run_gather_mm(gy, w_t, tgt, gx, B, NT, NS, K, Co, Ci, 1, NS, accumulate ? kEpiAdd : kEpiStore, nullptr,
+                       nullptr, dtype, stream);
 }
 
 extern "C" int bpc_gather_mm_wgrad(const void* x, const void* gy, const int32_t* idx, float* dw, void* workspace,

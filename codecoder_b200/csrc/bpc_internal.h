@@ -17,6 +17,7 @@ enum EpiMode : int {
   kEpiGeluInit = 1,   // y = GELU(acc)
   kEpiGeluResid = 2,  // y = y + GELU(acc)
   kEpiAffineSilu = 3, // y = SiLU(scale[c] acc + shift[c])  (an inference BatchNorm folded into scale / shift)
+  kEpiAdd = 4,        // y = y + acc  (row layouts: accumulate a second input gradient onto the first)
 };
 
 // Optional work fused into the epilogue of the last check -> data step of the pre-decoder.

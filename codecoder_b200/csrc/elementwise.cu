@@ -61,11 +61,225 @@ __global__ void __launch_bounds__(256) residual_affine_silu_kernel(const float* 
   }
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// The training network's residual steps around the op (one pass each, 8 channels per thread):
+//   forward   u = GELU(a) (rounded to bf16, as torch's gelu on bf16 does),  y = h + u
+//             h bf16 -> y bf16 (bf16 add, rounded);  h fp32 -> y fp32 and its bf16 copy (the next op's input);
+//             no h -> y = u
+//   backward  g = gy (+ gy16 for the fp32 stream: the gradient of the bf16 copy);  gh = g;
+//             ga = GELU'(a) * g   (g rounded to bf16 first on the fp32 stream, as autograd casts it for the add)
+// a and ga hold the pre-activations type-major: (T, B, NT / T, C), so that each target type's op output and input
+// gradient is one contiguous (B, NT / T, C) block; h, y, gy, gh are (B, NT, C).
+// GELU in the tanh form g(x) = x (1 + tanh(k (x + c x^3))) / 2, k = sqrt(2 / pi), c = 0.044715, with
+// g'(x) = (1 + t) / 2 + x (1 - t^2) k (1 + 3 c x^2) / 2, t = tanh(k (x + c x^3)); tanhf (accurate) in both.
+constexpr float kGeluK = 0.7978845608028654f;
+constexpr float kGeluC = 0.044715f;
+
+__device__ __forceinline__ float gelu_acc(float x) {
+  const float t = tanhf(kGeluK * fmaf(kGeluC * x, x * x, x));
+  return 0.5f * x * (1.0f + t);
+}
+__device__ __forceinline__ float gelu_grad(float x) {
+  const float t = tanhf(kGeluK * fmaf(kGeluC * x, x * x, x));
+  return 0.5f * (1.0f + t) + 0.5f * x * (1.0f - t * t) * kGeluK * fmaf(3.0f * kGeluC, x * x, 1.0f);
+}
+__device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+__device__ __forceinline__ uint32_t bf_pack(float lo, float hi) {
+  const __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&p);
+}
+__device__ __forceinline__ float bf_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+struct StepShape {
+  int64_t units;     // B * NT * C / 8
+  int64_t B;
+  int32_t NT, NTt, C8;
+};
+
+// offset (elements) of pre-activation unit u in the type-major (T, B, NT / T, C) layout
+__device__ __forceinline__ int64_t pre_off(const StepShape& sh, int64_t u) {
+  const int64_t row = u / sh.C8;
+  const int c8 = static_cast<int>(u - row * sh.C8);
+  const int64_t b = row / sh.NT;
+  const int n = static_cast<int>(row - b * sh.NT);
+  const int t = n / sh.NTt;
+  return ((t * sh.B + b) * sh.NTt + (n - t * sh.NTt)) * (8 * static_cast<int64_t>(sh.C8)) + 8 * c8;
+}
+
+// HMODE: 0 no h, 1 h bf16, 2 h fp32 (+ bf16 copy)
+template <int HMODE>
+__global__ void __launch_bounds__(256) gelu_residual_fwd_kernel(const __nv_bfloat16* __restrict__ a,
+                                                                const void* __restrict__ h, void* __restrict__ y,
+                                                                __nv_bfloat16* __restrict__ y16, StepShape sh) {
+  for (int64_t u = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; u < sh.units;
+       u += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint4 av = *reinterpret_cast<const uint4*>(a + pre_off(sh, u));
+    const uint32_t* aw = reinterpret_cast<const uint32_t*>(&av);
+    float g[8];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      g[2 * e] = bf_round(gelu_acc(bf_lo(aw[e])));
+      g[2 * e + 1] = bf_round(gelu_acc(bf_hi(aw[e])));
+    }
+    if (HMODE == 2) {
+      const float4 h0 = reinterpret_cast<const float4*>(h)[2 * u];
+      const float4 h1 = reinterpret_cast<const float4*>(h)[2 * u + 1];
+      const float v[8] = {h0.x + g[0], h0.y + g[1], h0.z + g[2], h0.w + g[3],
+                          h1.x + g[4], h1.y + g[5], h1.z + g[6], h1.w + g[7]};
+      reinterpret_cast<float4*>(y)[2 * u] = make_float4(v[0], v[1], v[2], v[3]);
+      reinterpret_cast<float4*>(y)[2 * u + 1] = make_float4(v[4], v[5], v[6], v[7]);
+      uint4 o;
+      o.x = bf_pack(v[0], v[1]);
+      o.y = bf_pack(v[2], v[3]);
+      o.z = bf_pack(v[4], v[5]);
+      o.w = bf_pack(v[6], v[7]);
+      reinterpret_cast<uint4*>(y16)[u] = o;
+    } else {
+      if (HMODE == 1) {
+        const uint4 hv = reinterpret_cast<const uint4*>(h)[u];
+        const uint32_t* hw = reinterpret_cast<const uint32_t*>(&hv);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          g[2 * e] += bf_lo(hw[e]);
+          g[2 * e + 1] += bf_hi(hw[e]);
+        }
+      }
+      uint4 o;
+      o.x = bf_pack(g[0], g[1]);
+      o.y = bf_pack(g[2], g[3]);
+      o.z = bf_pack(g[4], g[5]);
+      o.w = bf_pack(g[6], g[7]);
+      reinterpret_cast<uint4*>(y)[u] = o;
+    }
+  }
+}
+
+// F32: the fp32 stream (gy fp32, optional gy16 bf16, gh fp32); else the bf16 stream (gy bf16, gh unused: the
+// residual gradient is gy itself)
+template <bool F32>
+__global__ void __launch_bounds__(256) gelu_residual_bwd_kernel(const void* __restrict__ gy,
+                                                                const __nv_bfloat16* __restrict__ gy16,
+                                                                const __nv_bfloat16* __restrict__ a,
+                                                                float* __restrict__ gh,
+                                                                __nv_bfloat16* __restrict__ ga, StepShape sh) {
+  for (int64_t u = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; u < sh.units;
+       u += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float g[8];
+    if (F32) {
+      const float4 g0 = reinterpret_cast<const float4*>(gy)[2 * u];
+      const float4 g1 = reinterpret_cast<const float4*>(gy)[2 * u + 1];
+      g[0] = g0.x; g[1] = g0.y; g[2] = g0.z; g[3] = g0.w;
+      g[4] = g1.x; g[5] = g1.y; g[6] = g1.z; g[7] = g1.w;
+      if (gy16) {
+        const uint4 v = reinterpret_cast<const uint4*>(gy16)[u];
+        const uint32_t* w = reinterpret_cast<const uint32_t*>(&v);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          g[2 * e] += bf_lo(w[e]);
+          g[2 * e + 1] += bf_hi(w[e]);
+        }
+      }
+      if (gh) {
+        reinterpret_cast<float4*>(gh)[2 * u] = make_float4(g[0], g[1], g[2], g[3]);
+        reinterpret_cast<float4*>(gh)[2 * u + 1] = make_float4(g[4], g[5], g[6], g[7]);
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) g[e] = bf_round(g[e]);
+    } else {
+      const uint4 v = reinterpret_cast<const uint4*>(gy)[u];
+      const uint32_t* w = reinterpret_cast<const uint32_t*>(&v);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        g[2 * e] = bf_lo(w[e]);
+        g[2 * e + 1] = bf_hi(w[e]);
+      }
+    }
+    const int64_t po = pre_off(sh, u);
+    const uint4 av = *reinterpret_cast<const uint4*>(a + po);
+    const uint32_t* aw = reinterpret_cast<const uint32_t*>(&av);
+    uint4 o;
+    uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      ow[e] = bf_pack(g[2 * e] * gelu_grad(bf_lo(aw[e])), g[2 * e + 1] * gelu_grad(bf_hi(aw[e])));
+    *reinterpret_cast<uint4*>(ga + po) = o;
+  }
+}
+
+int step_shape(int64_t B, int32_t NT, int32_t C, int32_t n_types, StepShape* sh) {
+  if (B < 0 || NT < 1 || C < 8 || C % 8 || n_types < 1 || NT % n_types)
+    return fail(BPC_ERR_ARG, "B >= 0, NT a multiple of the type count, C a multiple of 8");
+  sh->B = B;
+  sh->NT = NT;
+  sh->NTt = NT / n_types;
+  sh->C8 = C / 8;
+  sh->units = B * NT * (C / 8);
+  return 0;
+}
+
+int elementwise_grid(int64_t units) {
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((units + 255) / 256, 8 * num_sms())));
+}
+
 }  // namespace
 
 }  // namespace bpc
 
 using namespace bpc;
+
+extern "C" int bpc_gelu_residual_fwd(const void* a, const void* h, void* y, void* y_bf16, int64_t B, int32_t NT,
+                                     int32_t C, int32_t n_types, int32_t h_dtype, bpc_stream_t stream) {
+  StepShape sh;
+  if (int e = step_shape(B, NT, C, n_types, &sh)) return e;
+  if (h && h_dtype != BPC_DTYPE_BF16 && h_dtype != BPC_DTYPE_F32) return fail(BPC_ERR_ARG, "h must be bf16 or f32");
+  const bool f32 = h && h_dtype == BPC_DTYPE_F32;
+  if (sh.units == 0) return 0;
+  if (!a || !y || (f32 && !y_bf16)) return fail(BPC_ERR_ARG, "null buffer");
+  if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(y) |
+       reinterpret_cast<uintptr_t>(y_bf16)) & 15)
+    return fail(BPC_ERR_ARG, "a, h, y and y_bf16 must be 16-byte aligned");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const auto* ab = static_cast<const __nv_bfloat16*>(a);
+  auto* yb = static_cast<__nv_bfloat16*>(y_bf16);
+  const int grid = elementwise_grid(sh.units);
+  if (!h)
+    gelu_residual_fwd_kernel<0><<<grid, 256, 0, s>>>(ab, h, y, yb, sh);
+  else if (!f32)
+    gelu_residual_fwd_kernel<1><<<grid, 256, 0, s>>>(ab, h, y, yb, sh);
+  else
+    gelu_residual_fwd_kernel<2><<<grid, 256, 0, s>>>(ab, h, y, yb, sh);
+  cudaError_t le = cudaGetLastError();
+  if (le != cudaSuccess) return fail(BPC_ERR_LAUNCH, std::string("gelu_residual_fwd_kernel launch: ") + cudaGetErrorString(le));
+  return 0;
+}
+
+extern "C" int bpc_gelu_residual_bwd(const void* gy, const void* gy_bf16, const void* a, void* gh, void* ga,
+                                     int64_t B, int32_t NT, int32_t C, int32_t n_types, int32_t gy_dtype,
+                                     bpc_stream_t stream) {
+  StepShape sh;
+  if (int e = step_shape(B, NT, C, n_types, &sh)) return e;
+  if (gy_dtype != BPC_DTYPE_BF16 && gy_dtype != BPC_DTYPE_F32) return fail(BPC_ERR_ARG, "gy must be bf16 or f32");
+  const bool f32 = gy_dtype == BPC_DTYPE_F32;
+  if (!f32 && (gy_bf16 || gh)) return fail(BPC_ERR_ARG, "the bf16 stream takes no second gradient and no gh");
+  if (sh.units == 0) return 0;
+  if (!gy || !a || !ga) return fail(BPC_ERR_ARG, "null buffer");
+  if ((reinterpret_cast<uintptr_t>(gy) | reinterpret_cast<uintptr_t>(gy_bf16) | reinterpret_cast<uintptr_t>(a) |
+       reinterpret_cast<uintptr_t>(gh) | reinterpret_cast<uintptr_t>(ga)) & 15)
+    return fail(BPC_ERR_ARG, "gy, gy_bf16, a, gh and ga must be 16-byte aligned");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int grid = elementwise_grid(sh.units);
+  const auto* ab = static_cast<const __nv_bfloat16*>(a);
+  auto* gab = static_cast<__nv_bfloat16*>(ga);
+  if (f32)
+    gelu_residual_bwd_kernel<true><<<grid, 256, 0, s>>>(gy, static_cast<const __nv_bfloat16*>(gy_bf16), ab,
+                                                        static_cast<float*>(gh), gab, sh);
+  else
+    gelu_residual_bwd_kernel<false><<<grid, 256, 0, s>>>(gy, nullptr, ab, nullptr, gab, sh);
+  cudaError_t le = cudaGetLastError();
+  if (le != cudaSuccess) return fail(BPC_ERR_LAUNCH, std::string("gelu_residual_bwd_kernel launch: ") + cudaGetErrorString(le));
+  return 0;
+}
 
 extern "C" int bpc_residual_affine_silu(const float* h, const void* u, float* out, void* x, int64_t rows, int32_t H,
                                         float scale_h, float scale_u, const float* a, const float* b,

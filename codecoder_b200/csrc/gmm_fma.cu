@@ -102,6 +102,7 @@ __global__ void __launch_bounds__(kFmaThreads) gmm_fma_kernel(const FmaArgs a) {
         T* yp = yr + ch_off(o0 + j, a.y_cg_stride);
         if (a.epi == kEpiGeluInit) v = gelu_tanh(v);
         else if (a.epi == kEpiGeluResid) v = ld_elem(yp) + gelu_tanh(v);
+        else if (a.epi == kEpiAdd) v = ld_elem(yp) + v;
         else if (a.epi == kEpiAffineSilu) v = silu_exact(fmaf(v, __ldg(a.epi_scale + o0 + j), __ldg(a.epi_shift + o0 + j)));
         const T sv = st_conv<T>(v);
         *yp = sv;

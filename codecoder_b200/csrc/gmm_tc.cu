@@ -327,7 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------------ epilogue (warps 2..9)
     // One shot (TMEM lane) per thread.  Element math runs on packed fp32 pairs (f32x2); the residual row is loaded
     // before the accumulator wait (whole row up to 128 channels, then two 32-channel chunks ahead).
-    constexpr bool kResid = EPI == kEpiGeluResid;
+    constexpr bool kResid = EPI == kEpiGeluResid || EPI == kEpiAdd;
     constexpr int kPre = NCH <= 4 ? NCH : 2;          // chunks loaded before the accumulator wait
     const int q = warp & 3;                   // TMEM lane quarter this warp may access
     const int m = (warp - 2) >> 2;            // which 128-shot sub-tile
@@ -395,7 +395,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                   const int colp = c * 32 + j * 8 + 2 * e;
                   x = silu_tanh_fast2(f2_fma(x, *reinterpret_cast<const uint64_t*>(a.epi_scale + colp),
                                              *reinterpret_cast<const uint64_t*>(a.epi_shift + colp)));
-                } else if (EPI != kEpiStore) {
+                } else if (EPI == kEpiGeluInit || EPI == kEpiGeluResid) {
                   x = gelu_tanh_fast2(x);
                 }
                 if (kResid) x = f2_add(x, bf2_to_f2(h[e]));
@@ -838,6 +838,7 @@ KernelFn kernel_for(bool blocked, int epi, bool head) {
     if (head) return nullptr;
     if (epi == kEpiStore) return &gmm_tc_kernel<MT, NCH, false, kEpiStore, false>;
     if (epi == kEpiAffineSilu) return &gmm_tc_kernel<MT, NCH, false, kEpiAffineSilu, false>;
+    if (epi == kEpiAdd) return &gmm_tc_kernel<MT, NCH, false, kEpiAdd, false>;
     return nullptr;
   }
   if (epi == kEpiGeluInit)

@@ -215,6 +215,100 @@ class GatherMMB200(torch.autograd.Function):
         return gx, gw, None, None
 
 
+def _gmm_into(a: torch.Tensor, idx32: torch.Tensor, w: torch.Tensor, out: torch.Tensor) -> None:
+    """Forward into a caller's contiguous bf16 (B, NT, C_out) block (the op with an output argument)."""
+    B, NS, Ci = a.shape
+    NT, K = idx32.shape
+    Co = w.shape[0]
+    rc = _lib.lib().bpc_gather_mm_fwd(a.data_ptr(), w.data_ptr(), idx32.data_ptr(), out.data_ptr(), B, NS, NT, K, Ci,
+                                      Co, _DTYPES[a.dtype], _stream_ptr(a.device))
+    _lib.check(rc, "bpc_gather_mm_fwd")
+
+
+def _dgrad_into(gy: torch.Tensor, tgt32: torch.Tensor, w: torch.Tensor, gx: torch.Tensor, accumulate: bool) -> None:
+    """gx (=|+=) the input gradient of one weight set (bpc_gather_mm_dgrad_ex)."""
+    B, NT, Co = gy.shape
+    NS, K = tgt32.shape
+    Ci = w.shape[1] // K
+    w_t = torch.empty_like(w)
+    rc = _lib.lib().bpc_gather_mm_dgrad_ex(gy.data_ptr(), w.data_ptr(), tgt32.data_ptr(), gx.data_ptr(), w_t.data_ptr(),
+                                           B, NT, NS, K, Ci, Co, int(accumulate), _DTYPES[gy.dtype],
+                                           _stream_ptr(gy.device))
+    _lib.check(rc, "bpc_gather_mm_dgrad_ex")
+
+
+class BipartiteStepB200(torch.autograd.Function):
+    """One residual bipartite step of the training network, y = h + GELU(gather_mm(x, W_t, idx_t)) over T target
+    types (targets of type t are the rows [t NT / T, (t + 1) NT / T) of y), as the reference composes it under bf16
+    autocast from per-type gather_mm calls, a concatenation, GELU and an add (cascade_net.py:140-175,228-233):
+      x (B, NS, C_in) bf16; h (B, NT, C_out) bf16 (-> y bf16), fp32 (-> y fp32 and its bf16 copy, returned as a
+      pair: the copy is the next op's input) or None (y = bf16 GELU); ws: T fp32 master weights (C_out, K C_in),
+      cast to bf16 here; tables: per type (idx (NT / T, K), target table (NS, K)) int32 on the device.
+    The T forwards write one type-major pre-activation block (T, B, NT / T, C_out) that is kept for the backward;
+    GELU, the add and the cast run as one pass (bpc_gelu_residual_fwd), the GELU gradient and the residual sum as
+    one pass back (bpc_gelu_residual_bwd); the input gradients of the T types accumulate in the second dgrad's
+    epilogue, and the weight gradients are fp32 from the deterministic wgrad kernel."""
+
+    @staticmethod
+    def forward(ctx, x, h, tables, *ws):
+        T = len(ws)
+        B, NS, Ci = x.shape
+        NTt = tables[0][0].shape[0]
+        NT = T * NTt
+        w16 = [w.to(torch.bfloat16).contiguous() for w in ws]
+        Co = w16[0].shape[0]
+        a = torch.empty(T, B, NTt, Co, device=x.device, dtype=torch.bfloat16)
+        for t in range(T):
+            _gmm_into(x, tables[t][0], w16[t], a[t])
+        L = _lib.lib()
+        st = _stream_ptr(x.device)
+        f32 = h is not None and h.dtype == torch.float32
+        y = torch.empty(B, NT, Co, device=x.device, dtype=torch.float32 if f32 else torch.bfloat16)
+        y16 = torch.empty(B, NT, Co, device=x.device, dtype=torch.bfloat16) if f32 else None
+        hdt = _lib.BPC_DTYPE_F32 if f32 else _lib.BPC_DTYPE_BF16
+        rc = L.bpc_gelu_residual_fwd(a.data_ptr(), h.data_ptr() if h is not None else None, y.data_ptr(),
+                                     y16.data_ptr() if f32 else None, B, NT, Co, T, hdt, st)
+        _lib.check(rc, "bpc_gelu_residual_fwd")
+        ctx.save_for_backward(x, a, *w16)
+        ctx.tables, ctx.f32, ctx.has_h = tables, f32, h is not None
+        return (y, y16) if f32 else y
+
+    @staticmethod
+    def backward(ctx, gy, gy16=None):
+        x, a, *w16 = ctx.saved_tensors
+        T, B, NTt, Co = a.shape
+        NT = T * NTt
+        L = _lib.lib()
+        st = _stream_ptr(x.device)
+        gh = None
+        ga = torch.empty_like(a)
+        if ctx.f32:
+            gy = gy.float().contiguous()
+            g16 = gy16.to(torch.bfloat16).contiguous() if gy16 is not None else None
+            gh = torch.empty_like(gy) if ctx.needs_input_grad[1] else None
+            rc = L.bpc_gelu_residual_bwd(gy.data_ptr(), g16.data_ptr() if g16 is not None else None, a.data_ptr(),
+                                         gh.data_ptr() if gh is not None else None, ga.data_ptr(), B, NT, Co, T,
+                                         _lib.BPC_DTYPE_F32, st)
+        else:
+            gy = gy.to(torch.bfloat16).contiguous()
+            rc = L.bpc_gelu_residual_bwd(gy.data_ptr(), None, a.data_ptr(), None, ga.data_ptr(), B, NT, Co, T,
+                                         _lib.BPC_DTYPE_BF16, st)
+            gh = gy if ctx.has_h and ctx.needs_input_grad[1] else None
+        _lib.check(rc, "bpc_gelu_residual_bwd")
+        gx = None
+        if ctx.needs_input_grad[0]:
+            gx = torch.empty_like(x)
+            for t in range(T):
+                _dgrad_into(ga[t], ctx.tables[t][1], w16[t], gx, accumulate=t > 0)
+        gws = [gmm_wgrad(x, ga[t], ctx.tables[t][0]) if ctx.needs_input_grad[3 + t] else None for t in range(T)]
+        return (gx, gh, None, *gws)
+
+
+def bipartite_step(x, h, tables, *ws):
+    """BipartiteStepB200.apply (see there)."""
+    return BipartiteStepB200.apply(x, h, tables, *ws)
+
+
 def gather_mm(x, w, idx, inv):
     """y[b, n] = W cat_r x[b, idx[n, r]] (cascade_net.py:174-175), on the B200 kernels."""
     return GatherMMB200.apply(x, w, idx, inv)

@@ -24,7 +24,7 @@ import torch
 import torch.nn.functional as F
 from torch import nn
 
-from .ops import gather_mm
+from .ops import bipartite_step, gather_mm, target_table
 from .params import N_TOKENS
 
 
@@ -33,8 +33,9 @@ class PreDecoderNet(nn.Module):
     numpy) to start from, else a seeded init with the same bounds.  `gmm` is the bipartite-conv op with the
     reference's signature gmm(x, w, idx, inv) (default: the B200 op)."""
 
-    def __init__(self, geo, cfg, params: dict | None = None, gmm=gather_mm, seed: int = 0):
+    def __init__(self, geo, cfg, params: dict | None = None, gmm=gather_mm, seed: int = 0, fused: bool = True):
         super().__init__()
+        self.fused = fused
         if cfg.K != geo.K or cfg.d != geo.d or cfg.rounds != geo.R:
             raise ValueError("configuration and geometry disagree")
         self.cfg, self.gmm = cfg, gmm
@@ -56,6 +57,17 @@ class PreDecoderNet(nn.Module):
             buf[f"inv_d2c{c}"] = geo.inverse(geo.d2c[c], geo.N_d)
         for k, v in buf.items():
             self.register_buffer(k, torch.as_tensor(np.asarray(v, np.int64)), persistent=False)
+        # int32 gather and target tables of the fused steps (checks are type-major: X checks, then Z checks)
+        K = cfg.K
+        i32 = {"c2d_i32": geo.c2d[0], "c2d_tgt": target_table(torch.as_tensor(buf["inv_c2d"]), geo.N_d, K)}
+        for c in range(2):
+            i32[f"d2c{c}_i32"] = geo.d2c[c]
+            i32[f"d2c{c}_tgt"] = target_table(torch.as_tensor(buf[f"inv_d2c{c}"]), geo.d2c[c].shape[0], K)
+        for k, v in i32.items():
+            self.register_buffer(k, torch.as_tensor(np.asarray(v), dtype=torch.int32), persistent=False)
+        self._fused_ok = (geo.d2c[0].shape[0] == geo.d2c[1].shape[0] and
+                          np.array_equal(np.concatenate([np.flatnonzero(geo.check_type == 0),
+                                                         np.flatnonzero(geo.check_type == 1)]), np.arange(geo.N_c)))
         # the logits read h_d after the last check -> data step: the last data -> check step does not reach the
         # loss, so its weights take no gradient (kept for the inference weight set)
         for c in range(2):
@@ -63,6 +75,10 @@ class PreDecoderNet(nn.Module):
 
     def forward(self, det: torch.Tensor) -> torch.Tensor:
         """det (B, N_c) uint8 -> logits (B, N_d, 2) (bf16 under autocast)."""
+        if (self.fused and self._fused_ok and self.gmm is gather_mm and det.is_cuda and
+                torch.is_autocast_enabled("cuda") and torch.get_autocast_dtype("cuda") == torch.bfloat16 and
+                self.cfg.channels % 8 == 0):
+            return self._forward_fused(det)
         tok = 2 * self.check_type + det.long()
         hc = F.embedding(tok, self.embed)
         hd = None
@@ -74,6 +90,23 @@ class PreDecoderNet(nn.Module):
             a = torch.cat([self.gmm(hd, self.w_d2c[2 * l + c], getattr(self, f"d2c{c}"), getattr(self, f"inv_d2c{c}"))
                            for c in range(2)], 1)
             hc = hc + F.gelu(a, approximate="tanh")
+        return F.linear(hd, self.head_w, self.head_b)
+
+    def _forward_fused(self, det: torch.Tensor) -> torch.Tensor:
+        """The same network under bf16 autocast through ops.bipartite_step: each step is the op's forward kernels
+        plus one GELU + residual pass (forward) and one GELU-gradient pass (backward), the check stream fp32 with its
+        bf16 copy made in the same pass, the data stream bf16."""
+        tok = 2 * self.check_type + det.long()
+        hc = F.embedding(tok, self.embed)
+        hc16 = hc.to(torch.bfloat16)
+        c2d = ((self.c2d_i32, self.c2d_tgt),)
+        d2c = ((self.d2c0_i32, self.d2c0_tgt), (self.d2c1_i32, self.d2c1_tgt))
+        hd = None
+        for l in range(self.cfg.layers):
+            hd = bipartite_step(hc16, hd, c2d, self.w_c2d[l])
+            if l == self.cfg.layers - 1:
+                break
+            hc, hc16 = bipartite_step(hd, hc, d2c, self.w_d2c[2 * l], self.w_d2c[2 * l + 1])
         return F.linear(hd, self.head_w, self.head_b)
 
 

@@ -52,13 +52,14 @@ BPC_API int bpc_gather_mm_fwd(const void* x, const void* w, const int32_t* idx, 
                       int32_t K, int32_t Ci, int32_t Co, int32_t dtype, bpc_stream_t stream);
 
 /* Epilogues of bpc_gather_mm_fwd_ex. */
-enum { BPC_EPILOGUE_STORE = 0, BPC_EPILOGUE_AFFINE_SILU = 1 };
+enum { BPC_EPILOGUE_STORE = 0, BPC_EPILOGUE_AFFINE_SILU = 1, BPC_EPILOGUE_ADD = 2 };
 
 /* bpc_gather_mm_fwd with two weight sets and an epilogue, for the layers around the op (no reference counterpart as
  * one call; it computes what the reference's BipartiteConv / Block compose from several calls):
  *   y[b, n, :] = epi( sum_r x[b, idx[n, r], :] W_{t(n), r}^T ),  t(n) = (n >= type_split), W = n_wtypes stacked
- *   (Co, K*Ci) matrices; epi = identity (BPC_EPILOGUE_STORE) or c -> SiLU(scale[c] v + shift[c])
- *   (BPC_EPILOGUE_AFFINE_SILU: an inference BatchNorm + SiLU; scale / shift fp32 (Co,) device vectors).
+ *   (Co, K*Ci) matrices; epi = identity (BPC_EPILOGUE_STORE), c -> SiLU(scale[c] v + shift[c])
+ *   (BPC_EPILOGUE_AFFINE_SILU: an inference BatchNorm + SiLU; scale / shift fp32 (Co,) device vectors), or
+ *   y[b, n, :] += v (BPC_EPILOGUE_ADD: y is read and written, same dtype).
  * The concatenation of the reference's per-type calls (cascade_net.py:228-233) is one call with n_wtypes = 2 when
  * the targets are ordered by type. */
 BPC_API int bpc_gather_mm_fwd_ex(const void* x, const void* w, const int32_t* idx, void* y, int64_t B, int32_t NS,
@@ -75,6 +76,19 @@ BPC_API int bpc_gather_mm_fwd_ex(const void* x, const void* w, const int32_t* id
 BPC_API int bpc_residual_affine_silu(const float* h, const void* u, float* out, void* x, int64_t rows, int32_t H,
                                      float scale_h, float scale_u, const float* a, const float* b, bpc_stream_t stream);
 
+/* The residual steps of the training network around the op, one memory-bound pass each (no reference counterpart as
+ * one call; torch runs GELU, the residual add and the casts as separate kernels):
+ *   forward   y = h + bf16(GELU(a))   h bf16 -> y bf16 (rounded once); h f32 -> y f32 and y_bf16 = bf16(y);
+ *             h NULL -> y = bf16(GELU(a)) (h_dtype ignored)
+ *   backward  g = gy (+ gy_bf16, f32 stream only);  gh = g (f32 stream; may be NULL);
+ *             ga = bf16(GELU'(a) * g), g rounded to bf16 first on the f32 stream
+ * a and ga are bf16 (n_types, B, NT / n_types, C): the pre-activations of target type t are one contiguous block;
+ * h, y, gy, gh are (B, NT, C).  GELU is the tanh form.  C % 8 == 0, every pointer 16-byte aligned. */
+BPC_API int bpc_gelu_residual_fwd(const void* a, const void* h, void* y, void* y_bf16, int64_t B, int32_t NT, int32_t C,
+                                  int32_t n_types, int32_t h_dtype, bpc_stream_t stream);
+BPC_API int bpc_gelu_residual_bwd(const void* gy, const void* gy_bf16, const void* a, void* gh, void* ga, int64_t B,
+                                  int32_t NT, int32_t C, int32_t n_types, int32_t gy_dtype, bpc_stream_t stream);
+
 /* Input gradient of bpc_gather_mm_fwd through the target table:
  *   gx[b, s, :] = sum_r gy[b, tgt[s, r], :] W_r,   tgt (NS, K) int32, NT (or any value outside [0, NT)) = none
  * gy (B, NT, Co), gx (B, NS, Ci), W (Co, K*Ci) as in the forward.  tgt[s, r] is the target that reads source s
@@ -85,6 +99,13 @@ BPC_API int bpc_residual_affine_silu(const float* h, const void* u, float* out, 
 BPC_API int bpc_gather_mm_dgrad(const void* gy, const void* w, const int32_t* tgt, void* gx, void* w_t, int64_t B,
                                 int32_t NT, int32_t NS, int32_t K, int32_t Ci, int32_t Co, int32_t dtype,
                                 bpc_stream_t stream);
+
+/* bpc_gather_mm_dgrad that adds into gx when accumulate != 0 (gx += the sum, rounded once to gx's dtype): the input
+ * gradient of a source read by targets of two types (two weight sets, two target tables) in two calls, where
+ * autograd over the reference's per-type calls (cascade_net.py:228-233) sums two gradients. */
+BPC_API int bpc_gather_mm_dgrad_ex(const void* gy, const void* w, const int32_t* tgt, void* gx, void* w_t, int64_t B,
+                                   int32_t NT, int32_t NS, int32_t K, int32_t Ci, int32_t Co, int32_t accumulate,
+                                   int32_t dtype, bpc_stream_t stream);
 
 /* Weight gradient of bpc_gather_mm_fwd, fp32 and deterministic (fixed split of the rows, fixed-order sum):
  *   dw[o, r*Ci + i] = sum_{b, n} gy[b, n, o] x[b, idx[n, r], i]      (pads contribute nothing)

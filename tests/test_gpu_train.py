@@ -71,3 +71,26 @@ def test_training_lowers_the_loss():
         losses.append(float(tr.step(det, err)))
     assert np.isfinite(losses).all()
     assert np.mean(losses[-10:]) < 0.7 * np.mean(losses[:5]), losses
+
+
+def test_fused_steps_match_the_unfused_network():
+    """Under bf16 autocast PreDecoderNet runs each residual step as ops.bipartite_step (op kernels + one GELU /
+    residual pass each way, both check types in one pre-activation block); the unfused torch composition of the same
+    network gives the same logits and gradients up to bf16 rounding (GELU on tanh.approx vs tanhf, one rounding of
+    the summed input gradient instead of two)."""
+    cfg = replace(CONFIGS["d11_train"], d=5, rounds=5, layers=3)
+    g = RotatedSurface(cfg.d, cfg.rounds)
+    params = init_params(cfg, 51)
+    det, err = sample(g, 0.03, 300, 52)
+    out = []
+    for fused in (True, False):
+        net = PreDecoderNet(g, cfg, params, fused=fused).cuda()
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            z = net(torch.as_tensor(det).cuda())
+        F.binary_cross_entropy_with_logits(z.float(), torch.as_tensor(err).cuda().float()).backward()
+        out.append((z, dict(net.named_parameters())))
+    (zf, pf), (zu, pu) = out
+    assert rel(zf, zu) < 1e-2
+    for k in pu:
+        if pu[k].requires_grad:
+            assert rel(pf[k].grad, pu[k].grad) < 2e-2, (k, rel(pf[k].grad, pu[k].grad))
