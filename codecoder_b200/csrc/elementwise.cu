@@ -207,6 +207,87 @@ __global__ void __launch_bounds__(256) gelu_residual_bwd_kernel(const void* __re
   }
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// Token embedding of the training network, tok[b, n] = 2 type[n] + det[b, n] in {0..3} (cascade_net.py:279-285):
+//   forward   h[b, n, :] = E[tok, :] (fp32) and its bf16 copy, one pass
+//   backward  dE[k, :] = sum over (b, n) with tok = k of (g + g_bf16)[b, n, :]: per-block partial sums (each warp
+//             a fixed set of rows, warps added in order in shared memory), then a fixed-order sum over the blocks;
+//             deterministic, no atomics
+constexpr int kEmbBwdBlocks = 1024;
+constexpr int kEmbBwdThreads = 256;
+constexpr int kEmbMaxC = 256;
+
+__global__ void __launch_bounds__(256) embed_tokens_fwd_kernel(const uint8_t* __restrict__ det,
+                                                               const uint8_t* __restrict__ ctype,
+                                                               const float* __restrict__ E, float* __restrict__ h,
+                                                               __nv_bfloat16* __restrict__ h16, int64_t units, int N,
+                                                               int C8) {
+  for (int64_t u = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; u < units;
+       u += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = u / C8;
+    const int c8 = static_cast<int>(u - row * C8);
+    const int tok = 2 * __ldg(ctype + row % N) + __ldg(det + row);
+    const float4 e0 = __ldg(reinterpret_cast<const float4*>(E + static_cast<int64_t>(tok) * C8 * 8 + c8 * 8));
+    const float4 e1 = __ldg(reinterpret_cast<const float4*>(E + static_cast<int64_t>(tok) * C8 * 8 + c8 * 8 + 4));
+    reinterpret_cast<float4*>(h)[2 * u] = e0;
+    reinterpret_cast<float4*>(h)[2 * u + 1] = e1;
+    uint4 o;
+    o.x = bf_pack(e0.x, e0.y);
+    o.y = bf_pack(e0.z, e0.w);
+    o.z = bf_pack(e1.x, e1.y);
+    o.w = bf_pack(e1.z, e1.w);
+    reinterpret_cast<uint4*>(h16)[u] = o;
+  }
+}
+
+__global__ void __launch_bounds__(kEmbBwdThreads) embed_tokens_bwd_partial_kernel(
+    const uint8_t* __restrict__ det, const uint8_t* __restrict__ ctype, const float* __restrict__ g,
+    const __nv_bfloat16* __restrict__ g16, float* __restrict__ partial, int64_t rows, int N, int C) {
+  __shared__ float red[kEmbBwdThreads / 32][4][kEmbMaxC];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int kSlots = kEmbMaxC / 32;
+  float acc[4][kSlots];
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+#pragma unroll
+    for (int j = 0; j < kSlots; ++j) acc[k][j] = 0.f;
+  const int64_t per_block = (rows + gridDim.x - 1) / gridDim.x;
+  const int64_t r0 = blockIdx.x * per_block, r1 = min(rows, r0 + per_block);
+  for (int64_t r = r0 + warp; r < r1; r += kEmbBwdThreads / 32) {
+    const int tok = 2 * __ldg(ctype + r % N) + __ldg(det + r);
+#pragma unroll
+    for (int j = 0; j < kSlots; ++j) {
+      const int c = lane + 32 * j;
+      if (c < C) {
+        float v = g ? __ldg(g + r * C + c) : 0.f;
+        if (g16) v += __bfloat162float(g16[r * C + c]);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) acc[k][j] += (tok == k) ? v : 0.f;
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+#pragma unroll
+    for (int j = 0; j < kSlots; ++j)
+      if (lane + 32 * j < C) red[warp][k][lane + 32 * j] = acc[k][j];
+  __syncthreads();
+  for (int i = threadIdx.x; i < 4 * C; i += blockDim.x) {
+    const int k = i / C, c = i - k * C;
+    float v = 0.f;
+    for (int w = 0; w < kEmbBwdThreads / 32; ++w) v += red[w][k][c];
+    partial[static_cast<int64_t>(blockIdx.x) * 4 * C + i] = v;
+  }
+}
+
+__global__ void embed_tokens_bwd_sum_kernel(const float* __restrict__ partial, float* __restrict__ dE, int n, int blocks) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float v = 0.f;
+  for (int b = 0; b < blocks; ++b) v += partial[static_cast<int64_t>(b) * n + i];
+  dE[i] = v;
+}
+
 int step_shape(int64_t B, int32_t NT, int32_t C, int32_t n_types, StepShape* sh) {
   if (B < 0 || NT < 1 || C < 8 || C % 8 || n_types < 1 || NT % n_types)
     return fail(BPC_ERR_ARG, "B >= 0, NT a multiple of the type count, C a multiple of 8");
@@ -298,5 +379,46 @@ extern "C" int bpc_residual_affine_silu(const float* h, const void* u, float* ou
       a, b);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(BPC_ERR_LAUNCH, std::string("residual_affine_silu_kernel: ") + cudaGetErrorString(e));
+  return 0;
+}
+
+extern "C" int bpc_embed_tokens_fwd(const uint8_t* det, const uint8_t* check_type, const float* E, float* h,
+                                    void* h_bf16, int64_t B, int32_t N, int32_t C, bpc_stream_t stream) {
+  if (B < 0 || N < 1 || C < 8 || C % 8) return fail(BPC_ERR_ARG, "B >= 0, N >= 1, C a multiple of 8");
+  if (B == 0) return 0;
+  if (!det || !check_type || !E || !h || !h_bf16) return fail(BPC_ERR_ARG, "null buffer");
+  if ((reinterpret_cast<uintptr_t>(E) | reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(h_bf16)) & 15)
+    return fail(BPC_ERR_ARG, "E, h and h_bf16 must be 16-byte aligned");
+  const int64_t units = B * N * (C / 8);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  embed_tokens_fwd_kernel<<<elementwise_grid(units), 256, 0, s>>>(det, check_type, E, h,
+                                                                  static_cast<__nv_bfloat16*>(h_bf16), units, N, C / 8);
+  cudaError_t le = cudaGetLastError();
+  if (le != cudaSuccess) return fail(BPC_ERR_LAUNCH, std::string("embed_tokens_fwd_kernel launch: ") + cudaGetErrorString(le));
+  return 0;
+}
+
+extern "C" size_t bpc_embed_tokens_bwd_workspace_size(int32_t C) {
+  return C < 1 ? 0 : static_cast<size_t>(kEmbBwdBlocks) * 4 * C * sizeof(float);
+}
+
+extern "C" int bpc_embed_tokens_bwd(const uint8_t* det, const uint8_t* check_type, const float* g, const void* g_bf16,
+                                    float* dE, void* workspace, size_t workspace_bytes, int64_t B, int32_t N, int32_t C,
+                                    bpc_stream_t stream) {
+  if (B < 0 || N < 1 || C < 1 || C > kEmbMaxC) return fail(BPC_ERR_ARG, "B >= 0, N >= 1, 1 <= C <= 256");
+  if (!dE) return fail(BPC_ERR_ARG, "null dE");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (B == 0) {
+    cudaError_t e = cudaMemsetAsync(dE, 0, sizeof(float) * 4 * C, s);
+    return e == cudaSuccess ? 0 : fail(BPC_ERR_LAUNCH, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
+  }
+  if (!det || !check_type || (!g && !g_bf16) || !workspace) return fail(BPC_ERR_ARG, "null buffer");
+  if (workspace_bytes < bpc_embed_tokens_bwd_workspace_size(C)) return fail(BPC_ERR_SPACE, "embedding workspace too small");
+  float* partial = static_cast<float*>(workspace);
+  embed_tokens_bwd_partial_kernel<<<kEmbBwdBlocks, kEmbBwdThreads, 0, s>>>(
+      det, check_type, g, static_cast<const __nv_bfloat16*>(g_bf16), partial, B * N, N, C);
+  embed_tokens_bwd_sum_kernel<<<(4 * C + 127) / 128, 128, 0, s>>>(partial, dE, 4 * C, kEmbBwdBlocks);
+  cudaError_t le = cudaGetLastError();
+  if (le != cudaSuccess) return fail(BPC_ERR_LAUNCH, std::string("embed_tokens_bwd launch: ") + cudaGetErrorString(le));
   return 0;
 }

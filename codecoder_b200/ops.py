@@ -304,6 +304,50 @@ class BipartiteStepB200(torch.autograd.Function):
         return (gx, gh, None, *gws)
 
 
+class EmbedTokensB200(torch.autograd.Function):
+    """Detector tokens -> the fp32 check stream and its bf16 copy (C ABI bpc_embed_tokens_fwd / _bwd):
+    det (B, N) uint8, check_type (N) uint8, E (4, C) fp32 -> (E[2 type + det] fp32, the same in bf16).  The weight
+    gradient sums both outputs' gradients per token, deterministically (cascade_net.py:279-285,310-312)."""
+
+    @staticmethod
+    def forward(ctx, det, check_type, E):
+        B, N = det.shape
+        C = E.shape[1]
+        det = det.contiguous()
+        E = E.float().contiguous()
+        h = torch.empty(B, N, C, device=det.device, dtype=torch.float32)
+        h16 = torch.empty(B, N, C, device=det.device, dtype=torch.bfloat16)
+        rc = _lib.lib().bpc_embed_tokens_fwd(det.data_ptr(), check_type.data_ptr(), E.data_ptr(), h.data_ptr(),
+                                             h16.data_ptr(), B, N, C, _stream_ptr(det.device))
+        _lib.check(rc, "bpc_embed_tokens_fwd")
+        ctx.save_for_backward(det, check_type)
+        ctx.C = C
+        return h, h16
+
+    @staticmethod
+    def backward(ctx, g, g16):
+        det, check_type = ctx.saved_tensors
+        B, N = det.shape
+        C = ctx.C
+        L = _lib.lib()
+        dE = torch.empty(4, C, device=det.device, dtype=torch.float32)
+        ws = torch.empty(max(int(L.bpc_embed_tokens_bwd_workspace_size(C)), 16), device=det.device, dtype=torch.uint8)
+        g = g.float().contiguous() if g is not None else None
+        g16 = g16.to(torch.bfloat16).contiguous() if g16 is not None else None
+        if g is None and g16 is None:
+            return None, None, torch.zeros_like(dE)
+        rc = L.bpc_embed_tokens_bwd(det.data_ptr(), check_type.data_ptr(), g.data_ptr() if g is not None else None,
+                                    g16.data_ptr() if g16 is not None else None, dE.data_ptr(), ws.data_ptr(),
+                                    ws.numel(), B, N, C, _stream_ptr(det.device))
+        _lib.check(rc, "bpc_embed_tokens_bwd")
+        return None, None, dE
+
+
+def embed_tokens(det, check_type, E):
+    """EmbedTokensB200.apply (see there)."""
+    return EmbedTokensB200.apply(det, check_type, E)
+
+
 def bipartite_step(x, h, tables, *ws):
     """BipartiteStepB200.apply (see there)."""
     return BipartiteStepB200.apply(x, h, tables, *ws)

@@ -24,7 +24,7 @@ import torch
 import torch.nn.functional as F
 from torch import nn
 
-from .ops import bipartite_step, gather_mm, target_table
+from .ops import bipartite_step, embed_tokens, gather_mm, target_table
 from .params import N_TOKENS
 
 
@@ -65,6 +65,7 @@ class PreDecoderNet(nn.Module):
             i32[f"d2c{c}_tgt"] = target_table(torch.as_tensor(buf[f"inv_d2c{c}"]), geo.d2c[c].shape[0], K)
         for k, v in i32.items():
             self.register_buffer(k, torch.as_tensor(np.asarray(v), dtype=torch.int32), persistent=False)
+        self.register_buffer("check_type_u8", torch.as_tensor(geo.check_type.astype(np.uint8)), persistent=False)
         self._fused_ok = (geo.d2c[0].shape[0] == geo.d2c[1].shape[0] and
                           np.array_equal(np.concatenate([np.flatnonzero(geo.check_type == 0),
                                                          np.flatnonzero(geo.check_type == 1)]), np.arange(geo.N_c)))
@@ -96,9 +97,7 @@ class PreDecoderNet(nn.Module):
         """The same network under bf16 autocast through ops.bipartite_step: each step is the op's forward kernels
         plus one GELU + residual pass (forward) and one GELU-gradient pass (backward), the check stream fp32 with its
         bf16 copy made in the same pass, the data stream bf16."""
-        tok = 2 * self.check_type + det.long()
-        hc = F.embedding(tok, self.embed)
-        hc16 = hc.to(torch.bfloat16)
+        hc, hc16 = embed_tokens(det.to(torch.uint8), self.check_type_u8, self.embed)
         c2d = ((self.c2d_i32, self.c2d_tgt),)
         d2c = ((self.d2c0_i32, self.d2c0_tgt), (self.d2c1_i32, self.d2c1_tgt))
         hd = None

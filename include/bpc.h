@@ -89,6 +89,19 @@ BPC_API int bpc_gelu_residual_fwd(const void* a, const void* h, void* y, void* y
 BPC_API int bpc_gelu_residual_bwd(const void* gy, const void* gy_bf16, const void* a, void* gh, void* ga, int64_t B,
                                   int32_t NT, int32_t C, int32_t n_types, int32_t gy_dtype, bpc_stream_t stream);
 
+/* The detector-token embedding of the training network (cascade_net.py:279-285,310-312: tok = 2 type + bit, here
+ * with the 4 tokens of a rotated-surface check), forward and weight gradient:
+ *   forward   h[b, n, :] = E[2 check_type[n] + det[b, n], :]  (fp32 (B, N, C)) and h_bf16 = bf16(h), one pass
+ *   backward  dE[k, :] = sum over (b, n) with token k of g[b, n, :] + g_bf16[b, n, :] (either may be NULL), fp32 (4, C),
+ *             deterministic (fixed per-block partial sums in `workspace`, then a fixed-order sum)
+ * det (B, N) uint8 0/1, check_type (N) uint8 0/1, E (4, C) fp32; C % 8 == 0 (forward), C <= 256 (backward). */
+BPC_API int bpc_embed_tokens_fwd(const uint8_t* det, const uint8_t* check_type, const float* E, float* h, void* h_bf16,
+                                 int64_t B, int32_t N, int32_t C, bpc_stream_t stream);
+BPC_API size_t bpc_embed_tokens_bwd_workspace_size(int32_t C);
+BPC_API int bpc_embed_tokens_bwd(const uint8_t* det, const uint8_t* check_type, const float* g, const void* g_bf16,
+                                 float* dE, void* workspace, size_t workspace_bytes, int64_t B, int32_t N, int32_t C,
+                                 bpc_stream_t stream);
+
 /* Input gradient of bpc_gather_mm_fwd through the target table:
  *   gx[b, s, :] = sum_r gy[b, tgt[s, r], :] W_r,   tgt (NS, K) int32, NT (or any value outside [0, NT)) = none
  * gy (B, NT, Co), gx (B, NS, Ci), W (Co, K*Ci) as in the forward.  tgt[s, r] is the target that reads source s
