@@ -449,28 +449,29 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// Wide-tile kernel: blocked layout, C_in = C_out = 128 (the pre-decoder's hidden-128 networks).
+// Wide-tile kernel: C_out in {64, 96, 128}, C_in <= 128, both layouts.
 //
-// The MMA rows are the 128 output channels and its columns the tile's 256 shots: one tcgen05.mma M=128 N=256 K=16
-// per 16 input channels, W_r's 64-channel stage (the same TMA box as above) as the K-major 128-byte-swizzled A
-// operand and the blocked activation stage as the K-major no-swizzle B operand.  The tensor pipe takes a 256-column
-// MMA at its full rate, while 128-column MMAs cost more than their share per instruction (measured on B200 with
-// one issuing thread: M128 N128 K16 80-100 cycles each against 64, M128 N256 K16 at 128 when eight are committed
-// together, 143 when four are).  So the two stages of one relation are freed by one commit after its eight MMAs.
+// The MMA rows are the output channels (M = 128; rows past C_out compute values nobody reads) and its columns the
+// tile's 256 shots: one tcgen05.mma M=128 N=256 K=16 per 16 input channels, W_r's 64-channel stage (the same TMA box
+// as above) as the K-major 128-byte-swizzled A operand and the activation stage as the B operand: the blocked
+// stage (one bulk copy) in the K-major no-swizzle layout, or the row layout's TMA box (64 channels x 256 shots) in
+// the K-major 128-byte-swizzled layout.  The tensor pipe takes a 256-column MMA at its full rate, while 128-column
+// MMAs cost more than their share per instruction (measured on B200 with one issuing thread: M128 N128 K16 80-100
+// cycles each against 64 ideal, M128 N256 K16 at the ideal 128).  Each stage is freed by a commit after its MMAs.
 //
 // The accumulator rows are channels.  Each epilogue warp owns one TMEM lane quarter (32 channels) and one half of
 // the tile's shots; it reads 16 shot columns at a time (tcgen05.ld 32x32b.x16), turns them around through a 2 KB
 // scratch of its own (row = channel, 16-byte chunks swizzled: conflict-free stores and loads) so that each thread
-// holds 16 channels of one shot, and then runs the row kernel's element arithmetic (same bits).  With the head,
-// the logits of a shot need all 128 channels: after every warp has stored its part of the tile (an mbarrier of
-// 256 arrivals, waited with the watchdog), each warp reads 32 shots' rows back and forms the logits, threshold and
-// residual XOR exactly as the row kernel does.
+// holds 16 channels of one shot, and then runs the row kernel's element arithmetic (same bits).  Quarters past
+// C_out only keep the barriers.  With the head (blocked layout), the logits of a shot need all its channels: after
+// every warp has stored its part of the tile (an mbarrier of 256 arrivals, waited with the watchdog), each warp
+// reads 32 shots' rows back and forms the logits, threshold and residual XOR exactly as the row kernel does.
 constexpr int kWideShots = 256;                       // tile shots = MMA N
-constexpr int kWideC = 128;                           // C_in = C_out = MMA M
-constexpr uint32_t kWideXBytes = kWideShots * 64 * 2;   // one 64-channel activation stage (8 channel groups)
-constexpr uint32_t kWideWBytes = kWideC * 128;          // W_r rows x 64 channels
+constexpr int kWideM = 128;                           // MMA M (output channels, padded)
+constexpr uint32_t kWideXBytes = kWideShots * 64 * 2;   // one 64-channel activation stage
+constexpr uint32_t kWideWBytes = kWideM * 128;          // W_r rows x 64 channels
 constexpr uint32_t kWideStageBytes = kWideXBytes + kWideWBytes;
-constexpr int kWideStages = 4;                        // two relation slots of two 64-channel stages
+constexpr int kWideStages = 4;
 constexpr int kWideScratch = 2048;                    // per epilogue warp: 32 channels x 16 shots fp32
 constexpr int kWideBars = 2 * kWideStages + 2 + 2 + 1 + 2 * kRing + 2;
 
@@ -483,11 +484,15 @@ __device__ __forceinline__ uint32_t wide_scr_off(int c, int s) {
   return static_cast<uint32_t>((c ^ ((c >> 4) & 1)) * 64 + (((s >> 2) ^ ((c >> 1) & 3)) << 4) + (s & 3) * 4);
 }
 
-template <int EPI, bool HEAD>
+// NKB 64-channel blocks of C_in, KLAST 16-channel MMA steps in the last one (C_in = 64 (NKB - 1) + 16 KLAST): the MMA
+// issue sequence is unrolled at compile time.  Blocked layout: C_out = C_in.
+template <bool BLOCKED, int EPI, bool HEAD, int NKB, int KLAST>
 __global__ void __launch_bounds__(kThreads, 1)
-    gmm_wide_kernel(const __grid_constant__ CUtensorMap tmW, const TcArgs a) {
-  constexpr int kCgElems = kWideShots * 8;            // one channel group of a tile (elements)
-  constexpr bool kResid = EPI == kEpiGeluResid;
+    gmm_wide_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW, const TcArgs a) {
+  constexpr int kCgElems = kWideShots * 8;            // blocked: one channel group of a tile (elements)
+  constexpr int kCi = 64 * (NKB - 1) + 16 * KLAST;
+  constexpr bool kLoadY = EPI == kEpiGeluResid || EPI == kEpiAdd;     // the epilogue reads y before writing it
+  constexpr bool kGelu = EPI == kEpiGeluInit || EPI == kEpiGeluResid;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* scratch = smem + kWideStages * kWideStageBytes;
@@ -506,6 +511,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const int Co = a.Co;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kWideStages; ++i) {
@@ -524,6 +530,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(smem_u32(drain), 1);
     *abort_flag = 0;
     fence_mbar_init();
+    if (!BLOCKED) tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmW);
   }
   if (warp == 1) {
@@ -538,12 +545,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------------ producer
     if (lane == 0) {
-      int slot = 0;
-      uint32_t sphase = 0;
+      int stage = 0;
+      uint32_t phase = 0;
       uint32_t armed = 0, armed_parity = 0;
       int rslot = 0;
       uint32_t rphase = 0;
       bool ok = true;
+      const uint32_t stage_tx = kWideXBytes + static_cast<uint32_t>(Co) * 128;
       long long next = a.tile_counter ? atomicAdd(a.tile_counter, 1ull) : static_cast<long long>(blockIdx.x);
       TileRow nrow;
       issue_row(a, next < a.num_tiles ? next : 0, nrow);
@@ -564,29 +572,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         next = a.tile_counter ? atomicAdd(a.tile_counter, 1ull) : tile + gridDim.x;
         issue_row(a, next < a.num_tiles ? next : tile, nrow);
         const int64_t s0 = (tile / a.NT) * kWideShots;
-        const int wrow = (cur.n >= a.type_split) ? kWideC : 0;
+        const int wrow = (cur.n >= a.type_split) ? Co : 0;
 #pragma unroll 1
-        for (int r = 0; r < a.K; ++r) {
+        for (int r = 0; r < a.K && ok; ++r) {
           if (!(cur.vm & (1u << r))) continue;
-          const __nv_bfloat16* xs = a.x + static_cast<int64_t>(cur.src[r]) * a.x_node_stride + s0 * kWideC;
 #pragma unroll
-          for (int kb = 0; kb < 2; ++kb) {
-            const int st = slot * 2 + kb;
-            if (!mbar_wait(smem_u32(&empty[st]), sphase ^ 1u, abort_flag, a.status, a.timeout_ns)) {
+          for (int kb = 0; kb < NKB; ++kb) {
+            if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, a.status, a.timeout_ns)) {
               ok = false;
               break;
             }
-            const uint32_t sa = smem_u32(smem + st * kWideStageBytes);
-            const uint32_t fb = smem_u32(&full[st]);
-            mbar_arrive_expect_tx(fb, kWideStageBytes);
-            bulk_load(sa, xs + kb * 8 * kCgElems, kWideXBytes, fb);
+            const uint32_t sa = smem_u32(smem + stage * kWideStageBytes);
+            const uint32_t fb = smem_u32(&full[stage]);
+            if (BLOCKED) {
+              const int ncg = kb + 1 < NKB ? 8 : 2 * KLAST;
+              mbar_arrive_expect_tx(fb, ncg * kCgElems * 2 + static_cast<uint32_t>(Co) * 128);
+              bulk_load(sa, a.x + static_cast<int64_t>(cur.src[r]) * a.x_node_stride + s0 * kCi + kb * 8 * kCgElems,
+                        ncg * kCgElems * 2, fb);
+            } else {
+              mbar_arrive_expect_tx(fb, stage_tx);
+              tma_load_3d(sa, &tmA, kb * kKBlock, static_cast<int32_t>(s0), cur.src[r], fb);
+            }
             tma_load_3d(sa + kWideXBytes, &tmW, kb * kKBlock, r, wrow, fb);
-            armed |= 1u << st;
-            armed_parity = (armed_parity & ~(1u << st)) | (sphase << st);
+            armed |= 1u << stage;
+            armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
+            if (++stage == kWideStages) {
+              stage = 0;
+              phase ^= 1u;
+            }
           }
-          if (!ok) break;
-          slot ^= 1;
-          if (slot == 0) sphase ^= 1u;
         }
       }
       if (!ok) {
@@ -602,9 +616,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(kWideC, kWideShots);
-      int slot = 0;
-      uint32_t sphase = 0;
+      constexpr uint32_t idesc = idesc_bf16_f32(kWideM, kWideShots);
+      int stage = 0;
+      uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       int rslot = 0;
@@ -628,26 +642,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int r = 0; r < a.K && ok; ++r) {
           if (!(vm & (1u << r))) continue;
 #pragma unroll
-          for (int kb = 0; kb < 2; ++kb) {
-            const int st = slot * 2 + kb;
-            if (!mbar_wait(smem_u32(&full[st]), sphase, abort_flag, a.status, a.timeout_ns)) {
+          for (int kb = 0; kb < NKB; ++kb) {
+            if (!mbar_wait(smem_u32(&full[stage]), phase, abort_flag, a.status, a.timeout_ns)) {
               ok = false;
               break;
             }
-            const uint32_t sa = smem_u32(smem + st * kWideStageBytes);
+            const uint32_t sa = smem_u32(smem + stage * kWideStageBytes);
             const uint64_t ad0 = sdesc_k_sw128(sa + kWideXBytes);
-            const uint64_t bd0 = sdesc_k_none(sa, kCgElems * 2, 128);
+            const uint64_t bd0 = BLOCKED ? sdesc_k_none(sa, kCgElems * 2, 128) : sdesc_k_sw128(sa);
+            const int ksteps = kb + 1 < NKB ? 4 : KLAST;
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-              tc_mma_ss(d_tmem, ad0 + static_cast<uint64_t>((k * 32) >> 4),
-                        bd0 + static_cast<uint64_t>((2 * k * kCgElems * 2) >> 4), idesc, accumulate);
-              accumulate = 1;
+              if (k < ksteps) {
+                const uint32_t boff = BLOCKED ? 2 * k * kCgElems * 2 : k * 32;
+                tc_mma_ss(d_tmem, ad0 + static_cast<uint64_t>((k * 32) >> 4), bd0 + static_cast<uint64_t>(boff >> 4),
+                          idesc, accumulate);
+                accumulate = 1;
+              }
             }
-            tc_commit(smem_u32(&empty[st]));      // the stage is free once its four MMAs have read it
+            tc_commit(smem_u32(&empty[stage]));   // the stage is free once its MMAs have read it
+            if (++stage == kWideStages) {
+              stage = 0;
+              phase ^= 1u;
+            }
           }
-          if (!ok) break;
-          slot ^= 1;
-          if (slot == 0) sphase ^= 1u;
         }
         if (!ok) break;
         tc_commit(smem_u32(&accf[acc]));
@@ -662,13 +680,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------------------ epilogue (warps 2..9)
     const int q = warp & 3;                   // TMEM lane quarter: channels 32 q .. 32 q + 31
+    const bool live = 32 * q < Co;            // quarters past C_out only keep the barriers
     const int e = warp - 2;
     const int half = e >> 2;                  // tile shots 128 half .. 128 half + 127
     const int s = lane & 15;                  // after the turn-around: shot s of the 16-shot piece ...
     const int h = lane >> 4;                  // ... channels 32 q + 16 h .. + 15 (channel groups 4 q + 2 h, + 1)
     const int cg0 = 4 * q + 2 * h;
-    uint8_t* scr = scratch + e * kWideScratch;
-    const uint32_t scr_u = smem_u32(scr);
+    const uint32_t scr_u = smem_u32(scratch + e * kWideScratch);
     int acc = 0;
     uint32_t acc_phase = 0;
     int rslot = 0;
@@ -689,16 +707,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (tile < 0) break;
       const int64_t s0 = (tile / a.NT) * kWideShots;
-      __nv_bfloat16* yt = reinterpret_cast<__nv_bfloat16*>(a.y) + static_cast<int64_t>(n) * a.y_node_stride + s0 * kWideC;
-      // this thread's two 16-byte chunks of piece j: shot 128 half + 16 j + s, channel groups cg0, cg0 + 1
-      __nv_bfloat16* yc = yt + cg0 * kCgElems + (128 * half + s) * 8;
-      uint4 rb[kResid ? 8 : 1][2];
-      if (kResid) {
+      __nv_bfloat16* const y = reinterpret_cast<__nv_bfloat16*>(a.y);
+      __nv_bfloat16* const yt = y + static_cast<int64_t>(n) * a.y_node_stride + (BLOCKED ? s0 * kCi : 0);
+      // this thread's two 16-byte chunks of piece j (shot 128 half + 16 j + s of the tile, channels 32 q + 16 h ..):
+      // blocked: channel groups cg0 and cg0 + 1 of the tile block; rows: 32 contiguous bytes of the shot's row
+      const int64_t step_j = BLOCKED ? 128 : 16 * a.y_shot_stride;
+      const int64_t step_g = BLOCKED ? kCgElems : 8;
+      __nv_bfloat16* const yc = BLOCKED ? yt + cg0 * kCgElems + (128 * half + s) * 8
+                                        : yt + (s0 + 128 * half + s) * a.y_shot_stride + 32 * q + 16 * h;
+      uint4 rb[kLoadY ? 8 : 1][2];
+      if (kLoadY && live) {
 #pragma unroll
         for (int j = 0; j < 8; ++j)
           if (s0 + 128 * half + 16 * j + s < a.shots) {
-            rb[j][0] = *reinterpret_cast<const uint4*>(yc + j * 128);
-            rb[j][1] = *reinterpret_cast<const uint4*>(yc + j * 128 + kCgElems);
+            rb[j][0] = *reinterpret_cast<const uint4*>(yc + j * step_j);
+            rb[j][1] = *reinterpret_cast<const uint4*>(yc + j * step_j + step_g);
           }
       }
       if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&accf[acc]), acc_phase, abort_flag, a.status, a.timeout_ns)))
@@ -709,7 +732,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         float v[16];
-        if (vm) {
+        if (vm && live) {
           tmem_ld16(taddr + 16 * j, v);
         } else {
 #pragma unroll
@@ -720,6 +743,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(smem_u32(&acce[acc]));
         }
+        if (!live) continue;
         // turn around: row = channel (this lane), 16 shot columns -> this thread: shot s, 16 channels
 #pragma unroll
         for (int c4 = 0; c4 < 4; ++c4)
@@ -738,20 +762,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int g = 0; g < 2; ++g) {
             uint4 u;
             uint32_t* o = reinterpret_cast<uint32_t*>(&u);
-            const uint32_t* hr = reinterpret_cast<const uint32_t*>(&rb[kResid ? j : 0][g]);
+            const uint32_t* hr = reinterpret_cast<const uint32_t*>(&rb[kLoadY ? j : 0][g]);
 #pragma unroll
             for (int e4 = 0; e4 < 4; ++e4) {
-              uint64_t xx = gelu_tanh_fast2(f2_pack(x[8 * g + 2 * e4], x[8 * g + 2 * e4 + 1]));
-              if (kResid) xx = f2_add(xx, bf2_to_f2(hr[e4]));
+              uint64_t xx = f2_pack(x[8 * g + 2 * e4], x[8 * g + 2 * e4 + 1]);
+              if (kGelu) xx = gelu_tanh_fast2(xx);
+              if (kLoadY) xx = f2_add(xx, bf2_to_f2(hr[e4]));
               o[e4] = f2_to_bf2(xx);
             }
-            *reinterpret_cast<uint4*>(yc + j * 128 + g * kCgElems) = u;
+            *reinterpret_cast<uint4*>(yc + j * step_j + g * step_g) = u;
           }
         }
       }
       if (HEAD) {
         // every warp's part of the tile is stored: read 32 shots' rows back and form the logits in the row kernel's
-        // order (channel pairs, four 32-channel chunks, stored bf16 values)
+        // order (channel pairs, 32-channel chunks in order, stored bf16 values)
         mbar_arrive(smem_u32(&stored[acc]));
         if (!__all_sync(0xffffffffu,
                         mbar_wait(smem_u32(&stored[acc]), acc_phase, abort_flag, a.status, a.timeout_ns)))
@@ -760,7 +785,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool ok = s0 + sl < a.shots;
         uint64_t lg0 = 0, lg1 = 0;
 #pragma unroll
-        for (int cg = 0; cg < 16; ++cg) {
+        for (int cg = 0; cg < kCi / 8; ++cg) {
           const uint4 u = *reinterpret_cast<const uint4*>(yt + cg * kCgElems + sl * 8);
           const uint32_t* o = reinterpret_cast<const uint32_t*>(&u);
 #pragma unroll
@@ -768,7 +793,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t f = bf2_to_f2(o[e4]);
             const int col = cg * 8 + 2 * e4;
             lg0 = f2_fma(f, *reinterpret_cast<const uint64_t*>(a.head.head_w + col), lg0);
-            lg1 = f2_fma(f, *reinterpret_cast<const uint64_t*>(a.head.head_w + kWideC + col), lg1);
+            lg1 = f2_fma(f, *reinterpret_cast<const uint64_t*>(a.head.head_w + kCi + col), lg1);
           }
         }
         const float l0 = f2_lo(lg0) + f2_hi(lg0) + __ldg(a.head.head_b);
@@ -861,6 +886,31 @@ KernelFn select_kernel(int Co, bool blocked, int epi, bool head) {
     case 8: return kernel_for<8>(blocked, epi, head);
     default: return nullptr;
   }
+}
+
+// wide-tile kernel for (layout, epilogue, head, C_in in {64, 96, 128})
+template <bool BLOCKED, int EPI, bool HEAD>
+const void* wide_for_ci(int Ci) {
+  switch (Ci) {
+    case 64: return reinterpret_cast<const void*>(&gmm_wide_kernel<BLOCKED, EPI, HEAD, 1, 4>);
+    case 96: return reinterpret_cast<const void*>(&gmm_wide_kernel<BLOCKED, EPI, HEAD, 2, 2>);
+    case 128: return reinterpret_cast<const void*>(&gmm_wide_kernel<BLOCKED, EPI, HEAD, 2, 4>);
+    default: return nullptr;
+  }
+}
+
+const void* wide_kernel_for(bool blocked, int epi, bool head, int Ci) {
+  if (blocked) {
+    if (epi == kEpiGeluInit)
+      return head ? wide_for_ci<true, kEpiGeluInit, true>(Ci) : wide_for_ci<true, kEpiGeluInit, false>(Ci);
+    if (epi == kEpiGeluResid)
+      return head ? wide_for_ci<true, kEpiGeluResid, true>(Ci) : wide_for_ci<true, kEpiGeluResid, false>(Ci);
+    return nullptr;
+  }
+  if (head) return nullptr;
+  if (epi == kEpiStore) return wide_for_ci<false, kEpiStore, false>(Ci);
+  if (epi == kEpiAdd) return wide_for_ci<false, kEpiAdd, false>(Ci);
+  return nullptr;
 }
 
 }  // namespace
@@ -1007,17 +1057,20 @@ int gmm_tc_launch(const GmmProblem& p, const GmmMaps& maps, int* status, uint64_
   while (cols < static_cast<uint32_t>(2 * mt_for(p.Co) * p.Co)) cols <<= 1;
   a.tmem_cols = cols;
   const bool head = p.head.head_w != nullptr;
-  if (p.blocked && p.Ci == kWideC && p.Co == kWideC && (p.epi == kEpiGeluInit || p.epi == kEpiGeluResid)) {
-    using WideFn = void (*)(CUtensorMap, TcArgs);
-    WideFn wf = p.epi == kEpiGeluInit ? (head ? &gmm_wide_kernel<kEpiGeluInit, true> : &gmm_wide_kernel<kEpiGeluInit, false>)
-                                      : (head ? &gmm_wide_kernel<kEpiGeluResid, true>
-                                              : &gmm_wide_kernel<kEpiGeluResid, false>);
+  // wide tiles: C_out in {64, 96, 128} and C_in <= 128; blocked layout (C_in = C_out) with the GELU epilogues and
+  // the head, row layouts with contiguous channels and the store / add epilogues
+  const bool wide_shape = p.Co >= 64 && p.Co <= kWideM && p.Co % 32 == 0 && (p.Ci == 64 || p.Ci == 96 || p.Ci == 128);
+  const bool wide_blocked = p.blocked && p.Ci == p.Co && (p.epi == kEpiGeluInit || p.epi == kEpiGeluResid);
+  const bool wide_rows = !p.blocked && !head && p.y_cg_stride == 8 && (p.epi == kEpiStore || p.epi == kEpiAdd);
+  if (wide_shape && (wide_blocked || wide_rows)) {
+    const void* wf = wide_kernel_for(p.blocked, p.epi, head, p.Ci);
+    if (!wf) return fail(2, "unsupported wide-tile configuration");
     constexpr int wsmem = wide_smem_bytes();
     static_assert(wsmem <= kSmemLimit, "wide-tile kernel exceeds the shared memory per CTA");
-    if (int e = allow_smem(reinterpret_cast<const void*>(wf), wsmem)) return e;
+    if (int e = allow_smem(wf, wsmem)) return e;
     const int64_t grid = std::min<int64_t>(a.num_tiles, num_sms());
-    void* args[] = {const_cast<CUtensorMap*>(&maps.w), &a};
-    cudaError_t le = cudaLaunchKernel(reinterpret_cast<const void*>(wf), dim3(static_cast<unsigned>(grid)),
+    void* args[] = {const_cast<CUtensorMap*>(&maps.x), const_cast<CUtensorMap*>(&maps.w), &a};
+    cudaError_t le = cudaLaunchKernel(wf, dim3(static_cast<unsigned>(grid)),
                                       dim3(kThreads), args, static_cast<size_t>(wsmem), stream);
     if (le != cudaSuccess) return fail(4, std::string("gmm_wide_kernel launch: ") + cudaGetErrorString(le));
     return 0;
