@@ -511,7 +511,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int Co = a.Co;
+  const int Co = BLOCKED ? kCi : a.Co;                // blocked layout: C_out = C_in, known at compile time
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kWideStages; ++i) {
