@@ -86,6 +86,42 @@ def test_gmm_ragged_batches(B, C):
     assert rel_err(y, ref) < 1e-2
 
 
+@pytest.mark.parametrize("Ci,Co", [(64, 96), (96, 64), (96, 96), (128, 96), (96, 128), (64, 128)])
+def test_gmm_rectangular_channels(Ci, Co):
+    """C_in and C_out in {64, 96, 128} in any pair (the wide-tile kernel: M = 128 output channels, rows past C_out
+    unused; a 96-channel input is one full and one half 64-channel block), over two 256-shot tiles, the second
+    partial."""
+    g = RotatedSurface(5, 5)
+    B = 300
+    rng = np.random.default_rng(Ci * 1000 + Co)
+    x = torch.as_tensor(rng.standard_normal((B, g.N_d, Ci)).astype(np.float32)).to(torch.bfloat16)
+    w = torch.as_tensor((rng.standard_normal((Co, 8 * Ci)) / np.sqrt(8 * Ci)).astype(np.float32)).to(torch.bfloat16)
+    idx = g.d2c[0]
+    ref = orc.gather_mm(x.float(), w.float(), idx).numpy()
+    y = gmm(x.to(DEV), torch.as_tensor(idx).to(DEV), w.to(DEV)).float().cpu().numpy()
+    assert y.shape == (B, idx.shape[0], Co)
+    assert rel_err(y, ref) < 1e-2
+
+
+def test_dgrad_accumulate_adds_the_second_type():
+    """bpc_gather_mm_dgrad_ex with accumulate: the input gradient of a source read by X- and Z-check targets is the
+    first type's gradient plus the second's, the second added in the kernel's epilogue."""
+    from codecoder_b200.ops import _dgrad_into, target_table
+    g = RotatedSurface(5, 5)
+    B, C, K = 200, 96, 8
+    rng = np.random.default_rng(7)
+    gx = torch.empty(B, g.N_d, C, dtype=torch.bfloat16, device=DEV)
+    ref = np.zeros((B, g.N_d, C))
+    for t in range(2):
+        NT = g.d2c[t].shape[0]
+        gy = torch.as_tensor(rng.standard_normal((B, NT, C)).astype(np.float32)).to(torch.bfloat16)
+        w = torch.as_tensor((rng.standard_normal((C, K * C)) / np.sqrt(K * C)).astype(np.float32)).to(torch.bfloat16)
+        tgt = target_table(torch.as_tensor(g.inverse(g.d2c[t], g.N_d)), NT, K)
+        _dgrad_into(gy.to(DEV), tgt.to(DEV), w.to(DEV), gx, accumulate=t > 0)
+        ref += orc.gather_mm_dgrad(gy.float().numpy(), w.float().numpy(), tgt.numpy(), C)
+    assert rel_err(gx.float().cpu().numpy(), ref) < 2e-2
+
+
 def test_gmm_pad_rows_and_negative_indices_read_zeros():
     NS, NT, K, C, B = 50, 40, 8, 128, 130
     rng = np.random.default_rng(5)
