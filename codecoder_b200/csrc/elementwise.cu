@@ -251,20 +251,41 @@ __global__ void __launch_bounds__(kEmbBwdThreads) embed_tokens_bwd_partial_kerne
   for (int k = 0; k < 4; ++k)
 #pragma unroll
     for (int j = 0; j < kSlots; ++j) acc[k][j] = 0.f;
+  // each warp a contiguous run of rows, four rows per iteration with all their loads issued before the adds
   const int64_t per_block = (rows + gridDim.x - 1) / gridDim.x;
   const int64_t r0 = blockIdx.x * per_block, r1 = min(rows, r0 + per_block);
-  for (int64_t r = r0 + warp; r < r1; r += kEmbBwdThreads / 32) {
-    const int tok = 2 * __ldg(ctype + r % N) + __ldg(det + r);
+  const int64_t per_warp = (r1 - r0 + kEmbBwdThreads / 32 - 1) / (kEmbBwdThreads / 32);
+  const int64_t w0 = r0 + warp * per_warp, w1 = min(r1, w0 + per_warp);
+  int n = w0 < w1 ? static_cast<int>(w0 % N) : 0;      // node of row w0; advanced without a division per row
+  for (int64_t r = w0; r < w1; r += 4) {
+    int tok[4];
+    float v[4][kSlots];
 #pragma unroll
-    for (int j = 0; j < kSlots; ++j) {
-      const int c = lane + 32 * j;
-      if (c < C) {
-        float v = g ? __ldg(g + r * C + c) : 0.f;
-        if (g16) v += __bfloat162float(g16[r * C + c]);
+    for (int u = 0; u < 4; ++u) {
+      const int64_t rr = r + u;
+      int nn = n + u;
+      while (nn >= N) nn -= N;
+      const bool ok = rr < w1;
+      tok[u] = ok ? 2 * __ldg(ctype + nn) + __ldg(det + rr) : -1;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) acc[k][j] += (tok == k) ? v : 0.f;
+      for (int j = 0; j < kSlots; ++j) {
+        const int c = lane + 32 * j;
+        float x = 0.f;
+        if (ok && c < C) {
+          if (g) x = __ldg(g + rr * C + c);
+          if (g16) x += __bfloat162float(g16[rr * C + c]);
+        }
+        v[u][j] = x;
       }
     }
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int j = 0; j < kSlots; ++j)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) acc[k][j] += (tok[u] == k) ? v[u][j] : 0.f;
+    n += 4;
+    while (n >= N) n -= N;
   }
 #pragma unroll
   for (int k = 0; k < 4; ++k)
