@@ -167,8 +167,9 @@ __global__ void __launch_bounds__(256) gelu_residual_bwd_kernel(const void* __re
        u += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     float g[8];
     if (F32) {
-      const float4 g0 = reinterpret_cast<const float4*>(gy)[2 * u];
-      const float4 g1 = reinterpret_cast<const float4*>(gy)[2 * u + 1];
+      const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 g0 = gy ? reinterpret_cast<const float4*>(gy)[2 * u] : z;       // no gy: that output is unused
+      const float4 g1 = gy ? reinterpret_cast<const float4*>(gy)[2 * u + 1] : z;
       g[0] = g0.x; g[1] = g0.y; g[2] = g0.z; g[3] = g0.w;
       g[4] = g1.x; g[5] = g1.y; g[6] = g1.z; g[7] = g1.w;
       if (gy16) {
@@ -365,7 +366,7 @@ extern "C" int bpc_gelu_residual_bwd(const void* gy, const void* gy_bf16, const 
   const bool f32 = gy_dtype == BPC_DTYPE_F32;
   if (!f32 && (gy_bf16 || gh)) return fail(BPC_ERR_ARG, "the bf16 stream takes no second gradient and no gh");
   if (sh.units == 0) return 0;
-  if (!gy || !a || !ga) return fail(BPC_ERR_ARG, "null buffer");
+  if ((!gy && !(f32 && gy_bf16)) || !a || !ga) return fail(BPC_ERR_ARG, "null buffer");
   if ((reinterpret_cast<uintptr_t>(gy) | reinterpret_cast<uintptr_t>(gy_bf16) | reinterpret_cast<uintptr_t>(a) |
        reinterpret_cast<uintptr_t>(gh) | reinterpret_cast<uintptr_t>(ga)) & 15)
     return fail(BPC_ERR_ARG, "gy, gy_bf16, a, gh and ga must be 16-byte aligned");

@@ -270,6 +270,7 @@ class BipartiteStepB200(torch.autograd.Function):
                                      y16.data_ptr() if f32 else None, B, NT, Co, T, hdt, st)
         _lib.check(rc, "bpc_gelu_residual_fwd")
         ctx.save_for_backward(x, a, *w16)
+        ctx.set_materialize_grads(False)     # an unused output's gradient stays None, not a zero-filled tensor
         ctx.tables, ctx.f32, ctx.has_h = tables, f32, h is not None
         return (y, y16) if f32 else y
 
@@ -280,13 +281,16 @@ class BipartiteStepB200(torch.autograd.Function):
         NT = T * NTt
         L = _lib.lib()
         st = _stream_ptr(x.device)
+        if gy is None and gy16 is None:
+            return (None, None, None, *([None] * T))
         gh = None
         ga = torch.empty_like(a)
         if ctx.f32:
-            gy = gy.float().contiguous()
+            gy = gy.float().contiguous() if gy is not None else None
             g16 = gy16.to(torch.bfloat16).contiguous() if gy16 is not None else None
-            gh = torch.empty_like(gy) if ctx.needs_input_grad[1] else None
-            rc = L.bpc_gelu_residual_bwd(gy.data_ptr(), g16.data_ptr() if g16 is not None else None, a.data_ptr(),
+            gh = torch.empty(B, NT, Co, device=x.device, dtype=torch.float32) if ctx.needs_input_grad[1] else None
+            rc = L.bpc_gelu_residual_bwd(gy.data_ptr() if gy is not None else None,
+                                         g16.data_ptr() if g16 is not None else None, a.data_ptr(),
                                          gh.data_ptr() if gh is not None else None, ga.data_ptr(), B, NT, Co, T,
                                          _lib.BPC_DTYPE_F32, st)
         else:
@@ -321,6 +325,7 @@ class EmbedTokensB200(torch.autograd.Function):
                                              h16.data_ptr(), B, N, C, _stream_ptr(det.device))
         _lib.check(rc, "bpc_embed_tokens_fwd")
         ctx.save_for_backward(det, check_type)
+        ctx.set_materialize_grads(False)     # an unused output's gradient stays None
         ctx.C = C
         return h, h16
 

@@ -80,7 +80,8 @@ BPC_API int bpc_residual_affine_silu(const float* h, const void* u, float* out, 
  * one call; torch runs GELU, the residual add and the casts as separate kernels):
  *   forward   y = h + bf16(GELU(a))   h bf16 -> y bf16 (rounded once); h f32 -> y f32 and y_bf16 = bf16(y);
  *             h NULL -> y = bf16(GELU(a)) (h_dtype ignored)
- *   backward  g = gy (+ gy_bf16, f32 stream only);  gh = g (f32 stream; may be NULL);
+ *   backward  g = gy (+ gy_bf16, f32 stream only; on the f32 stream either may be NULL = zero);  gh = g (f32
+ *             stream; may be NULL);
  *             ga = bf16(GELU'(a) * g), g rounded to bf16 first on the f32 stream
  * a and ga are bf16 (n_types, B, NT / n_types, C): the pre-activations of target type t are one contiguous block;
  * h, y, gy, gh are (B, NT, C).  GELU is the tanh form.  C % 8 == 0, every pointer 16-byte aligned. */
