@@ -71,16 +71,18 @@ __global__ void __launch_bounds__(256) residual_affine_silu_kernel(const float* 
 // a and ga hold the pre-activations type-major: (T, B, NT / T, C), so that each target type's op output and input
 // gradient is one contiguous (B, NT / T, C) block; h, y, gy, gh are (B, NT, C).
 // GELU in the tanh form g(x) = x (1 + tanh(k (x + c x^3))) / 2, k = sqrt(2 / pi), c = 0.044715, with
-// g'(x) = (1 + t) / 2 + x (1 - t^2) k (1 + 3 c x^2) / 2, t = tanh(k (x + c x^3)); tanhf (accurate) in both.
+// g'(x) = (1 + t) / 2 + x (1 - t^2) k (1 + 3 c x^2) / 2, t = tanh(k (x + c x^3)), t from the hardware tanh.approx
+// (relative error about 2^-11, below the bf16 rounding both results get; accurate tanhf made these passes
+// instruction-bound rather than HBM-bound).
 constexpr float kGeluK = 0.7978845608028654f;
 constexpr float kGeluC = 0.044715f;
 
 __device__ __forceinline__ float gelu_acc(float x) {
-  const float t = tanhf(kGeluK * fmaf(kGeluC * x, x * x, x));
+  const float t = tanh_approx(kGeluK * fmaf(kGeluC * x, x * x, x));
   return 0.5f * x * (1.0f + t);
 }
 __device__ __forceinline__ float gelu_grad(float x) {
-  const float t = tanhf(kGeluK * fmaf(kGeluC * x, x * x, x));
+  const float t = tanh_approx(kGeluK * fmaf(kGeluC * x, x * x, x));
   return 0.5f * (1.0f + t) + 0.5f * x * (1.0f - t * t) * kGeluK * fmaf(3.0f * kGeluC, x * x, 1.0f);
 }
 __device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
@@ -95,10 +97,23 @@ struct StepShape {
   int64_t units;     // B * NT * C / 8
   int64_t B;
   int32_t NT, NTt, C8;
+  bool one_type;     // T = 1: the pre-activation layout is the row layout
+  bool small;        // units < 2^32: the index arithmetic fits 32-bit divisions
 };
 
 // offset (elements) of pre-activation unit u in the type-major (T, B, NT / T, C) layout
 __device__ __forceinline__ int64_t pre_off(const StepShape& sh, int64_t u) {
+  if (sh.one_type) return 8 * u;
+  if (sh.small) {
+    const uint32_t uu = static_cast<uint32_t>(u);
+    const uint32_t row = uu / static_cast<uint32_t>(sh.C8);
+    const uint32_t c8 = uu - row * static_cast<uint32_t>(sh.C8);
+    const uint32_t b = row / static_cast<uint32_t>(sh.NT);
+    const uint32_t n = row - b * static_cast<uint32_t>(sh.NT);
+    const uint32_t t = n / static_cast<uint32_t>(sh.NTt);
+    return ((static_cast<int64_t>(t) * sh.B + b) * sh.NTt + (n - t * sh.NTt)) * (8 * static_cast<int64_t>(sh.C8)) +
+           8 * c8;
+  }
   const int64_t row = u / sh.C8;
   const int c8 = static_cast<int>(u - row * sh.C8);
   const int64_t b = row / sh.NT;
@@ -318,6 +333,8 @@ int step_shape(int64_t B, int32_t NT, int32_t C, int32_t n_types, StepShape* sh)
   sh->NTt = NT / n_types;
   sh->C8 = C / 8;
   sh->units = B * NT * (C / 8);
+  sh->one_type = n_types == 1;
+  sh->small = sh->units < (int64_t(1) << 32);
   return 0;
 }
 
