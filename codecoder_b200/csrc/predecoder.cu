@@ -84,25 +84,29 @@ __global__ void __launch_bounds__(256) embed_kernel(const uint8_t* __restrict__ 
       if (lane == 0 && word < words) bits[static_cast<int64_t>(n) * words + word] = m;
     }
   }
-  // features in 8-element groups (16 bytes of bf16, 32 of fp32: two 16-byte vectors), one (node, group, shot)
-  // element per thread and iteration, shots fastest (contiguous in the chunked layout)
+  // features in 8-element groups (16 bytes of bf16, 32 of fp32: two 16-byte vectors): one warp per (node, group),
+  // lanes over the shots (contiguous in the chunked layout); a block's shots lie in one tile of the chunked layout
+  // (kEmbShots divides tm), so the tile offset is computed once
   constexpr int kVec = 16 / sizeof(T);
   const int groups = C / 8;
   const int smax = static_cast<int>((shots - s0) < kEmbShots ? (shots - s0) : kEmbShots);
-  const int per_node = groups * smax;
-  for (int e = threadIdx.x; e < kEmbNodes * per_node; e += blockDim.x) {
-    const int j = e / per_node;
-    const int rem = e - j * per_node;
-    const int g = rem / smax, s = rem - g * smax;
+  const int64_t tile_off = tm ? (s0 / tm) * C * static_cast<int64_t>(tm) : 0;
+  const int s_in_tile = tm ? static_cast<int>(s0 % tm) : 0;
+  for (int jg = warp; jg < kEmbNodes * groups; jg += blockDim.x / 32) {
+    const int j = jg / groups, g = jg - j * groups;
     const int n = n0 + j;
-    if (n >= N_c) continue;
-    const int tok = 2 * types[j] + tile[j][s];
-    const int64_t shot = s0 + s;
+    if (n >= N_c) break;
     T* base = hc + static_cast<int64_t>(n) * node_stride;
-    T* dst = tm ? base + (shot / tm) * C * tm + g * tm * 8 + (shot % tm) * 8 : base + g * cg_stride + shot * shot_stride;
-    const uint4* src = reinterpret_cast<const uint4*>(emb + tok * C + g * 8);
+    T* gbase = tm ? base + tile_off + static_cast<int64_t>(g) * tm * 8 + static_cast<int64_t>(s_in_tile) * 8
+                  : base + g * cg_stride + s0 * shot_stride;
+    const int64_t sstep = tm ? 8 : shot_stride;
+    for (int s = lane; s < smax; s += 32) {
+      const int tok = 2 * types[j] + tile[j][s];
+      const uint4* src = reinterpret_cast<const uint4*>(emb + tok * C + g * 8);
+      T* dst = gbase + s * sstep;
 #pragma unroll
-    for (int v = 0; v < 8 / kVec; ++v) reinterpret_cast<uint4*>(dst)[v] = src[v];
+      for (int v = 0; v < 8 / kVec; ++v) reinterpret_cast<uint4*>(dst)[v] = src[v];
+    }
   }
 }
 
@@ -269,6 +273,7 @@ extern "C" int bpc_predecoder_forward(bpc_predecoder* h, const uint8_t* det, flo
   const int64_t cg_stride = 8;
   const int64_t node_stride = L.S * c.channels;
   if (shot_tiles && L.S % tm != 0) return fail(BPC_ERR_ARG, "pass size is not a multiple of the tensor-core tile");
+  if (tm % kEmbShots != 0) return fail(BPC_ERR_ARG, "the embedding's shot block must divide the tensor-core tile");
   GmmProblem c2d, d2c;
   c2d.x = hc;
   c2d.blocked = shot_tiles;
