@@ -51,7 +51,7 @@ class StreamingDecoder:
         """The current window (1, N_c) on the device."""
         return self.win[self.cur]
 
-    def _work(self, src: int):
+    def _round(self, src: int):
         W, nh = self.W, self.nh
         cur, nxt = self.win[src].view(2, W, nh), self.win[1 - src].view(2, W, nh)
         self.new_dev.copy_(self.new_host, non_blocking=True)
@@ -62,8 +62,8 @@ class StreamingDecoder:
     def capture(self):
         """Warm up (first launches configure the kernels) and capture one graph per window buffer."""
         with torch.cuda.device(self.device), torch.cuda.stream(self.stream):
-            self._work(0)
-            self._work(1)
+            self._round(0)
+            self._round(1)
             self.stream.synchronize()
             for w in self.win:
                 w.zero_()
@@ -72,7 +72,7 @@ class StreamingDecoder:
             for src in range(2):
                 g = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(g, stream=self.stream):
-                    self._work(src)
+                    self._round(src)
                 self.graphs.append(g)
             self.stream.synchronize()            # this stream only: a resident kernel may run on another
         self.cur = 0
