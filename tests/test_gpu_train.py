@@ -94,3 +94,64 @@ def test_fused_steps_match_the_unfused_network():
     for k in pu:
         if pu[k].requires_grad:
             assert rel(pf[k].grad, pu[k].grad) < 2e-2, (k, rel(pf[k].grad, pu[k].grad))
+
+
+@pytest.mark.parametrize("f32", [True, False])
+def test_gelu_residual_passes_match_torch(f32):
+    """bpc_gelu_residual_fwd / _bwd through the C ABI against torch's composition of the same step (bf16 GELU in the
+    tanh form, residual add, cast; and back): the residual gradient exactly, GELU and its gradient to bf16 rounding
+    (the kernels use the hardware tanh.approx)."""
+    from codecoder_b200 import _lib
+    torch.manual_seed(3)
+    T, B, NTt, C = 2, 40, 37, 96
+    NT = T * NTt
+    dev = "cuda"
+    a = torch.randn(T, B, NTt, C, device=dev).to(torch.bfloat16)
+    a_rows = a.permute(1, 0, 2, 3).reshape(B, NT, C)          # type-major block -> (B, NT, C)
+    h = torch.randn(B, NT, C, device=dev, dtype=torch.float32 if f32 else torch.bfloat16)
+    L = _lib.lib()
+    st = torch.cuda.current_stream().cuda_stream
+    dt = _lib.BPC_DTYPE_F32 if f32 else _lib.BPC_DTYPE_BF16
+    y = torch.empty_like(h)
+    y16 = torch.empty(B, NT, C, device=dev, dtype=torch.bfloat16) if f32 else None
+    _lib.check(L.bpc_gelu_residual_fwd(a.data_ptr(), h.data_ptr(), y.data_ptr(), y16.data_ptr() if f32 else None,
+                                       B, NT, C, T, dt, st), "fwd")
+    u = F.gelu(a_rows.float(), approximate="tanh").to(torch.bfloat16)
+    y_ref = h + u.float() if f32 else (h.float() + u.float()).to(torch.bfloat16)
+    assert rel(y, y_ref) < 1e-2
+    if f32:
+        assert torch.equal(y16, y.to(torch.bfloat16))
+    gy = torch.randn(B, NT, C, device=dev, dtype=torch.float32 if f32 else torch.bfloat16)
+    gy16 = torch.randn(B, NT, C, device=dev).to(torch.bfloat16) if f32 else None
+    gh = torch.empty(B, NT, C, device=dev, dtype=torch.float32) if f32 else None
+    ga = torch.empty_like(a)
+    _lib.check(L.bpc_gelu_residual_bwd(gy.data_ptr(), gy16.data_ptr() if f32 else None, a.data_ptr(),
+                                       gh.data_ptr() if f32 else None, ga.data_ptr(), B, NT, C, T, dt, st), "bwd")
+    g = gy + gy16.float() if f32 else gy.float()
+    if f32:
+        assert torch.equal(gh, g)
+    x = a_rows.float().requires_grad_(True)
+    F.gelu(x, approximate="tanh").backward(g.to(torch.bfloat16).float())
+    ga_ref = x.grad.to(torch.bfloat16).reshape(B, T, NTt, C).permute(1, 0, 2, 3)
+    assert rel(ga, ga_ref) < 2e-2
+
+
+def test_embed_tokens_match_torch():
+    """bpc_embed_tokens_fwd / _bwd through ops.embed_tokens against F.embedding and its autograd gradient: the
+    features exactly, the weight gradient to fp32 summation order."""
+    from codecoder_b200.ops import embed_tokens
+    g = RotatedSurface(5, 5)
+    det, _ = sample(g, 0.05, 300, 61)
+    det = torch.as_tensor(det).cuda()
+    ctype = torch.as_tensor(g.check_type.astype(np.uint8)).cuda()
+    E = torch.randn(4, 64, device="cuda", requires_grad=True)
+    h, h16 = embed_tokens(det, ctype, E)
+    E_ref = E.detach().clone().requires_grad_(True)
+    h_ref = F.embedding(2 * ctype.long() + det.long(), E_ref)
+    assert torch.equal(h, h_ref) and torch.equal(h16, h_ref.to(torch.bfloat16))
+    gh = torch.randn_like(h)
+    gh16 = torch.randn_like(h).to(torch.bfloat16)
+    (h * gh).sum().backward(retain_graph=True)
+    (h16.float() * gh16.float()).sum().backward()
+    (h_ref * (gh + gh16.float())).sum().backward()
+    assert rel(E.grad, E_ref.grad) < 1e-5
