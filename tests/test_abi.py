@@ -65,3 +65,34 @@ def test_ops_refuse_cpu_tensors():
     with pytest.raises(RuntimeError, match="CUDA"):
         gmm(torch.zeros(1, 4, 64, dtype=torch.bfloat16), torch.zeros(2, 8, dtype=torch.int32),
             torch.zeros(64, 512, dtype=torch.bfloat16))
+
+
+def test_training_entry_points_check_arguments_first(lib):
+    """The training network's passes reject bad shapes and null buffers with BPC_ERR_ARG before any device work, and
+    an empty batch is a no-op."""
+    bf16, f32 = _lib.BPC_DTYPE_BF16, _lib.BPC_DTYPE_F32
+    # NT not a multiple of the type count, C not a multiple of 8
+    assert lib.bpc_gelu_residual_fwd(None, None, None, None, 4, 7, 64, 2, bf16, None) == 2
+    assert "multiple" in _lib.last_error()
+    assert lib.bpc_gelu_residual_fwd(None, None, None, None, 4, 8, 60, 2, bf16, None) == 2
+    # null buffers
+    assert lib.bpc_gelu_residual_fwd(None, None, None, None, 4, 8, 64, 2, bf16, None) == 2
+    assert "null" in _lib.last_error()
+    # the bf16 stream takes neither a second gradient nor gh
+    assert lib.bpc_gelu_residual_bwd(16, 16, 16, 16, 16, 4, 8, 64, 2, bf16, None) == 2
+    assert lib.bpc_gelu_residual_bwd(None, None, None, None, None, 4, 8, 64, 2, f32, None) == 2
+    # empty batches
+    assert lib.bpc_gelu_residual_fwd(None, None, None, None, 0, 8, 64, 2, bf16, None) == 0
+    assert lib.bpc_gelu_residual_bwd(None, None, None, None, None, 0, 8, 64, 2, f32, None) == 0
+    # embedding: C limits, null buffers, workspace size
+    assert lib.bpc_embed_tokens_fwd(None, None, None, None, None, 4, 10, 60, None) == 2
+    assert lib.bpc_embed_tokens_fwd(None, None, None, None, None, 4, 10, 64, None) == 2
+    assert lib.bpc_embed_tokens_fwd(None, None, None, None, None, 0, 10, 64, None) == 0
+    assert lib.bpc_embed_tokens_bwd_workspace_size(96) >= 4 * 96 * 4
+    assert lib.bpc_embed_tokens_bwd(None, None, None, None, 16, None, 0, 4, 10, 300, None) == 2
+    assert lib.bpc_embed_tokens_bwd(None, None, None, None, 16, None, 0, 4, 10, 96, None) == 2
+    # accumulating input gradient: shape and dtype checks
+    assert lib.bpc_gather_mm_dgrad_ex(None, None, None, None, None, 4, 0, 10, 8, 64, 64, 1, bf16, None) == 2
+    assert lib.bpc_gather_mm_dgrad_ex(None, None, None, None, None, 4, 10, 10, 8, 64, 64, 1, 9, None) == 2
+    assert lib.bpc_gather_mm_dgrad_ex(None, None, None, None, None, 4, 10, 10, 8, 64, 64, 1, bf16, None) == 2
+    assert "null" in _lib.last_error()
