@@ -29,9 +29,14 @@ REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 
 METRIC = "syndromes/sec/GPU at d=13 (1/2/4/8 B200, % roofline); p99 per-round latency d=17"
-UNIT = "syndromes/s"
+UNIT = "syndromes/s (aggregate over all GPUs)"
 TOTAL_SHOTS = 262144
 SEED = 1234
+# DRAM bytes per (target node x shot) of one d = 13 bipartite step of gmm_wide_kernel, from one ncu capture of a
+# 4,096-shot check -> data launch: (dram__bytes_read.sum + dram__bytes_write.sum) / (2,197 nodes x 4,096 shots).
+# Traffic grows in proportion to the shots, so it is scaled to the shots of a launch.
+WIDE_D13_DRAM_BYTES_PER_NODE_SHOT = 766.4
+PARITY_SHOTS = 64
 
 
 def parse():
@@ -46,6 +51,7 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-parity", action="store_true")
     ap.add_argument("--no-stream", action="store_true")
     ap.add_argument("--stream-rounds", type=int, default=20000)
     ap.add_argument("--no-train", action="store_true")
@@ -133,59 +139,83 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(busy), "power_w_max": max(r[2] for r in rows)}
 
 
+CPU_BATCHES = (1, 2, 4, 8, 16, 64)
+
+
+def best_cpu_batch(g, cfg32, params, det):
+    """The reference's CPU path (restated by the oracle: fp32 torch index_select + matmul on every host thread) is
+    fastest at a small batch, where the materialised (B, NT, K C) gather stays in cache.  One warm-up and one timed
+    call per candidate batch -> (batch, shots/s at that batch)."""
+    import torch
+    from oracle import predecoder_oracle as orc
+    best = (1, 0.0)
+    with torch.no_grad():
+        for b in CPU_BATCHES:
+            if b > len(det):
+                break
+            orc.predecoder(g, cfg32, params, det[:b], dtype=torch.float32)
+            t = time.perf_counter()
+            orc.predecoder(g, cfg32, params, det[:b], dtype=torch.float32)
+            rate = b / (time.perf_counter() - t)
+            if rate > best[1]:
+                best = (b, rate)
+    return best
+
+
 def cpu_rate(g, cfg, params, det, seconds):
-    """The CPU oracle (fp32 torch on every host thread) on a bounded sample -> (shots/s, shots, threads)."""
+    """The CPU oracle (fp32 torch on every host thread) at its best batch on a bounded sample
+    -> (shots/s, shots, threads, batch)."""
     import torch
     from oracle import predecoder_oracle as orc
     torch.set_num_threads(os.cpu_count() or 1)
     cfg32 = replace(cfg, dtype="f32")
-    batch = 2
-    done, t0 = 0, time.perf_counter()
+    batch, _ = best_cpu_batch(g, cfg32, params, det)
+    done = 0
     with torch.no_grad():
-        orc.predecoder(g, cfg32, params, det[:1], dtype=torch.float32)      # warm-up
         t0 = time.perf_counter()
         while True:
-            sl = det[done % len(det):done % len(det) + batch]
-            orc.predecoder(g, cfg32, params, sl, dtype=torch.float32)
-            done += len(sl)
+            b0 = (done // batch * batch) % (len(det) - batch + 1)
+            orc.predecoder(g, cfg32, params, det[b0:b0 + batch], dtype=torch.float32)
+            done += batch
             if time.perf_counter() - t0 >= seconds:
                 break
     dt = time.perf_counter() - t0
-    return done / dt, done, torch.get_num_threads()
+    return done / dt, done, torch.get_num_threads(), batch
 
 
 def run_reference(args, cfg, g, params, rank, world):
-    """--impl reference: the CPU path of the reference (restated by the oracle), rank 0 only."""
+    """--impl reference: the CPU path of the reference (restated by the oracle) at its best batch, rank 0 only."""
     if rank != 0:
         return
-    import numpy as np
     import torch
     from codecoder_b200.sampler import sample
     from oracle import predecoder_oracle as orc
     torch.set_num_threads(os.cpu_count() or 1)
     det, _ = sample(g, cfg.p, 64, SEED)
     cfg32 = replace(cfg, dtype="f32")
-    t0 = time.perf_counter()
-    with torch.no_grad():
-        orc.predecoder(g, cfg32, params, det[:1], dtype=torch.float32)
-    per_shot = max(time.perf_counter() - t0, 1e-3)
-    shots = int(max(1, min(64, 10.0 / per_shot)))          # a step of about 10 s
+    batch, probe_rate = best_cpu_batch(g, cfg32, params, det)
+    # a step is n_batch calls at the best batch, about 2 s of CPU work
+    n_batch = int(max(1, min(64, round(2.0 * probe_rate / batch))))
     times = []
     with torch.no_grad():
         for k in range(args.warmup + args.steps):
             t = time.perf_counter()
-            orc.predecoder(g, cfg32, params, det[:shots], dtype=torch.float32)
+            for i in range(n_batch):
+                b0 = (i * batch) % (len(det) - batch + 1)
+                orc.predecoder(g, cfg32, params, det[b0:b0 + batch], dtype=torch.float32)
             if k >= args.warmup:
                 times.append(time.perf_counter() - t)
     total = sum(times)
+    shots = n_batch * batch
     rate = shots * len(times) / total
-    sample_desc = f"{shots} shots per step of the d={cfg.d} workload (fp32 CPU oracle)"
+    sample_desc = (f"{shots} shots per step of the d={cfg.d} workload ({n_batch} calls at batch {batch}, the fastest of "
+                   f"{list(CPU_BATCHES)}), fp32 CPU oracle of the reference's gather_mm path")
     line = {"metric": METRIC, "value": rate, "unit": UNIT, "impl": "reference", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / len(times),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "config": workload(cfg, g, args.shots // world, world),
             "cpu_baseline": {"value": rate, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
-                             "sample": sample_desc},
+                             "sample": sample_desc, "batch": batch},
             "e2e": {"value": rate, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -291,20 +321,43 @@ def main():
             "flop_per_unit": 2 * cfg.K * cfg.channels ** 2, "unit_desc": "target node x shot",
             "executed_tflops": sum(exec_flops) / (tc_ms / 1000.0) / 1e12,
             "whole_step_frac": value / world * fps / 1e12 / pk["bf16_tflops_sustained"]}
-    tr_path = os.path.join(REPO, "profiles", "gmm_tc_d13_traffic.txt")
-    if os.path.exists(tr_path) and args.config == "d13_bf16":
-        per_unit = None
-        for line in open(tr_path):
-            if line.startswith("bytes_per_node_shot:"):
-                per_unit = float(line.split(":", 1)[1])
-        if per_unit:
-            units_per_launch = (sum(step_flops) / len(step_flops)) / (2 * cfg.K * cfg.channels ** 2)
-            roof["traffic"] = per_unit * units_per_launch
-            roof["traffic_unit"] = "bytes per launch (ncu capture scaled by shots)"
-            # sources read once + residual read + write, each 2C bytes per node and shot, averaged over the launches
-            roof["algorithmic_bytes_per_launch"] = sum(
-                (g.N_c + 2 * g.N_d if i % 2 == 0 else g.N_d + 2 * g.N_c) * sb * 2 * cfg.channels
-                for i, sb in enumerate(sb for sb in chunks for _ in range(2 * cfg.layers))) / len(step_flops)
+    if args.config == "d13_bf16":
+        units_per_launch = (sum(step_flops) / len(step_flops)) / (2 * cfg.K * cfg.channels ** 2)
+        roof["traffic"] = WIDE_D13_DRAM_BYTES_PER_NODE_SHOT * units_per_launch
+        roof["traffic_unit"] = "DRAM bytes per launch"
+        roof["traffic_source"] = ("ncu capture of one gmm_wide_kernel launch, d=13 check->data step, 4,096 shots "
+                                  "(dram__bytes_read.sum + dram__bytes_write.sum / (2,197 nodes x 4,096 shots)), "
+                                  "scaled by the shots of a launch")
+        # sources read once + residual read + write, each 2C bytes per node and shot, averaged over the launches
+        roof["algorithmic_bytes_per_launch"] = sum(
+            (g.N_c + 2 * g.N_d if i % 2 == 0 else g.N_d + 2 * g.N_c) * sb * 2 * cfg.channels
+            for i, sb in enumerate(sb for sb in chunks for _ in range(2 * cfg.layers))) / len(step_flops)
+
+    parity = None
+    if rank == 0 and not args.no_parity:
+        # the timed run's own outputs for a fixed sample of its shots (spread over every pass) against the CPU
+        # oracle, outside the timed region: the logit error, the band count and the residual bits
+        import torch as _t
+        from oracle import predecoder_oracle as orc
+        from codecoder_b200.params import storage_params
+        _t.set_num_threads(os.cpu_count() or 1)
+        pick = np.unique(np.linspace(0, shots - 1, min(PARITY_SHOTS, shots)).astype(np.int64))
+        sel = _t.as_tensor(pick, device=dev)
+        det_s = det.index_select(0, sel).cpu().numpy()
+        lg_s = logits.index_select(0, sel).cpu().numpy()
+        rs_s = resid.index_select(0, sel).cpu().numpy()
+        sp = storage_params(cfg, params)
+        ref64, res64 = orc.predecoder_batched(g, cfg, sp, det_s, dtype=_t.float64, batch=16)
+        if cfg.dtype == "f32":
+            parity = orc.parity_report(g, det_s, lg_s, rs_s, ref64, res64, 1e-4)
+            parity["pass"] = bool(parity["logit_max_rel_err"] < 1e-4 and parity["residual_mismatch_outside_band"] == 0
+                                  and parity["residual_is_own_xor"])
+        else:
+            ref32, _ = orc.predecoder_batched(g, cfg, sp, det_s, dtype=_t.float32, batch=16)
+            parity = orc.deep_parity(g, det_s, lg_s, rs_s, ref64, res64, ref32, 2e-2)
+        parity["sample"] = (f"{len(pick)} shots spread over the timed batch (the last timed step's outputs) against "
+                            f"the CPU oracle (float64 accumulation, bf16 storage rounding emulated; float32 "
+                            f"accumulation for the oracle's own spread)")
 
     e2e = None
     if not args.no_e2e:
@@ -332,10 +385,11 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         det_np = det[:64].cpu().numpy()
-        rate, n_shots, threads = cpu_rate(g, cfg, params, det_np, args.cpu_seconds)
-        cpu = {"value": rate, "unit": UNIT, "cores": threads, "kind": "port",
+        rate, n_shots, threads, cb = cpu_rate(g, cfg, params, det_np, args.cpu_seconds)
+        cpu = {"value": rate, "unit": UNIT, "cores": threads, "kind": "port", "batch": cb,
                "sample": f"{n_shots} shots of the d={cfg.d} workload through the CPU oracle (fp32 torch "
-                         f"index_select + matmul, the reference's gather_mm path), {threads} threads"}
+                         f"index_select + matmul, the reference's gather_mm path) at batch {cb}, the fastest of "
+                         f"{list(CPU_BATCHES)}, {threads} threads"}
 
     stream = None
     if rank == 0 and world == 1 and not args.no_stream:
@@ -416,7 +470,8 @@ def main():
                 "scaling": "strong", "vs_baseline": None, "dtype": cfg.dtype, "data": "synthetic",
                 "config": workload(cfg, g, shots, world), "per_gpu": value / world, "roofline": roof,
                 "cpu_baseline": cpu, "e2e": e2e, "clocks": clk.summary(),
-                "gpu_launches": launches_per_fwd * args.steps, "flop_per_shot": fps, "streaming": stream, "train": train}
+                "gpu_launches": launches_per_fwd * args.steps, "flop_per_shot": fps, "parity": parity,
+                "streaming": stream, "train": train}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

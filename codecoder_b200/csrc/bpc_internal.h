@@ -111,6 +111,9 @@ int predecoder_internals(const struct bpc_predecoder* h, bpc_predecoder_config* 
                          const void** w_c2d, const void** w_d2c, const float** head_w, const float** head_b,
                          const int32_t** c2d, const int32_t** d2c, const int32_t** xor_nbr);
 
+// CUDA device ordinal that was current when the pre-decoder handle was created (its tables and weights live there).
+int predecoder_device(const struct bpc_predecoder* h);
+
 // Device status word of the stand-alone op entry points (bpc_gather_mm_*), one per device.
 int* op_status_ptr();
 

@@ -19,6 +19,7 @@
 
 struct bpc_predecoder {
   bpc_predecoder_config cfg;
+  int device = 0;                // device current at create: tables, weights and status word live there
   int32_t* c2d = nullptr;        // (N_d, K)
   int32_t* d2c = nullptr;        // (N_c, K)
   int32_t* xor_nbr = nullptr;    // (N_d, 2, 2)
@@ -176,6 +177,10 @@ extern "C" int bpc_predecoder_create(const bpc_predecoder_config* cfg, const int
     return fail(BPC_ERR_ARG, "invalid pre-decoder configuration");
   auto* h = new bpc_predecoder();
   h->cfg = c;
+  if (cudaGetDevice(&h->device) != cudaSuccess) {
+    delete h;
+    return fail(BPC_ERR_LAUNCH, "cudaGetDevice failed");
+  }
   int e = 0;
   if ((e = copy_in(&h->c2d, c2d, sizeof(int32_t) * c.n_data * c.K)) ||
       (e = copy_in(&h->d2c, d2c, sizeof(int32_t) * c.n_checks * c.K)) ||
@@ -426,6 +431,10 @@ int predecoder_internals(const bpc_predecoder* h, bpc_predecoder_config* cfg, co
   *xor_nbr = h->xor_nbr;
   return 0;
 }
+}  // namespace bpc
+
+namespace bpc {
+int predecoder_device(const bpc_predecoder* h) { return h ? h->device : -1; }
 }  // namespace bpc
 
 extern "C" int bpc_predecoder_record_step_events(bpc_predecoder* h, void* const* events, int n_pairs) {

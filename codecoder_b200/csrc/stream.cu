@@ -487,6 +487,7 @@ struct bpc_stream {
   void* dev = nullptr;          // hc, hd, ring, res, barrier, abort
   cudaStream_t stream = nullptr;
   bool running = false;
+  bool desynced = false;        // a round was given up before its response: later rounds fail until stop / start
   uint64_t tag = 0;
   int smem = 0;
 };
@@ -612,6 +613,7 @@ extern "C" int bpc_stream_start(bpc_stream* s) {
   if (int e = allow_smem(reinterpret_cast<const void*>(&stream_kernel), s->smem)) return e;
   std::memset(s->host, 0, 65536);
   s->tag = 0;
+  s->desynced = false;
   if (cudaMemsetAsync(s->args.bar, 0, 256, s->stream) != cudaSuccess ||
       cudaMemsetAsync(s->args.ring, 0, 2 * s->args.W * s->args.nh, s->stream) != cudaSuccess)
     return fail(BPC_ERR_LAUNCH, "cudaMemsetAsync failed");
@@ -667,6 +669,8 @@ extern "C" int bpc_stream_round(bpc_stream* s, const uint8_t* round_dets, uint8_
                                 int64_t timeout_us) {
   if (!s || !round_dets) return fail(BPC_ERR_ARG, "null argument");
   if (!s->running) return fail(BPC_ERR_ARG, "the stream kernel is not running");
+  if (s->desynced)
+    return fail(BPC_ERR_DEVICE, "an earlier round timed out before its response; stop and start the stream again");
   const StreamArgs& a = s->args;
   volatile uint8_t* dst = s->host + kReqDets;
   for (int i = 0; i < 2 * a.nh; ++i) dst[i] = round_dets[i];
@@ -681,8 +685,11 @@ extern "C" int bpc_stream_round(bpc_stream* s, const uint8_t* round_dets, uint8_
       s->running = false;
       return fail(BPC_ERR_DEVICE, "the stream kernel left (status " + std::to_string(st) + ")");
     }
-    if (timeout_us > 0 && std::chrono::steady_clock::now() - t0 > std::chrono::microseconds(timeout_us))
+    if (timeout_us > 0 && std::chrono::steady_clock::now() - t0 > std::chrono::microseconds(timeout_us)) {
+      // the kernel may still answer this round later; a new request would overwrite the line it may be reading
+      s->desynced = true;
       return fail(BPC_ERR_DEVICE, "no response within the timeout");
+    }
   }
   std::atomic_thread_fence(std::memory_order_acquire);
   const uint8_t* src = s->host + kRespOff + kRespData;

@@ -197,8 +197,9 @@ BPC_API void bpc_predecoder_destroy(bpc_predecoder* h);
  * contract as bpc_predecoder_forward, but the scratch is a fixed array inside the library's device image
  * (bpc_noalloc_scratch_bytes(), 64 MiB, held by every GPU that loads the library until exit), so the caller passes
  * only det, logits and residual.  A network whose 256-shot pass needs more scratch than that is rejected with
- * BPC_ERR_SPACE.  The first call on a device looks the array's address up (cudaGetSymbolAddress) and should come
- * before any stream capture; every call shares the array, so calls whose work overlaps on the GPU race.
+ * BPC_ERR_SPACE, and a handle created on another device than the current one with BPC_ERR_ARG.  The first call in
+ * each CUDA context looks the array's address up (cudaGetSymbolAddress) and should come before any stream capture;
+ * every call shares the array, so calls whose work overlaps on the GPU race.
  * No counterpart in the reference (it allocates through torch). */
 BPC_API int bpc_predecoder_forward_noalloc(bpc_predecoder* h, const uint8_t* det, float* logits, uint8_t* residual,
                                            int64_t B, bpc_stream_t stream);

@@ -21,6 +21,10 @@ What it restates:
                  bf16 network rounds every stored activation to bf16 exactly where the device stores bf16, and
                  accumulates in float64 here (fp32 on the device).
   cancel         the GF(2) syndrome cancellation, integer numpy.
+  parity_report / deep_parity
+                 the parity figures of a GPU run against this oracle (logit error, band counts, residual bits);
+                 deep_parity is the bar for deep bf16 networks, whose logits are chaotic in the bf16 rounding of the
+                 stored activations, measured against the oracle's own float32-vs-float64 spread.
 Parity pin: tests/golden/*.npz were produced by the reference's own gather_mm / BipartiteConv (imported from the
 reference tree by tests/golden/make_golden.py); tests/test_oracle.py checks this module against them.
 """
@@ -162,6 +166,74 @@ def predecoder(geo, cfg, params: dict, det: np.ndarray, dtype=torch.float64, ret
     if return_features:
         return logits.numpy(), residual, hc.numpy(), hd.numpy()
     return logits.numpy(), residual
+
+
+def predecoder_batched(geo, cfg, params: dict, det: np.ndarray, dtype=torch.float64, batch: int = 64):
+    """predecoder() over slices of `batch` shots (shots are independent), so the gathered (B, NT, K C) operand stays
+    small at d = 13 -> (logits, residual) concatenated."""
+    det = np.asarray(det, np.uint8)
+    if len(det) == 0:
+        return predecoder(geo, cfg, params, det, dtype=dtype)
+    parts = [predecoder(geo, cfg, params, det[b:b + batch], dtype=dtype) for b in range(0, len(det), batch)]
+    return np.concatenate([p[0] for p in parts]), np.concatenate([p[1] for p in parts])
+
+
+def parity_report(geo, det, logits, residual, logits_ref, residual_ref, tol: float) -> dict:
+    """The parity figures of a GPU run against the oracle on the same shots: max relative logit error, logits inside
+    the band |logit| < tol rms (counted, and the shots that hold one), residual bits that differ at checks outside the
+    band, residual bits that differ anywhere, and whether the residual is exactly the XOR of the run's own
+    thresholded logits."""
+    band = band_mask(logits_ref, tol)
+    own = cancel(det, (np.asarray(logits) > 0).astype(np.uint8), geo)
+    return {"shots": int(len(det)), "tol": tol, "logit_max_rel_err": logit_error(logits, logits_ref),
+            "band_logits": int(band.sum()), "band_shots": int(band.reshape(len(det), -1).any(1).sum()),
+            "logits": int(np.asarray(logits_ref).size),
+            "residual_mismatch_outside_band": residual_mismatch_outside_band(residual, residual_ref, logits_ref, geo,
+                                                                             tol),
+            "residual_mismatch_total": int((np.asarray(residual) != np.asarray(residual_ref)).sum()),
+            "residual_is_own_xor": bool(np.array_equal(own, residual))}
+
+
+def _rel_err_stats(a, ref, rms):
+    rel = np.abs(np.asarray(a) - ref) / np.maximum(np.abs(ref), max(rms, 1e-30))
+    if rel.size == 0:
+        return 0.0, 0.0, 0.0
+    return (float(rel.max()), float(np.quantile(rel, 0.999)),
+            float(np.sqrt(np.mean(np.square(np.asarray(a) - ref)))) / max(rms, 1e-30))
+
+
+def deep_parity(geo, det, logits, residual, ref64, res64, ref32, tol: float = 2e-2) -> dict:
+    """Parity of a deep bf16 network, whose logits are chaotic in the bf16 rounding of every stored activation: two
+    correct restatements of the same arithmetic -- this oracle accumulating in float32 (ref32) and in float64 (ref64),
+    both rounding stored activations to bf16 -- already differ by a few percent at the largest of ~10^6 logits
+    (d = 13, 8 layers), because a rounding decision that tips the other way in an early layer propagates.  The bar,
+    for each of the max, the 99.9th percentile and the RMS of the relative logit error against ref64:
+      statistic <= max(floor, 2 x the same statistic of ref32 against ref64 on the same shots),
+    floors tol (max, p99.9) and tol / 2 (RMS); and
+      residual == XOR of the run's own thresholded logits (exact), and residual == the oracle's at every check none of
+      whose cancelling data nodes has a logit inside the band of the observed error (outside it the sign cannot
+      differ, so this checks the cancellation bit for bit).
+    Band counts are reported at tol and at the observed error."""
+    logits = np.asarray(logits)
+    ref64 = np.asarray(ref64)
+    rms = float(np.sqrt(np.mean(np.square(ref64)))) if ref64.size else 1.0
+    err, p999, rrms = _rel_err_stats(logits, ref64, rms)
+    s_max, s_p999, s_rms = _rel_err_stats(ref32, ref64, rms)
+    band_tol = max(tol, err)
+    own = cancel(det, (logits > 0).astype(np.uint8), geo)
+    rep = {"shots": int(len(det)), "tol": tol, "logits": int(ref64.size),
+           "logit_max_rel_err": err, "logit_p999_rel_err": p999, "logit_rms_rel_err": rrms,
+           "oracle_spread_fp32_vs_fp64": {"max": s_max, "p999": s_p999, "rms": s_rms},
+           "band_logits_at_tol": int(band_mask(ref64, tol).sum()),
+           "band_logits_at_err": int(band_mask(ref64, band_tol).sum()),
+           "band_shots_at_err": int(band_mask(ref64, band_tol).reshape(len(det), -1).any(1).sum()),
+           "residual_mismatch_outside_band": residual_mismatch_outside_band(residual, res64, ref64, geo, band_tol),
+           "residual_mismatch_total": int((np.asarray(residual) != np.asarray(res64)).sum()),
+           "residual_is_own_xor": bool(np.array_equal(own, residual))}
+    rep["pass"] = bool(err <= max(tol, 2 * s_max) and p999 <= max(tol, 2 * s_p999)
+                       and rrms <= max(tol / 2, 2 * s_rms) and rep["residual_mismatch_outside_band"] == 0
+                       and rep["residual_is_own_xor"])
+    return rep
 
 
 def band_mask(logits_ref: np.ndarray, tol: float) -> np.ndarray:

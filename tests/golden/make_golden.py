@@ -1,7 +1,7 @@
 """Generate the golden fixtures of tests/golden from the reference's own code.
 
-Run in a checkout that has the reference tree (default /root/reference, or REFERENCE_ROOT):
-    python tests/golden/make_golden.py
+Run where the reference tree is checked out, naming its root in REFERENCE_ROOT:
+    REFERENCE_ROOT=<reference checkout> python tests/golden/make_golden.py
 It imports the reference's bb.cascade_net (training/bb/ising_compare/bb/cascade_net.py) unchanged and records:
   bb72_c14_conv.npz      the reference's Geometry('bb72') tables, the trained relation matrices of the released C14
                          network's first block (weights/cascade_bb72/C14.pt, key 'ema', rounded to bf16), a seeded
@@ -30,7 +30,9 @@ import torch.nn.functional as F
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-REF = os.environ.get("REFERENCE_ROOT", "/root/reference")
+REF = os.environ.get("REFERENCE_ROOT")
+if not REF or not os.path.isdir(REF):
+    sys.exit("make_golden.py: set REFERENCE_ROOT to the root of the reference checkout")
 sys.path[:0] = [REPO, os.path.join(REF, "training/bb/ising_compare"), os.path.join(REF, "training/bb/qldpc_neural")]
 
 from bb import cascade_net as cn  # noqa: E402  (the reference, unchanged)

@@ -29,7 +29,7 @@ def run(cfg, seed, B, p=None, chunk_shots=16384, oracle_dtype=torch.float64):
     torch.cuda.synchronize()
     assert pd.status() == 0
     lg, rs = logits.cpu().numpy(), res.cpu().numpy()
-    ref_lg, ref_rs = orc.predecoder(g, cfg, storage_params(cfg, params), det, dtype=oracle_dtype)
+    ref_lg, ref_rs = orc.predecoder_batched(g, cfg, storage_params(cfg, params), det, dtype=oracle_dtype)
     return g, det, lg, rs, ref_lg, ref_rs, pd
 
 
@@ -75,6 +75,41 @@ def test_predecoder_d13_bf16_config():
     g, det, lg, rs, ref_lg, ref_rs, _ = run(cfg, 303, 48, p=0.02, oracle_dtype=torch.float32)
     band = check_parity(g, cfg, det, lg, rs, ref_lg, ref_rs)
     print("d13 band logits", band, "of", ref_lg.size)
+
+
+def deep_run(cfg, seed, B):
+    g = RotatedSurface(cfg.d, cfg.rounds)
+    params = init_params(cfg, seed)
+    det, _ = sample(g, cfg.p, B, seed + 1)
+    pd = PreDecoder(g, cfg, params, device=DEV)
+    logits, res = pd(torch.as_tensor(det).to(DEV))
+    torch.cuda.synchronize()
+    assert pd.status() == 0
+    sp = storage_params(cfg, params)
+    ref64, res64 = orc.predecoder_batched(g, cfg, sp, det, dtype=torch.float64)
+    ref32, _ = orc.predecoder_batched(g, cfg, sp, det, dtype=torch.float32)
+    rep = orc.deep_parity(g, det, logits.cpu().numpy(), res.cpu().numpy(), ref64, res64, ref32, 2e-2)
+    print(cfg.name, rep)
+    return rep
+
+
+def test_predecoder_d13_bench_path_full_depth():
+    """The benchmarked configuration as timed: d = 13, 13 rounds, 8 layers, C = 128, bf16, p = 0.005.  320 shots is
+    more than the 64-shot node-tiled limit, so every step runs the wide-tile kernel the benchmark times, over one full
+    and one partial 256-shot tile.  Deep bf16 bar (oracle.deep_parity): the max, p99.9 and RMS relative logit errors
+    each within twice the oracle's own fp32-vs-fp64 spread of the same statistic on the same shots (floors 2e-2, 2e-2,
+    1e-2), residual exact outside the band of the observed error and equal to the XOR of the run's own logits."""
+    cfg = CONFIGS["d13_bf16"]
+    assert (cfg.d, cfg.rounds, cfg.layers, cfg.channels, cfg.dtype, cfg.p) == (13, 13, 8, 128, "bf16", 0.005)
+    rep = deep_run(cfg, 313, 320)
+    assert rep["pass"], rep
+
+
+def test_predecoder_d9_config_full_depth():
+    """d = 9, 9 rounds, 6 layers, C = 64, bf16 at the configuration's p = 0.005, 320 shots (wide-tile kernel with
+    C_in = 64, one full and one partial tile), under the same deep bf16 bar."""
+    rep = deep_run(CONFIGS["d9_bf16"], 212, 320)
+    assert rep["pass"], rep
 
 
 def test_predecoder_d11_c96_tensor_path():

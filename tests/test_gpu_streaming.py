@@ -88,3 +88,29 @@ def test_persistent_stream_idle_watchdog_leaves_a_usable_context():
     lg, rs = PreDecoder(g, cfg, params, device="cuda")(torch.as_tensor(det).cuda())
     torch.cuda.synchronize()
     assert torch.isfinite(lg).all()
+
+
+def test_persistent_stream_round_timeout_refuses_rounds_until_restart():
+    """A round the host gives up on (its timeout ends before the response) leaves the kernel still working on it:
+    a later request would overwrite the line it may be reading, so every later round is refused until the stream is
+    stopped and started again; after the restart rounds are answered again."""
+    from codecoder_b200.streaming import PersistentStreamingDecoder
+    cfg = replace(CONFIGS["d17_stream"], d=9)
+    params = init_params(cfg, 7)
+    rounds = sample_stream(RotatedSurface(9, 1), 0.02, 4, 8)
+    ps = PersistentStreamingDecoder(9, cfg.rounds, cfg, params, device="cuda", idle_timeout_ms=2000)
+    try:
+        ps.start()
+        ps.step(rounds[0])
+        with pytest.raises(RuntimeError, match="within the timeout"):
+            ps.step(rounds[1], timeout_us=1)             # no round is answered within a microsecond
+        with pytest.raises(RuntimeError, match="stop and start"):
+            ps.step(rounds[2])
+        ps.stop()
+        ps.start()
+        res, lg = ps.step(rounds[3])
+        assert np.isfinite(lg).all() and res.shape == (ps.geo.N_c,)
+        ps.stop()
+        assert ps.status() == 2
+    finally:
+        ps.close()

@@ -125,3 +125,36 @@ def test_oracle_cascade_block_matches_reference_c14(bb72, golden_dir):
     out = orc.cascade_block(bf16_to_f32(z["h_bf16"]), p, [bb72["c2d0"], bb72["c2d1"]], [bb72["d2c0"], bb72["d2c1"]],
                             int(z["L"]), str(z["res"]), float(z["eps"]))
     assert _rel(out.numpy(), z["out"]) < 1e-5
+
+
+def test_deep_parity_bar_accepts_a_correct_restatement_and_catches_planted_mistakes():
+    """The full-depth bf16 bar: the oracle's own float32 restatement passes against the float64 one; a residual bit
+    flipped outside the band, a residual that is not the XOR of its own logits, and logits off by a few percent
+    everywhere all fail.  The mistakes are planted in copies of the oracle's outputs, on the CPU."""
+    from codecoder_b200.sampler import sample
+    cfg = PreDecoderConfig(d=5, rounds=5, layers=6, channels=32, dtype="bf16", p=0.02)
+    g = RotatedSurface(cfg.d, cfg.rounds)
+    sp = storage_params(cfg, init_params(cfg, 41))
+    det, _ = sample(g, cfg.p, 96, 42)
+    ref64, res64 = orc.predecoder_batched(g, cfg, sp, det, dtype=torch.float64, batch=32)
+    ref32, res32 = orc.predecoder_batched(g, cfg, sp, det, dtype=torch.float32, batch=32)
+    ok = orc.deep_parity(g, det, ref32, res32, ref64, res64, ref32)
+    assert ok["pass"], ok
+    # a residual bit flipped at a check far from every band logit
+    rep = orc.deep_parity(g, det, ref32, res32, ref64, res64, ref32)
+    band = orc.band_mask(ref64, max(2e-2, rep["logit_max_rel_err"]))
+    touched = np.zeros(res64.shape, bool)
+    for j in range(2):
+        for k in range(2):
+            c = g.xor_nbr[:, j, k]
+            okc = c >= 0
+            bi, ni = np.nonzero(band[:, okc, j])
+            touched[bi, c[okc][ni]] = True
+    b, c = np.argwhere(~touched)[0]
+    bad = res32.copy()
+    bad[b, c] ^= 1
+    r = orc.deep_parity(g, det, ref32, bad, ref64, res64, ref32)
+    assert not r["pass"] and r["residual_mismatch_outside_band"] == 1 and not r["residual_is_own_xor"]
+    # logits 5 % off everywhere
+    r = orc.deep_parity(g, det, ref32 * 1.05, res32, ref64, res64, ref32)
+    assert not r["pass"]

@@ -3,13 +3,14 @@
 It serves callers that cannot allocate device memory -- a host whose memory pool owns the device heap, a real-time
 loop that must not enter the CUDA allocator, a plugin handed only its input and output pointers -- by running the
 forward pass on a scratch array built into the library.  Its results must equal those of the workspace entry point
-(bpc_predecoder_forward, the same kernels), on two calls in a row (the array keeps the previous call's contents),
-and a network too large for the built-in scratch must be refused with a clear error.  This file is collected last.
+(bpc_predecoder_forward, the same kernels) bit for bit, on two calls in a row (the array keeps the previous call's
+contents); after the first call's set-up a call must leave the device's free memory unchanged; a network too large
+for the built-in scratch, and a handle of another device, must be refused with a clear error.  This file is
+collected last.
 """
 import ctypes
 from dataclasses import replace
 
-import numpy as np
 import pytest
 import torch
 
@@ -23,14 +24,10 @@ pytestmark = pytest.mark.gpu
 DEV = "cuda"
 
 
-def noalloc(pd, det):
-    B = det.shape[0]
-    logits = torch.empty(B, pd.geo.N_d, 2, dtype=torch.float32, device=pd.device)
-    residual = torch.empty(B, pd.geo.N_c, dtype=torch.uint8, device=pd.device)
-    rc = _lib.lib().bpc_predecoder_forward_noalloc(pd._h, det.data_ptr(), logits.data_ptr(), residual.data_ptr(), B,
-                                                   torch.cuda.current_stream(pd.device).cuda_stream)
+def noalloc_into(pd, det, logits, residual):
+    rc = _lib.lib().bpc_predecoder_forward_noalloc(pd._h, det.data_ptr(), logits.data_ptr(), residual.data_ptr(),
+                                                   det.shape[0], torch.cuda.current_stream(pd.device).cuda_stream)
     _lib.check(rc, "bpc_predecoder_forward_noalloc")
-    return logits, residual
 
 
 @pytest.mark.parametrize("name,B", [("d9_bf16", 600), ("d5_fp32", 1000)])
@@ -44,13 +41,32 @@ def test_noalloc_matches_workspace_entry_point(name, B):
         det, _ = sample(g, 0.02, B, 809 + call)
         d = torch.as_tensor(det).to(DEV)
         ref_lg, ref_rs = pd(d)
-        lg, rs = noalloc(pd, d)
+        lg = torch.empty(B, g.N_d, 2, dtype=torch.float32, device=DEV)
+        rs = torch.empty(B, g.N_c, dtype=torch.uint8, device=DEV)
         torch.cuda.synchronize()
+        before = (torch.cuda.memory_allocated(), torch.cuda.mem_get_info()[0])
+        noalloc_into(pd, d, lg, rs)
+        torch.cuda.synchronize()
+        after = (torch.cuda.memory_allocated(), torch.cuda.mem_get_info()[0])
         assert pd.status() == 0
-        tol = 1e-4 if cfg.dtype == "f32" else 2e-2
-        scale = max(float(ref_lg.abs().max()), 1e-30)
-        assert float((lg - ref_lg).abs().max()) <= tol * scale
-        assert torch.equal(rs, ref_rs)
+        # the same kernels on a different pass size: chunking does not change a bit
+        assert torch.equal(lg, ref_lg) and torch.equal(rs, ref_rs)
+        if call == 1:                                       # after the first call's set-up: nothing is allocated
+            assert after == before, f"device memory changed across a call: {before} -> {after}"
+
+
+def test_noalloc_refuses_a_handle_of_another_device():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    cfg = replace(CONFIGS["d9_bf16"], layers=1)
+    g = RotatedSurface(cfg.d, cfg.rounds)
+    pd = PreDecoder(g, cfg, init_params(cfg, 3), device="cuda:0")
+    with torch.cuda.device(1):
+        det = torch.zeros(8, g.N_c, dtype=torch.uint8, device="cuda:1")
+        lg = torch.empty(8, g.N_d, 2, dtype=torch.float32, device="cuda:1")
+        rs = torch.empty(8, g.N_c, dtype=torch.uint8, device="cuda:1")
+        rc = _lib.lib().bpc_predecoder_forward_noalloc(pd._h, det.data_ptr(), lg.data_ptr(), rs.data_ptr(), 8, None)
+    assert rc == 2 and "created on device 0" in _lib.last_error()
 
 
 def test_noalloc_refuses_networks_larger_than_its_scratch():
