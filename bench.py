@@ -53,6 +53,7 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-parity", action="store_true")
     ap.add_argument("--no-stream", action="store_true")
+    ap.add_argument("--no-configs", action="store_true", help="skip the d=5 fp32 and d=9 bf16 workloads")
     ap.add_argument("--stream-rounds", type=int, default=20000)
     ap.add_argument("--no-train", action="store_true")
     ap.add_argument("--train-steps", type=int, default=6)
@@ -181,6 +182,82 @@ def cpu_rate(g, cfg, params, det, seconds):
                 break
     dt = time.perf_counter() - t0
     return done / dt, done, torch.get_num_threads(), batch
+
+
+FP32_FMA_PEAK_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12   # nominal: 148 SMs x 128 FP32 FMA/clk x 2 x max SM clock
+
+
+def measure_config(name, shots, steps, warmup, dev, pk, cpu_seconds):
+    """One of the other workloads on one GPU: device-resident throughput, the step kernel's rate against its
+    roofline, a parity sample against the oracle and the CPU oracle at its best batch."""
+    import numpy as np
+    import torch
+    from codecoder_b200.geometry import RotatedSurface
+    from codecoder_b200.modules import PreDecoder
+    from codecoder_b200.params import CONFIGS, flops_per_shot, init_params, storage_params
+    from codecoder_b200.sampler import sample_torch
+    from oracle import predecoder_oracle as orc
+    cfg = CONFIGS[name]
+    g = RotatedSurface(cfg.d, cfg.rounds)
+    params = init_params(cfg, SEED)
+    det, _ = sample_torch(g, cfg.p, shots, SEED + 31, device=dev)
+    pd = PreDecoder(g, cfg, params, device=dev, chunk_shots=16384)
+    logits = torch.empty(shots, g.N_d, 2, dtype=torch.float32, device=dev)
+    resid = torch.empty(shots, g.N_c, dtype=torch.uint8, device=dev)
+    S = ((min(16384, shots) + 255) // 256) * 256
+    chunks = [min(S, shots - b) for b in range(0, shots, S)]
+    step_flops = [2.0 * cfg.K * cfg.channels ** 2 * (g.N_d if i % 2 == 0 else g.N_c) * sb
+                  for sb in chunks for i in range(2 * cfg.layers)]
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in step_flops]
+    for _ in range(warmup):
+        pd.forward_into(det, logits, resid)
+    torch.cuda.synchronize()
+    pd.record_step_events(ev)
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record()
+    for _ in range(steps):
+        pd.forward_into(det, logits, resid)
+    s1.record()
+    s1.synchronize()
+    pd.record_step_events([])
+    if pd.status() != 0:
+        raise RuntimeError(f"device watchdog fired in the {name} measurement")
+    ms = s0.elapsed_time(s1)
+    tc_ms = sum(a.elapsed_time(b) for a, b in ev)
+    achieved = sum(step_flops) / (tc_ms / 1000.0) / 1e12
+    f32 = cfg.dtype == "f32"
+    if f32:
+        peak, peak_kind, kernel, bound = FP32_FMA_PEAK_TFLOPS, "nominal FP32 FMA (148 SMs x 128 FMA/clk x 2 x 1965 MHz)", \
+            "gmm_fma_kernel<float>", "fma"
+    else:
+        peak, peak_kind, kernel, bound = pk["bf16_tflops_sustained"], f"{pk['source']} sustained bf16 (cuBLAS)", \
+            "gmm_wide_kernel", "tensor"
+    pick = np.unique(np.linspace(0, shots - 1, min(16, shots)).astype(np.int64))
+    sel = torch.as_tensor(pick, device=dev)
+    det_s = det.index_select(0, sel).cpu().numpy()
+    lg_s = logits.index_select(0, sel).cpu().numpy()
+    rs_s = resid.index_select(0, sel).cpu().numpy()
+    sp = storage_params(cfg, params)
+    torch.set_num_threads(os.cpu_count() or 1)
+    ref64, res64 = orc.predecoder_batched(g, cfg, sp, det_s, dtype=torch.float64, batch=16)
+    if f32:
+        parity = orc.parity_report(g, det_s, lg_s, rs_s, ref64, res64, 1e-4)
+        parity["pass"] = bool(parity["logit_max_rel_err"] < 1e-4 and parity["residual_mismatch_outside_band"] == 0
+                              and parity["residual_is_own_xor"])
+    else:
+        ref32, _ = orc.predecoder_batched(g, cfg, sp, det_s, dtype=torch.float32, batch=16)
+        parity = orc.deep_parity(g, det_s, lg_s, rs_s, ref64, res64, ref32, 2e-2)
+    rate, n_shots, threads, cb = cpu_rate(g, cfg, params, det[:64].cpu().numpy(), cpu_seconds)
+    return {"workload": f"rotated surface d={cfg.d}, {cfg.rounds} rounds, p={cfg.p}; {cfg.layers} layers, "
+                        f"C={cfg.channels}, K={cfg.K}, {cfg.dtype}; {shots} shots on one GPU",
+            "value": steps * shots / (ms / 1000.0), "unit": "syndromes/s", "ms_per_step": ms / steps,
+            "steps": steps, "warmup": warmup, "flop_per_shot": flops_per_shot(cfg, g.N_c, g.N_d),
+            "roofline": {"bound": bound, "kernel": kernel, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "peak_kind": peak_kind, "avg_launch_ms": tc_ms / len(ev),
+                         "launches": len(ev)},
+            "parity": parity,
+            "cpu_baseline": {"value": rate, "unit": "syndromes/s", "cores": threads, "kind": "port", "batch": cb,
+                             "sample": f"{n_shots} shots through the CPU oracle (fp32) at batch {cb}"}}
 
 
 def run_reference(args, cfg, g, params, rank, world):
@@ -313,7 +390,8 @@ def main():
     pk = peaks()
     achieved = tc_flops / (tc_ms / 1000.0) / 1e12
     fps = flops_per_shot(cfg, g.N_c, g.N_d)
-    step_kernel = "gmm_wide_kernel" if cfg.channels == 128 else "gmm_tc_kernel"
+    step_kernel = "gmm_pair_kernel" if (cfg.channels == 128 and os.environ.get("BPC_STEP_KERNEL") == "pair") \
+        else "gmm_wide_kernel"
     roof = {"bound": "tensor", "kernel": f"{step_kernel} (bipartite step)", "achieved": achieved,
             "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s", "frac": achieved / pk["bf16_tflops_sustained"],
             "peak_kind": f"{pk['source']} sustained bf16 (cuBLAS)", "traffic": None,
@@ -423,6 +501,12 @@ def main():
                                    "how": "StreamingDecoder: one CUDA-graph replay per round (node-tiled kernels)"},
                   "flop_per_round": sflop, "roofline_us_all_sms": sflop / (pk["bf16_tflops"] * 1e12) * 1e6}
 
+    configs = None
+    if rank == 0 and world == 1 and not args.no_configs:
+        # the d = 5 fp32 (CUDA-core) and d = 9 bf16 workloads at their stated batches
+        configs = {"d5_fp32": measure_config("d5_fp32", 1024, max(args.steps, 5), max(args.warmup, 3), dev, pk, 4.0),
+                   "d9_bf16": measure_config("d9_bf16", 65536, max(args.steps, 5), max(args.warmup, 3), dev, pk, 6.0)}
+
     train = None
     if not args.no_train:
         # d = 11 training step (bf16 autocast, BCE, Adam 1e-3) with DDP over NCCL at world > 1: fixed shots per GPU
@@ -471,7 +555,7 @@ def main():
                 "config": workload(cfg, g, shots, world), "per_gpu": value / world, "roofline": roof,
                 "cpu_baseline": cpu, "e2e": e2e, "clocks": clk.summary(),
                 "gpu_launches": launches_per_fwd * args.steps, "flop_per_shot": fps, "parity": parity,
-                "streaming": stream, "train": train}
+                "streaming": stream, "configs": configs, "train": train}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

@@ -1,14 +1,17 @@
 // Pre-decoder forward: detector bits -> L x [check -> data, data -> check] bipartite convolutions -> X/Z head ->
 // threshold -> XOR syndrome cancellation, on device buffers, with the caller's workspace.
 //
-// HBM layout of one chunk of S shots (S a multiple of 128; the workspace fixes S):
-//   h_c   (N_c, S, C)  check features, node-major: the 128 shots of a tile x one node are 128 x C contiguous
+// HBM layout of one chunk of S shots (S a multiple of 256; the workspace fixes S):
+//   h_c   (N_c, S, C)  check features, node-major; on the tensor-core paths blocked by TM shots (TM = 128 for the
+//                      CTA-pair steps at C = 128, 256 for the wide-tile steps): the TM shots of one node are TM x C
+//                      contiguous, channel groups of 8 outermost within the block
 //   h_d   (N_d, S, C)  data features, same layout
 //   bits  (N_c, S/32)  uint32 residual syndrome, bit s % 32 of word s / 32 = shot s
 // Per chunk: embed (det -> h_c, det -> bits), 2 L bipartite steps (the last check -> data step also writes the logits
 // and XORs the predicted flips into bits), unpack (bits -> residual bytes).  Logits go straight to the caller's
 // (B, N_d, 2) buffer from the head epilogue.
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -25,13 +28,14 @@ struct bpc_predecoder {
   int32_t* xor_nbr = nullptr;    // (N_d, 2, 2)
   uint8_t* check_type = nullptr; // (N_c)
   int32_t* check_order = nullptr; // (N_c) processing order of the data -> check steps, or null
+  int32_t* check_order_typed = nullptr;  // (N_c) the same order grouped by check type (X checks first)
   void* embed = nullptr;         // (4, C)
   void* w_c2d = nullptr;         // (L, C, K C)
   void* w_d2c = nullptr;         // (L, 2, C, K C)
   float* head_w = nullptr;       // (2, C)
   float* head_b = nullptr;       // (2)
   int* status = nullptr;         // device watchdog status word
-  unsigned long long* tile_counter = nullptr;   // dynamic tile scheduling of the tensor-core steps
+  unsigned long long* tile_counter = nullptr;   // dynamic tile scheduling of the tensor-core steps (2 words)
   bool weights_set = false;
   uint64_t timeout_ns = 2000000000ull;
   std::vector<cudaEvent_t> step_events;   // optional (before, after) pairs around each bipartite-step launch
@@ -203,8 +207,22 @@ extern "C" int bpc_predecoder_create(const bpc_predecoder_config* cfg, const int
       return e;
     }
   }
-  const unsigned long long zero64 = 0;
-  if ((e = copy_in(&h->tile_counter, &zero64, sizeof(zero64)))) {
+  {
+    // the data -> check order grouped by type (the CTA-pair steps give each check type its own pairs)
+    std::vector<int32_t> typed;
+    typed.reserve(c.n_checks);
+    for (int ty = 0; ty < 2; ++ty)
+      for (int i = 0; i < c.n_checks; ++i) {
+        const int n = check_order ? check_order[i] : i;
+        if ((n >= c.z_check_begin) == (ty == 1)) typed.push_back(n);
+      }
+    if ((e = copy_in(&h->check_order_typed, typed.data(), sizeof(int32_t) * c.n_checks))) {
+      bpc_predecoder_destroy(h);
+      return e;
+    }
+  }
+  const unsigned long long zero64[2] = {0, 0};
+  if ((e = copy_in(&h->tile_counter, zero64, sizeof(zero64)))) {
     bpc_predecoder_destroy(h);
     return e;
   }
@@ -267,13 +285,18 @@ extern "C" int bpc_predecoder_forward(bpc_predecoder* h, const uint8_t* det, flo
   const bool tc = !f32 && c.channels >= 64 && c.channels % 32 == 0;
   const bool nodes = tc && B <= kNodePathMaxShots && (c.channels == 64 || c.channels == 128);
   const bool shot_tiles = tc && !nodes;
+  // hidden-128 steps: the single-CTA wide-tile kernel; BPC_STEP_KERNEL=pair selects the CTA-pair kernel with resident
+  // relation matrices (same bits; measured slower on B200: half of its shared memory holds W, so half as many
+  // activation bytes are in flight and the loads' latency is not covered)
+  const char* sk = std::getenv("BPC_STEP_KERNEL");
+  const bool pair = shot_tiles && c.channels == 128 && c.K <= 8 && sk && std::strcmp(sk, "pair") == 0;
   const size_t es = esize(c.dtype);
   const size_t wl = static_cast<size_t>(c.channels) * c.K * c.channels;
 
   // the two steps of layer l as bipartite-conv problems on the chunk's buffers
   // shot-tiled tensor-core path: blocked (node, S / TM, C / 8, TM, 8) activations; node-tiled tensor-core and
   // CUDA-core paths: node-major rows (node, S, C)
-  const int tm = shot_tiles ? gmm_tc_tile_shots(c.channels) : 0;
+  const int tm = pair ? gmm_pair_tile_shots() : shot_tiles ? gmm_tc_tile_shots(c.channels) : 0;
   const int64_t shot_stride = c.channels;
   const int64_t cg_stride = 8;
   const int64_t node_stride = L.S * c.channels;
@@ -313,15 +336,16 @@ extern "C" int bpc_predecoder_forward(bpc_predecoder* h, const uint8_t* det, flo
     c2d.shots = d2c.shots = L.S;
     c2d.w = h->w_c2d;
     d2c.w = h->w_d2c;
-    if (int e = gmm_tc_make_maps(c2d, &mc2d)) return e;
-    if (int e = gmm_tc_make_maps(d2c, &md2c)) return e;
+    auto make = [&](const GmmProblem& q, GmmMaps* m) { return pair ? gmm_pair_make_maps(q, m) : gmm_tc_make_maps(q, m); };
+    if (int e = make(c2d, &mc2d)) return e;
+    if (int e = make(d2c, &md2c)) return e;
     for (int l = 0; l < c.layers; ++l) {
       GmmMaps tmp;
       c2d.w = static_cast<const uint8_t*>(h->w_c2d) + l * wl * es;
       d2c.w = static_cast<const uint8_t*>(h->w_d2c) + 2 * l * wl * es;
-      if (int e = gmm_tc_make_maps(c2d, &tmp)) return e;
+      if (int e = make(c2d, &tmp)) return e;
       wm_c2d.push_back(tmp.w);
-      if (int e = gmm_tc_make_maps(d2c, &tmp)) return e;
+      if (int e = make(d2c, &tmp)) return e;
       wm_d2c.push_back(tmp.w);
     }
   }
@@ -370,7 +394,7 @@ extern "C" int bpc_predecoder_forward(bpc_predecoder* h, const uint8_t* det, flo
       for (int step = 0; step < 2; ++step) {
         const GmmProblem& p = step == 0 ? c2d : d2c;
         const bool rec = 2 * n_rec + 1 < h->step_events.size();
-        if (shot_tiles) {   // the tile counter of the dynamic scheduler starts at zero
+        if (shot_tiles && !pair) {   // the tile counter of the dynamic scheduler starts at zero
           cudaError_t me = cudaMemsetAsync(h->tile_counter, 0, sizeof(unsigned long long), stream);
           if (me != cudaSuccess) return fail(BPC_ERR_LAUNCH, std::string("cudaMemsetAsync: ") + cudaGetErrorString(me));
         }
@@ -378,6 +402,11 @@ extern "C" int bpc_predecoder_forward(bpc_predecoder* h, const uint8_t* det, flo
         int e;
         if (nodes) {
           e = gmm_nodes_launch(p, h->status, h->timeout_ns, stream);
+        } else if (pair) {
+          GmmMaps m = step == 0 ? mc2d : md2c;
+          m.w = step == 0 ? wm_c2d[l] : wm_d2c[l];
+          e = gmm_pair_launch(p, m, step == 0 ? nullptr : h->check_order_typed, c.z_check_begin, h->tile_counter,
+                              h->status, h->timeout_ns, stream);
         } else if (tc) {
           GmmMaps m = step == 0 ? mc2d : md2c;
           m.w = step == 0 ? wm_c2d[l] : wm_d2c[l];
@@ -463,7 +492,7 @@ extern "C" int bpc_predecoder_status(bpc_predecoder* h, bpc_stream_t stream, int
 extern "C" void bpc_predecoder_destroy(bpc_predecoder* h) {
   if (!h) return;
   for (void* p : {static_cast<void*>(h->c2d), static_cast<void*>(h->d2c), static_cast<void*>(h->xor_nbr),
-                  static_cast<void*>(h->check_order),
+                  static_cast<void*>(h->check_order), static_cast<void*>(h->check_order_typed),
                   static_cast<void*>(h->check_type), h->embed, h->w_c2d, h->w_d2c, static_cast<void*>(h->head_w),
                   static_cast<void*>(h->head_b), static_cast<void*>(h->status), static_cast<void*>(h->tile_counter)})
     if (p) cudaFree(p);

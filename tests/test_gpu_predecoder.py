@@ -201,3 +201,22 @@ def test_d13_wide_tiles_match_node_tiles_bitwise():
     torch.cuda.synchronize()
     assert wide.status() == 0 and node.status() == 0
     assert torch.equal(w_lg, n_lg) and torch.equal(w_rs, n_rs)
+
+
+def test_d13_pair_steps_match_wide_tile_steps_bitwise(monkeypatch):
+    """Hidden-128 passes of more than 64 shots run the single-CTA wide-tile kernel; BPC_STEP_KERNEL=pair selects the
+    CTA-pair kernel (cta_group::2 MMAs, M = 256 shots, relation matrices resident in shared memory).  The two
+    accumulate every output in the same relation and channel order and use the same element arithmetic: every logit
+    and residual bit agrees, over full and partial tiles, in both step types and the head."""
+    cfg = replace(CONFIGS["d13_bf16"], layers=3)
+    g = RotatedSurface(cfg.d, cfg.rounds)
+    params = init_params(cfg, 919)
+    det, _ = sample(g, 0.02, 600, 920)
+    d = torch.as_tensor(det).to(DEV)
+    pd = PreDecoder(g, cfg, params, device=DEV)
+    w_lg, w_rs = pd(d)
+    monkeypatch.setenv("BPC_STEP_KERNEL", "pair")
+    p_lg, p_rs = pd(d)
+    torch.cuda.synchronize()
+    assert pd.status() == 0
+    assert torch.equal(p_lg, w_lg) and torch.equal(p_rs, w_rs)
