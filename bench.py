@@ -260,6 +260,46 @@ def measure_config(name, shots, steps, warmup, dev, pk, cpu_seconds):
                              "sample": f"{n_shots} shots through the CPU oracle (fp32) at batch {cb}"}}
 
 
+def measure_cascade_stack(tables_npz, dev, shots=512, steps=5):
+    """14 C14-shaped bottleneck blocks (the reference's Cascade BB72 network's backbone: H = 512, the bipartite
+    convolution at 128 channels on the BB72 Tanner graph, cascade_net.py:236-259) in eval mode, seeded weights and
+    BatchNorm statistics: device time per shot at `shots` shots.  The graph's tables are the reference's
+    Geometry('bb72') tables as recorded in the test fixture."""
+    import numpy as np
+    import torch
+    from types import SimpleNamespace
+    from codecoder_b200.modules import CascadeBlock, CascadeStack
+    z = np.load(tables_npz)
+    geo = SimpleNamespace(c2d=[z["c2d0"], z["c2d1"]], d2c=[z["d2c0"], z["d2c1"]],
+                          inv_c2d=[z["inv_c2d0"].astype(np.int64), z["inv_c2d1"].astype(np.int64)],
+                          inv_d2c=[z["inv_d2c0"].astype(np.int64), z["inv_d2c1"].astype(np.int64)])
+    torch.manual_seed(SEED)
+    blocks = CascadeStack([CascadeBlock(512, geo, 14, res="skip") for _ in range(14)]).to(dev).eval()
+    for b in blocks.blocks:
+        for i in (1, 2, 3):
+            getattr(b, f"bn{i}").running_var.uniform_(0.5, 2.0)
+    h = torch.randn(shots, int(z["N"]), 512, device=dev)
+    with torch.no_grad():
+        for _ in range(3):
+            blocks(h)
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(steps):
+            out = blocks(h)
+        e.record()
+        e.synchronize()
+    ms = s.elapsed_time(e) / steps
+    if not bool(torch.isfinite(out).all()):
+        raise RuntimeError("C14 stack produced non-finite values")
+    return {"workload": f"14 Cascade bottleneck blocks, H=512 (bottleneck 128), BB72 graph ({int(z['N'])} nodes), "
+                        f"eval, bf16 bottleneck + fp32 residual stream, {shots} shots", "ms_per_batch": ms,
+            "us_per_shot": ms * 1000.0 / shots,
+            "kernels": "per block: gmm_tc_kernel (down + BN2 + SiLU), gmm_wide_kernel x2 (two-type conv, conv + BN3 "
+                       "+ SiLU), cuBLAS bf16 GEMM (up, a plain dense projection), residual_affine_silu_kernel "
+                       "(residual + next block's BN1 + SiLU)"}
+
+
 def run_reference(args, cfg, g, params, rank, world):
     """--impl reference: the CPU path of the reference (restated by the oracle) at its best batch, rank 0 only."""
     if rank != 0:
@@ -501,6 +541,11 @@ def main():
                                    "how": "StreamingDecoder: one CUDA-graph replay per round (node-tiled kernels)"},
                   "flop_per_round": sflop, "roofline_us_all_sms": sflop / (pk["bf16_tflops"] * 1e12) * 1e6}
 
+    cascade = None
+    golden_bb72 = os.path.join(REPO, "tests", "golden", "bb72_c14_conv.npz")
+    if rank == 0 and world == 1 and not args.no_configs and os.path.exists(golden_bb72):
+        cascade = measure_cascade_stack(golden_bb72, dev)
+
     configs = None
     if rank == 0 and world == 1 and not args.no_configs:
         # the d = 5 fp32 (CUDA-core) and d = 9 bf16 workloads at their stated batches
@@ -555,7 +600,7 @@ def main():
                 "config": workload(cfg, g, shots, world), "per_gpu": value / world, "roofline": roof,
                 "cpu_baseline": cpu, "e2e": e2e, "clocks": clk.summary(),
                 "gpu_launches": launches_per_fwd * args.steps, "flop_per_shot": fps, "parity": parity,
-                "streaming": stream, "configs": configs, "train": train}
+                "streaming": stream, "configs": configs, "cascade_c14": cascade, "train": train}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

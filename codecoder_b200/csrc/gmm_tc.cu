@@ -26,6 +26,7 @@
 // Every wait is bounded (mbar_wait); a timeout sets the status word and the CTA drains and returns.
 #include <algorithm>
 #include <cstdio>
+#include <map>
 #include <mutex>
 #include <string>
 #include <set>
@@ -916,16 +917,18 @@ const void* wide_kernel_for(bool blocked, int epi, bool head, int Ci) {
 }  // namespace
 
 int allow_smem(const void* fn, int bytes) {
-  // the attribute is per device: remember (device, kernel) pairs
+  // the attribute is per device and kernel: remember the size set for each (device, kernel) pair and raise it when
+  // a launch needs more
   static std::mutex mu;
-  static std::set<std::pair<int, const void*>> configured;
+  static std::map<std::pair<int, const void*>, int> configured;
   int dev = 0;
   cudaGetDevice(&dev);
   std::lock_guard<std::mutex> lk(mu);
-  if (configured.count({dev, fn})) return 0;
+  auto it = configured.find({dev, fn});
+  if (it != configured.end() && it->second >= bytes) return 0;
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (e != cudaSuccess) return fail(4, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
-  configured.insert({dev, fn});
+  configured[{dev, fn}] = bytes;
   return 0;
 }
 
