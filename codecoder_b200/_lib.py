@@ -33,6 +33,9 @@ SIGNATURES = {
                                          c_vp]),
     "bpc_gather_mm_fwd_ex": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32,
                                             c_i32, c_i32, c_vp, c_vp, c_i32, c_vp]),
+    "bpc_route": (ctypes.c_int, [c_vp, c_vp, c_i64, c_i32, c_i32, ctypes.c_float, c_i32, c_vp, c_vp, c_vp, c_vp, c_vp,
+                                 c_vp, c_vp, ctypes.c_size_t, c_vp]),
+    "bpc_route_workspace_size": (ctypes.c_size_t, [c_i64]),
     "bpc_residual_affine_silu": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, ctypes.c_float, ctypes.c_float,
                                                 c_vp, c_vp, c_vp]),
     "bpc_gelu_residual_fwd": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_i32, c_i32, c_vp]),

@@ -235,6 +235,20 @@ BPC_API int bpc_stream_stop(bpc_stream* s);
 BPC_API int bpc_stream_status(const bpc_stream* s);
 BPC_API void bpc_stream_destroy(bpc_stream* s);
 
+/* Routing to a fallback decoder and its hand-off (the reference's decoder.route / decode and the router's matcher
+ * call: evaluation/convlines/decoder.py:116-142, evaluation/timing/d7/router.cc:142-168).  Per shot b of a
+ * pre-decoded batch (logits (B, n_data, 2) fp32, residual (B, n_checks) uint8, device buffers):
+ *   conf[b] = min |logits[b, :, :]|,  weight[b] = number of set residual bits,
+ *   routed[b] = conf[b] < tau || (route_residual && weight[b] > 0)        (uint8, (B,))
+ * and the routed shots in ascending order: index[i] (int64, room for B), their residual rows handoff[i, :] (uint8,
+ * room for B x n_checks, or NULL), the count in *n_routed (a device int64).  conf / weight may be NULL.  workspace:
+ * bpc_route_workspace_size(B) bytes of device memory, 8-byte aligned.  Every launch on `stream`. */
+BPC_API int bpc_route(const float* logits, const uint8_t* residual, int64_t B, int32_t n_data, int32_t n_checks,
+                      float tau, int32_t route_residual, uint8_t* routed, int64_t* index, uint8_t* handoff,
+                      int64_t* n_routed, float* conf, int32_t* weight, void* workspace, size_t workspace_bytes,
+                      bpc_stream_t stream);
+BPC_API size_t bpc_route_workspace_size(int64_t B);
+
 /* Size in bytes of the scratch array bpc_predecoder_forward_noalloc runs on. */
 BPC_API size_t bpc_noalloc_scratch_bytes(void);
 

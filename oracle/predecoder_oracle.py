@@ -21,6 +21,8 @@ What it restates:
                  bf16 network rounds every stored activation to bf16 exactly where the device stores bf16, and
                  accumulates in float64 here (fp32 on the device).
   cancel         the GF(2) syndrome cancellation, integer numpy.
+  route          the routing rule of the reference's decoder (|logit| < tau, here over the pre-decoder's data-qubit
+                 logits, or a non-empty residual) and its ordered hand-off.
   parity_report / deep_parity
                  the parity figures of a GPU run against this oracle (logit error, band counts, residual bits);
                  deep_parity is the bar for deep bf16 networks, whose logits are chaotic in the bf16 rounding of the
@@ -266,3 +268,17 @@ def residual_mismatch_outside_band(res, res_ref, logits_ref, geo, tol) -> int:
             touched[bi, c[ok][ni]] = True
     diff = (np.asarray(res) != np.asarray(res_ref)) & ~touched
     return int(diff.sum())
+
+
+def route(logits, residual, tau: float, route_residual: bool = True):
+    """The routing rule restated (evaluation/convlines/decoder.py:116-142 `route`, with the pre-decoder's confidence):
+    conf = min |logit| per shot, weight = set residual bits per shot, routed = conf < tau or (route_residual and
+    weight > 0); the routed shots in ascending order and their residual rows -> (routed, index, handoff, conf,
+    weight)."""
+    lg = np.asarray(logits, np.float32).reshape(len(logits), -1)
+    rs = np.asarray(residual, np.uint8) & 1
+    conf = np.abs(lg).min(1) if lg.shape[1] else np.full(len(lg), np.inf, np.float32)
+    weight = rs.sum(1).astype(np.int32)
+    routed = (conf < np.float32(tau)) | (bool(route_residual) & (weight > 0))
+    index = np.flatnonzero(routed).astype(np.int64)
+    return routed, index, np.asarray(residual, np.uint8)[index], conf.astype(np.float32), weight

@@ -158,3 +158,18 @@ def test_deep_parity_bar_accepts_a_correct_restatement_and_catches_planted_mista
     # logits 5 % off everywhere
     r = orc.deep_parity(g, det, ref32 * 1.05, res32, ref64, res64, ref32)
     assert not r["pass"]
+
+
+def test_route_rule_on_a_hand_made_batch():
+    """The routing rule: a shot goes to the fallback decoder when its least confident logit is inside tau or its
+    residual is not empty; the hand-off keeps ascending shot order and the shots' residual rows."""
+    lg = np.ones((4, 3, 2), np.float32)
+    lg[1, 2, 1] = -0.01                     # shot 1: one unsure logit
+    rs = np.zeros((4, 5), np.uint8)
+    rs[3, 4] = 1                            # shot 3: a detector left over
+    routed, index, handoff, conf, weight = orc.route(lg, rs, 0.05, True)
+    assert routed.tolist() == [False, True, False, True] and index.tolist() == [1, 3]
+    assert np.array_equal(handoff, rs[[1, 3]]) and weight.tolist() == [0, 0, 0, 1]
+    assert np.isclose(conf[1], 0.01) and conf[0] == 1.0
+    assert orc.route(lg, rs, 0.05, False)[1].tolist() == [1]
+    assert orc.route(lg, rs, 0.0, False)[1].tolist() == []
