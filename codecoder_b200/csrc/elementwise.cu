@@ -228,7 +228,7 @@ __global__ void __launch_bounds__(256) gelu_residual_bwd_kernel(const void* __re
 //   forward   h[b, n, :] = E[tok, :] (fp32) and its bf16 copy, one pass
 //   backward  dE[k, :] = sum over (b, n) with tok = k of (g + g_bf16)[b, n, :]: per-block partial sums (each warp
 //             a fixed set of rows, warps added in order in shared memory), then a fixed-order sum over the blocks;
-//             deterministic, no atomics
+//             deterministic, no atomics (the per-type sums below)
 constexpr int kEmbBwdBlocks = 1024;
 constexpr int kEmbBwdThreads = 256;
 constexpr int kEmbMaxC = 256;
@@ -256,64 +256,100 @@ __global__ void __launch_bounds__(256) embed_tokens_fwd_kernel(const uint8_t* __
   }
 }
 
+// The backward as two sums per check type t, because a token is 2 t + det and det = 1 is rare: S_t over every row of
+// type t and D_t over its rows with det = 1, so dE[2 t + 1] = D_t and dE[2 t] = S_t - D_t.  Each warp takes a fixed
+// run of rows, one row per step with four rows' loads in flight; lane l holds channels 4 l .. 4 l + 3 (+ 128), read as
+// one 16-byte (fp32) and one 8-byte (bf16) vector; the type and det branches are uniform across the warp.  The
+// block's warps are added in order in shared memory: deterministic, no atomics.
 __global__ void __launch_bounds__(kEmbBwdThreads) embed_tokens_bwd_partial_kernel(
     const uint8_t* __restrict__ det, const uint8_t* __restrict__ ctype, const float* __restrict__ g,
     const __nv_bfloat16* __restrict__ g16, float* __restrict__ partial, int64_t rows, int N, int C) {
   __shared__ float red[kEmbBwdThreads / 32][4][kEmbMaxC];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  constexpr int kSlots = kEmbMaxC / 32;
-  float acc[4][kSlots];
+  constexpr int kSlots = kEmbMaxC / 128;                 // 4 channels per lane per slot
+  float S[2][kSlots][4], D[2][kSlots][4];
 #pragma unroll
-  for (int k = 0; k < 4; ++k)
+  for (int t = 0; t < 2; ++t)
 #pragma unroll
-    for (int j = 0; j < kSlots; ++j) acc[k][j] = 0.f;
-  // each warp a contiguous run of rows, four rows per iteration with all their loads issued before the adds
+    for (int j = 0; j < kSlots; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) S[t][j][e] = D[t][j][e] = 0.f;
   const int64_t per_block = (rows + gridDim.x - 1) / gridDim.x;
   const int64_t r0 = blockIdx.x * per_block, r1 = min(rows, r0 + per_block);
   const int64_t per_warp = (r1 - r0 + kEmbBwdThreads / 32 - 1) / (kEmbBwdThreads / 32);
   const int64_t w0 = r0 + warp * per_warp, w1 = min(r1, w0 + per_warp);
   int n = w0 < w1 ? static_cast<int>(w0 % N) : 0;      // node of row w0; advanced without a division per row
   for (int64_t r = w0; r < w1; r += 4) {
-    int tok[4];
-    float v[4][kSlots];
+    float v[4][kSlots][4];
+    int ty[4], dt[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const int64_t rr = r + u;
       int nn = n + u;
       while (nn >= N) nn -= N;
       const bool ok = rr < w1;
-      tok[u] = ok ? 2 * __ldg(ctype + nn) + __ldg(det + rr) : -1;
+      ty[u] = ok ? __ldg(ctype + nn) : 0;
+      dt[u] = ok ? __ldg(det + rr) : 0;
 #pragma unroll
       for (int j = 0; j < kSlots; ++j) {
-        const int c = lane + 32 * j;
-        float x = 0.f;
+        const int c = 4 * lane + 128 * j;
+        float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
         if (ok && c < C) {
-          if (g) x = __ldg(g + rr * C + c);
-          if (g16) x += __bfloat162float(g16[rr * C + c]);
+          if (g) x = __ldg(reinterpret_cast<const float4*>(g + rr * C + c));
+          if (g16) {
+            const uint2 h = __ldg(reinterpret_cast<const uint2*>(g16 + rr * C + c));
+            x.x += __uint_as_float(h.x << 16);
+            x.y += __uint_as_float(h.x & 0xFFFF0000u);
+            x.z += __uint_as_float(h.y << 16);
+            x.w += __uint_as_float(h.y & 0xFFFF0000u);
+          }
         }
-        v[u][j] = x;
+        v[u][j][0] = x.x;
+        v[u][j][1] = x.y;
+        v[u][j][2] = x.z;
+        v[u][j][3] = x.w;
       }
     }
 #pragma unroll
-    for (int u = 0; u < 4; ++u)
+    for (int u = 0; u < 4; ++u) {
 #pragma unroll
       for (int j = 0; j < kSlots; ++j)
 #pragma unroll
-        for (int k = 0; k < 4; ++k) acc[k][j] += (tok[u] == k) ? v[u][j] : 0.f;
+        for (int e = 0; e < 4; ++e) {
+          if (ty[u]) S[1][j][e] += v[u][j][e];
+          else S[0][j][e] += v[u][j][e];
+        }
+      if (dt[u]) {
+#pragma unroll
+        for (int j = 0; j < kSlots; ++j)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            if (ty[u]) D[1][j][e] += v[u][j][e];
+            else D[0][j][e] += v[u][j][e];
+          }
+      }
+    }
     n += 4;
     while (n >= N) n -= N;
   }
 #pragma unroll
-  for (int k = 0; k < 4; ++k)
+  for (int t = 0; t < 2; ++t)
 #pragma unroll
     for (int j = 0; j < kSlots; ++j)
-      if (lane + 32 * j < C) red[warp][k][lane + 32 * j] = acc[k][j];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int c = 4 * lane + 128 * j + e;
+        if (c < C) {
+          red[warp][2 * t][c] = S[t][j][e] - D[t][j][e];
+          red[warp][2 * t + 1][c] = D[t][j][e];
+        }
+      }
   __syncthreads();
   for (int i = threadIdx.x; i < 4 * C; i += blockDim.x) {
     const int k = i / C, c = i - k * C;
-    float v = 0.f;
-    for (int w = 0; w < kEmbBwdThreads / 32; ++w) v += red[w][k][c];
-    partial[static_cast<int64_t>(blockIdx.x) * 4 * C + i] = v;
+    float s = 0.f;
+    for (int w = 0; w < kEmbBwdThreads / 32; ++w) s += red[w][k][c];
+    partial[static_cast<int64_t>(blockIdx.x) * 4 * C + i] = s;
   }
 }
 
@@ -444,7 +480,7 @@ extern "C" size_t bpc_embed_tokens_bwd_workspace_size(int32_t C) {
 extern "C" int bpc_embed_tokens_bwd(const uint8_t* det, const uint8_t* check_type, const float* g, const void* g_bf16,
                                     float* dE, void* workspace, size_t workspace_bytes, int64_t B, int32_t N, int32_t C,
                                     bpc_stream_t stream) {
-  if (B < 0 || N < 1 || C < 1 || C > kEmbMaxC) return fail(BPC_ERR_ARG, "B >= 0, N >= 1, 1 <= C <= 256");
+  if (B < 0 || N < 1 || C < 4 || C > kEmbMaxC || C % 4) return fail(BPC_ERR_ARG, "B >= 0, N >= 1, C in 4..256, a multiple of 4");
   if (!dE) return fail(BPC_ERR_ARG, "null dE");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (B == 0) {
@@ -452,6 +488,8 @@ extern "C" int bpc_embed_tokens_bwd(const uint8_t* det, const uint8_t* check_typ
     return e == cudaSuccess ? 0 : fail(BPC_ERR_LAUNCH, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
   }
   if (!det || !check_type || (!g && !g_bf16) || !workspace) return fail(BPC_ERR_ARG, "null buffer");
+  if ((reinterpret_cast<uintptr_t>(g) & 15) || (reinterpret_cast<uintptr_t>(g_bf16) & 7))
+    return fail(BPC_ERR_ARG, "g must be 16-byte and g_bf16 8-byte aligned");
   if (workspace_bytes < bpc_embed_tokens_bwd_workspace_size(C)) return fail(BPC_ERR_SPACE, "embedding workspace too small");
   float* partial = static_cast<float*>(workspace);
   embed_tokens_bwd_partial_kernel<<<kEmbBwdBlocks, kEmbBwdThreads, 0, s>>>(

@@ -122,7 +122,10 @@ class Trainer:
         if self.world > 1:
             from torch.nn.parallel import DistributedDataParallel as DDP
             ids = [self.device.index] if self.device.type == "cuda" else None
-            self.net = DDP(model, device_ids=ids, broadcast_buffers=False)
+            # ~5 MB of gradients in ~1 MB buckets: the all-reduce of the last layers' buckets runs while the
+            # backward of the earlier layers still computes, instead of one bucket after the whole backward
+            self.net = DDP(model, device_ids=ids, broadcast_buffers=False, bucket_cap_mb=1,
+                           gradient_as_bucket_view=True)
         self.params = [p for p in model.parameters() if p.requires_grad]
         self.opt = torch.optim.Adam(self.params, lr=lr)
         self.clip = clip

@@ -95,7 +95,8 @@ BPC_API int bpc_gelu_residual_bwd(const void* gy, const void* gy_bf16, const voi
  *   forward   h[b, n, :] = E[2 check_type[n] + det[b, n], :]  (fp32 (B, N, C)) and h_bf16 = bf16(h), one pass
  *   backward  dE[k, :] = sum over (b, n) with token k of g[b, n, :] + g_bf16[b, n, :] (either may be NULL), fp32 (4, C),
  *             deterministic (fixed per-block partial sums in `workspace`, then a fixed-order sum)
- * det (B, N) uint8 0/1, check_type (N) uint8 0/1, E (4, C) fp32; C % 8 == 0 (forward), C <= 256 (backward). */
+ * det (B, N) uint8 0/1, check_type (N) uint8 0/1, E (4, C) fp32; C % 8 == 0 (forward), C % 4 == 0 and C <= 256
+ * with g 16-byte and g_bf16 8-byte aligned (backward). */
 BPC_API int bpc_embed_tokens_fwd(const uint8_t* det, const uint8_t* check_type, const float* E, float* h, void* h_bf16,
                                  int64_t B, int32_t N, int32_t C, bpc_stream_t stream);
 BPC_API size_t bpc_embed_tokens_bwd_workspace_size(int32_t C);

@@ -275,7 +275,8 @@ def route(logits, residual, tau: float, route_residual: bool = True):
     conf = min |logit| per shot, weight = set residual bits per shot, routed = conf < tau or (route_residual and
     weight > 0); the routed shots in ascending order and their residual rows -> (routed, index, handoff, conf,
     weight)."""
-    lg = np.asarray(logits, np.float32).reshape(len(logits), -1)
+    lg = np.asarray(logits, np.float32)
+    lg = lg.reshape(lg.shape[0], int(np.prod(lg.shape[1:])))
     rs = np.asarray(residual, np.uint8) & 1
     conf = np.abs(lg).min(1) if lg.shape[1] else np.full(len(lg), np.inf, np.float32)
     weight = rs.sum(1).astype(np.int32)
