@@ -10,8 +10,9 @@
 //   swizzle is the canonical MN-major SW128 layout, so no operand is transposed anywhere.  Item = one target node
 //   x 128 shots; the CTA owns a group of up to 4 relations, keeps one 128 x N fp32 accumulator per relation in
 //   tensor memory (4 x 128 columns), loads the item's gy block once and the x block of every non-pad relation of
-//   the group, and runs 8 MMAs (K = 16 shots each) per relation.  The CTAs of one split take a fixed contiguous
-//   range of items, write fp32 partial sums, and a second kernel adds the splits in a fixed order: deterministic,
+//   the group, and runs 8 MMAs (K = 16 shots each) per relation.  The CTAs of split s take the items s, s + splits,
+//   ... (so all CTAs sweep one window of consecutive items together and share its blocks in L2), write fp32
+//   partial sums, and a second kernel adds the splits in a fixed order: deterministic,
 //   no atomics (the reference's split-K with a torch sum, cascade_triton.py:120-136).
 //   CUDA cores (fp32, or shapes the tensor-core path does not take): 32 x 32 output tiles, rows staged in shared
 //   memory, the same partial-sum format and reduction.
@@ -62,7 +63,7 @@ struct WgArgs {
   const int32_t* idx;
   int NT, NS, K, Ci, Co;
   int64_t num_items;          // NT x ceil(B / 128), item = stile * NT + n
-  int64_t items_per_split;
+  int64_t splits;             // split s takes items s, s + splits, s + 2 splits, ...
   int rg, n_groups, n_otiles, n_itiles;
   int n_abox, n_bbox;         // boxes per A (gy) and B (x) operand
   int n_mma;                  // N of the MMAs (channels of the i tile rounded up to 16)
@@ -110,8 +111,9 @@ __global__ void __launch_bounds__(kWgThreads, 1)
   const int split = b / a.n_groups;
   const int r0 = g * a.rg;
   const int rn = min(a.rg, a.K - r0);
-  const int64_t i_begin = split * a.items_per_split;
-  const int64_t i_end = min(a.num_items, i_begin + a.items_per_split);
+  // items split, split + splits, ...: at any time the CTAs of every split work on one window of consecutive items
+  // (consecutive target nodes of one shot tile), so the source and gradient blocks they share are read from L2
+  const int64_t n_mine = split < a.num_items ? (a.num_items - split + a.splits - 1) / a.splits : 0;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -148,7 +150,7 @@ __global__ void __launch_bounds__(kWgThreads, 1)
       uint32_t aph = 0, bph = 0;
       uint32_t armed_a = 0, armed_b = 0, par_a = 0, par_b = 0;
       bool ok = true;
-      for (int64_t item = i_begin; item < i_end && ok; ++item) {
+      for (int64_t item = split; item < a.num_items && ok; item += a.splits) {
         const int n = static_cast<int>(item % a.NT);
         const int32_t s0 = static_cast<int32_t>((item / a.NT) * kWgShots);
         int src[kWgMaxRel];
@@ -204,7 +206,7 @@ __global__ void __launch_bounds__(kWgThreads, 1)
       uint32_t aph = 0, bph = 0;
       uint32_t started = 0;
       bool ok = true;
-      for (int64_t item = i_begin; item < i_end && ok; ++item) {
+      for (int64_t item = split; item < a.num_items && ok; item += a.splits) {
         const int n = static_cast<int>(item % a.NT);
         int src[kWgMaxRel];
         const uint32_t vm = group_mask(a, n, r0, rn, src);
@@ -251,7 +253,7 @@ __global__ void __launch_bounds__(kWgThreads, 1)
     const int o = ot * 128 + row;
     // the accumulators are final only when this CTA's whole item range is done: allow 20 us per item on top of the
     // watchdog limit (an item is at most 32 MMAs)
-    const uint64_t limit = a.timeout_ns + static_cast<uint64_t>(i_end - i_begin) * 20000ull;
+    const uint64_t limit = a.timeout_ns + static_cast<uint64_t>(n_mine) * 20000ull;
     bool ok = mbar_wait(smem_u32(done), 0, abort_flag, a.status, limit);
     ok = ok && mbar_wait(smem_u32(accf), 0, abort_flag, a.status, limit);
     ok = ok && !*abort_flag;
@@ -388,7 +390,7 @@ __global__ void wgrad_reduce_kernel(const float* __restrict__ partial, float* __
 struct WgPlan {
   bool tc;
   int rg, n_groups, n_otiles, n_itiles, splits;
-  int64_t items, items_per_split;   // tensor-core path
+  int64_t items;                    // tensor-core path
   int n_ot, n_it;                   // CUDA-core path (32 x 32 tiles)
   int64_t rows, rows_per_split;
 };
@@ -411,8 +413,7 @@ WgPlan plan_wgrad(int64_t B, int32_t NT, int32_t K, int32_t Ci, int32_t Co, int3
     const int per = p.n_groups * p.n_otiles * p.n_itiles;
     int64_t splits = std::max<int64_t>(1, sms / per);
     splits = std::min<int64_t>(splits, std::max<int64_t>(1, p.items));
-    p.items_per_split = (p.items + splits - 1) / splits;
-    p.splits = static_cast<int>((p.items + p.items_per_split - 1) / p.items_per_split);
+    p.splits = static_cast<int>(splits);   // every split has at least one item (splits <= items)
   } else {
     p.n_ot = (Co + 31) / 32;
     p.n_it = (Ci + 31) / 32;
@@ -470,7 +471,7 @@ int gmm_wgrad_launch(const void* x, const void* gy, const int32_t* idx, float* d
     a.Ci = Ci;
     a.Co = Co;
     a.num_items = p.items;
-    a.items_per_split = p.items_per_split;
+    a.splits = p.splits;
     a.rg = p.rg;
     a.n_groups = p.n_groups;
     a.n_otiles = p.n_otiles;
