@@ -260,44 +260,79 @@ def measure_config(name, shots, steps, warmup, dev, pk, cpu_seconds):
                              "sample": f"{n_shots} shots through the CPU oracle (fp32) at batch {cb}"}}
 
 
-def measure_cascade_stack(tables_npz, dev, shots=512, steps=5):
-    """14 C14-shaped bottleneck blocks (the reference's Cascade BB72 network's backbone: H = 512, the bipartite
-    convolution at 128 channels on the BB72 Tanner graph, cascade_net.py:236-259) in eval mode, seeded weights and
-    BatchNorm statistics: device time per shot at `shots` shots.  The graph's tables are the reference's
-    Geometry('bb72') tables as recorded in the test fixture."""
+def synthetic_bb_layout(T, n2, n_det, k, seed):
+    """A seeded stand-in for a BB code memory's circuit layout (the reference reads it from its Stim circuit):
+    n_det detectors on distinct nodes of the (type, round, site) grid and k observables of 12 data qubits each."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    node = np.sort(rng.choice(2 * T * n2, size=n_det, replace=False))
+    det_typ, rem = np.divmod(node, T * n2)
+    det_t, det_site = np.divmod(rem, n2)
+    logicals = np.zeros((k, 2 * n2), np.int64)
+    for o in range(k):
+        logicals[o, rng.choice(2 * n2, size=12, replace=False)] = 1
+    return det_t, det_typ, det_site, logicals
+
+
+def measure_cascade_net(tables_npz, dev, pk, shots=4096, steps=5, warmup=3):
+    """The reference's Cascade BB72 network at C14's size (CascadeBB, cascade_net.py:262-343: H = 512, 14 bottleneck
+    blocks with the bipartite convolution at 128 channels, pooled scatter read-out, 12 observables) in eval mode,
+    seeded weights and BatchNorm statistics, on a seeded synthetic detector layout: device time per shot at `shots`
+    shots with the detector bits resident on the GPU (the reference quotes C14 at batch 4,096, input on GPU), and
+    the backbone (the 14 blocks alone) beside it.  The graph's tables are the reference's Geometry('bb72') tables as
+    recorded in the test fixture."""
     import numpy as np
     import torch
     from types import SimpleNamespace
-    from codecoder_b200.modules import CascadeBlock, CascadeStack
+    from codecoder_b200.modules import CascadeNet, CascadeStack
     z = np.load(tables_npz)
-    geo = SimpleNamespace(c2d=[z["c2d0"], z["c2d1"]], d2c=[z["d2c0"], z["d2c1"]],
+    T, n2, N = int(z["T"]), int(z["n2"]), int(z["N"])
+    geo = SimpleNamespace(T=T, n2=n2, N=N, c2d=[z["c2d0"], z["c2d1"]], d2c=[z["d2c0"], z["d2c1"]],
                           inv_c2d=[z["inv_c2d0"].astype(np.int64), z["inv_c2d1"].astype(np.int64)],
                           inv_d2c=[z["inv_d2c0"].astype(np.int64), z["inv_d2c1"].astype(np.int64)])
+    H, L, n_det, k = 512, 14, 360, 12
     torch.manual_seed(SEED)
-    blocks = CascadeStack([CascadeBlock(512, geo, 14, res="skip") for _ in range(14)]).to(dev).eval()
-    for b in blocks.blocks:
-        for i in (1, 2, 3):
-            getattr(b, f"bn{i}").running_var.uniform_(0.5, 2.0)
-    h = torch.randn(shots, int(z["N"]), 512, device=dev)
+    net = CascadeNet(geo, H, L, *synthetic_bb_layout(T, n2, n_det, k, SEED), res="skip").to(dev).eval()
     with torch.no_grad():
-        for _ in range(3):
-            blocks(h)
-        torch.cuda.synchronize()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        for _ in range(steps):
-            out = blocks(h)
-        e.record()
-        e.synchronize()
-    ms = s.elapsed_time(e) / steps
-    if not bool(torch.isfinite(out).all()):
-        raise RuntimeError("C14 stack produced non-finite values")
-    return {"workload": f"14 Cascade bottleneck blocks, H=512 (bottleneck 128), BB72 graph ({int(z['N'])} nodes), "
-                        f"eval, bf16 bottleneck + fp32 residual stream, {shots} shots", "ms_per_batch": ms,
-            "us_per_shot": ms * 1000.0 / shots,
-            "kernels": "per block: gmm_tc_kernel (down + BN2 + SiLU), gmm_wide_kernel x2 (two-type conv, conv + BN3 "
-                       "+ SiLU), cuBLAS bf16 GEMM (up, a plain dense projection), residual_affine_silu_kernel "
-                       "(residual + next block's BN1 + SiLU)"}
+        for m in net.modules():
+            if isinstance(m, torch.nn.BatchNorm1d):
+                m.running_var.uniform_(0.5, 2.0)
+        net.mlp2.weight.normal_()
+    rng = np.random.default_rng(SEED)
+    det = torch.as_tensor((rng.random((shots, n_det)) < 0.05).astype(np.uint8), device=dev)
+    h0 = torch.randn(shots, N, H, device=dev)
+
+    def timed(fn):
+        with torch.no_grad():
+            for _ in range(warmup):
+                out = fn()
+            torch.cuda.synchronize()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            for _ in range(steps):
+                out = fn()
+            e.record()
+            e.synchronize()
+        if not bool(torch.isfinite(out).all()):
+            raise RuntimeError("C14-sized Cascade network produced non-finite values")
+        return s.elapsed_time(e) / steps
+
+    ms = timed(lambda: net(det))
+    ms_blocks = timed(lambda: CascadeStack.forward_blocks(net.blocks, h0))
+    Hb, K = H // 4, int(z["c2d0"].shape[1])
+    flop = L * (2 * 2 * N * K * Hb * Hb + 2 * 2 * N * H * Hb) + 2 * k * 2 * K * N * H + 2 * k * 2 * K * H * H \
+        + 2 * k * (H * 2 * H + 2 * H)
+    return {"workload": f"Cascade network at C14 size: H=512, 14 bottleneck blocks (conv at 128 channels), BB72 graph "
+                        f"({N} nodes), {n_det} detectors (seeded synthetic layout), {k} observables, eval, bf16 "
+                        f"bottleneck and read-out GEMMs + fp32 residual stream, {shots} shots, input on the GPU",
+            "shots": shots, "ms_per_batch": ms, "us_per_shot": ms * 1000.0 / shots,
+            "backbone_us_per_shot": ms_blocks * 1000.0 / shots, "flop_per_shot": flop,
+            "tflops": flop * shots / (ms * 1e-3) / 1e12, "tensor_frac_of_sustained": flop * shots / (ms * 1e-3) / 1e12
+            / pk["bf16_tflops_sustained"],
+            "kernels": "stem (torch gather + embedding); per block: gmm_tc_kernel (down + BN2 + SiLU), gmm_wide_kernel "
+                       "x2 (two-type conv, conv + BN3 + SiLU), cuBLAS bf16 GEMM (up, a plain dense projection), "
+                       "residual_affine_silu_kernel (residual + next block's BN1 + SiLU, or bn_out + SiLU after the "
+                       "last); read-out: cuBLAS bf16 GEMMs (pooling, scatter, MLP)"}
 
 
 def run_reference(args, cfg, g, params, rank, world):
@@ -544,7 +579,7 @@ def main():
     cascade = None
     golden_bb72 = os.path.join(REPO, "tests", "golden", "bb72_c14_conv.npz")
     if rank == 0 and world == 1 and not args.no_configs and os.path.exists(golden_bb72):
-        cascade = measure_cascade_stack(golden_bb72, dev)
+        cascade = measure_cascade_net(golden_bb72, dev, pk)
 
     configs = None
     if rank == 0 and world == 1 and not args.no_configs:

@@ -20,7 +20,7 @@ import torch.nn.functional as F
 from torch import nn
 
 from . import _lib
-from .ops import gather_mm
+from .ops import gather_mm, residual_affine_silu
 
 
 class BipartiteConv(nn.Module):
@@ -325,10 +325,93 @@ class CascadeStack(nn.Module):
             for b in self.blocks:
                 h = b(h)
             return h
+        return CascadeStack.forward_blocks(self.blocks, h)
+
+    @staticmethod
+    def forward_blocks(blocks, h):
+        """The fused inference path over a sequence of CascadeBlocks (eval mode, fp32 h on the GPU)."""
         x = None
-        for i, b in enumerate(self.blocks):
+        for i, b in enumerate(blocks):
             if b._cache is None or b._cache["a1"].device != h.device:
                 b.prepare_inference()
-            nxt = self.blocks[i + 1] if i + 1 < len(self.blocks) else None
+            nxt = blocks[i + 1] if i + 1 < len(blocks) else None
             h, x = b._fused(h, x, nxt)
         return h
+
+
+class CascadeNet(nn.Module):
+    """The reference's whole Cascade network for a BB code memory, CascadeBB (cascade_net.py:262-343): detector bits
+    (B, D) -> one logit per observable (B, k), with its parameter names (embed, blocks.*, bn_out, scatter, mlp1,
+    mlp2) so its state_dicts load unchanged.
+
+    geo: the code's Tanner-graph tables with T, n2, N, c2d / d2c (per data / check type, (T n2, 12)) and their
+    inverses, as the reference's Geometry gives them; det_t / det_typ / det_site: each detector's place; logicals
+    (k, 2 n2): the observables' supports on the data qubits.
+      stem      token = 2 type + bit at every detector's node, 4 at nodes without a detector; Embedding(5, H)
+      blocks    L CascadeBlocks (the fused inference path of CascadeStack in eval mode on the GPU)
+      read-out  SiLU(bn_out(h)); per observable the pooled sources of its support's check -> data relations
+                (a fixed (24 k, N) pooling matrix), the scatter projection (24 H -> H), mlp1, SiLU, mlp2
+    Eval on the GPU: the blocks on the B200 kernels; bn_out + SiLU in one pass (bpc_residual_affine_silu); the
+    read-out's pooling and scatter are plain dense GEMMs (cuBLAS) in bf16 as under the reference's autocast, its MLP
+    in fp32."""
+
+    def __init__(self, geo, H, L, det_t, det_typ, det_site, logicals, res="branch"):
+        super().__init__()
+        if H % 4:
+            raise ValueError("H must be a multiple of 4")
+        self.H, self.L = H, L
+        T, n2, N = int(geo.T), int(geo.n2), int(geo.N)
+        det_t, det_typ, det_site = (np.asarray(a, np.int64) for a in (det_t, det_typ, det_site))
+        self.D = D = len(det_t)
+        node = (det_typ * T + det_t) * n2 + det_site
+        if len(np.unique(node)) != D or node.max() >= N:
+            raise ValueError("detector places collide or fall outside the grid")
+        gidx = np.full(N, D, np.int64)
+        gidx[node] = np.arange(D)
+        tbase = np.full(N, 4, np.int64)               # the "absent" token
+        tbase[node] = 2 * det_typ
+        self.register_buffer("gidx", torch.as_tensor(gidx), persistent=False)
+        self.register_buffer("tbase", torch.as_tensor(tbase), persistent=False)
+        self.embed = nn.Embedding(5, H)
+        self.blocks = nn.ModuleList([CascadeBlock(H, geo, L, res) for _ in range(L)])
+        self.bn_out = nn.BatchNorm1d(H)
+        logicals = np.asarray(logicals, np.int64)
+        self.k = k = len(logicals)
+        self.support = [np.flatnonzero(r) for r in logicals]      # each observable's data qubits, d n2 + s
+        K = int(np.asarray(geo.c2d[0]).shape[1])
+        pool = np.zeros((k, 2, K, N + 1))
+        for o in range(k):
+            sup = np.flatnonzero(logicals[o])
+            w = 1.0 / (T * len(sup))
+            for q in sup:
+                d, s = divmod(int(q), n2)
+                for t in range(T):
+                    np.add.at(pool[o, d], (np.arange(K), np.asarray(geo.c2d[d])[t * n2 + s]), w)
+        self.register_buffer("pool", torch.as_tensor(pool[..., :N].reshape(k * 2 * K, N), dtype=torch.float32),
+                             persistent=False)
+        self.scatter = nn.Parameter(torch.randn(H, 2 * K * H) / math.sqrt(K * H))
+        self.mlp1 = nn.Linear(H, 2 * H)
+        self.mlp2 = nn.Linear(2 * H, 1)
+
+    def tokens(self, det: torch.Tensor) -> torch.Tensor:
+        det = F.pad(det.to(torch.uint8), (0, 1))
+        return self.tbase + det[:, self.gidx].long()
+
+    def readout(self, x: torch.Tensor, dt: torch.dtype | None = None) -> torch.Tensor:
+        """x = SiLU(bn_out(h)) (B, N, H) -> (B, k): the pooling and scatter GEMMs in dt (x's dtype by default), the
+        observables' MLP (k rows per shot, a negligible share of the work) in fp32."""
+        B, dt = x.shape[0], dt or x.dtype
+        pooled = torch.matmul(self.pool.to(dt), x.to(dt))                      # (B, 24 k, H)
+        z = (pooled.view(B, self.k, -1) @ self.scatter.t().to(dt)).float()     # (B, k, H)
+        return self.mlp2(F.silu(self.mlp1(z))).squeeze(-1)
+
+    def forward(self, det: torch.Tensor) -> torch.Tensor:
+        h = self.embed(self.tokens(det))
+        if self.training or not h.is_cuda:
+            for b in self.blocks:
+                h = b(h)
+            return self.readout(F.silu(self.bn_out(h.reshape(-1, self.H)).view(h.shape)))
+        h = CascadeStack.forward_blocks(self.blocks, h.float().contiguous())
+        a, b = _fold_bn(self.bn_out)
+        _, x = residual_affine_silu(h, None, 1.0, 0.0, a, b, want_out=False)
+        return self.readout(x, torch.bfloat16)

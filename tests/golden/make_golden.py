@@ -14,6 +14,9 @@ It imports the reference's bb.cascade_net (training/bb/ising_compare/bb/cascade_
   cascade_block_c14.npz  the reference's Block(512, Geometry('bb72'), L=14, res='skip') in eval mode with the C14
                          network's block-0 weights (relation, down and up matrices rounded to bf16; BatchNorm in
                          fp32) on a seeded bf16-valued input, and its output (fp32, CPU)
+  cascade_net_bb72.npz   the reference's whole CascadeBB (H = 128, L = 2) on the BB72 graph with a seeded synthetic
+                         detector layout (the Stim layout is absent): its state_dict, the layout, seeded shots and
+                         the fp32 CPU forward's logits
   gather_mm_bwd.npz      input and weight gradients from the reference's _GatherMM.backward (autograd through
                          cn.gather_mm, fp32, CPU) for seeded upstream gradients: rotated-surface steps at several
                          widths and BipartiteConv(128, Geometry('bb72')) with the C14 relation matrices (its
@@ -228,10 +231,72 @@ def make_cascade_block():
     print("cascade_block_c14", h.shape, float(out.abs().mean()))
 
 
+def synthetic_bb72_layout(geo, rng, D=360, k=12):
+    """A seeded stand-in for the Relay-BP circuit layout (bb.code.Layout needs Stim, which is absent): D detectors on
+    distinct nodes of the (type, round, site) grid and k observables with supports on the 2 n2 data qubits."""
+    T, n2 = geo.T, geo.n2
+    node = np.sort(rng.choice(2 * T * n2, size=D, replace=False))
+    det_typ, rem = np.divmod(node, T * n2)
+    det_t, det_site = np.divmod(rem, n2)
+    logicals = np.zeros((k, 2 * n2), np.int64)
+    for o in range(k):
+        logicals[o, rng.choice(2 * n2, size=12, replace=False)] = 1
+    return det_t.astype(np.int64), det_typ.astype(np.int64), det_site.astype(np.int64), logicals
+
+
+def make_cascade_net():
+    """The reference's whole CascadeBB (stem, blocks, bn_out, pooled scatter read-out, MLP) at H = 128, L = 2 on the
+    BB72 graph with a seeded synthetic layout; BatchNorm statistics and the (zero-initialised) last MLP layer drawn at
+    random and the scatter projection scaled by 4, with a detector density of 0.25, so that the logits vary from shot
+    to shot by ~15 % of their size (at initialisation they hardly depend on the detectors); matrices of the blocks
+    rounded to bf16; fp32 CPU forward on 16 seeded shots, and the same forward under CPU bf16 autocast (the
+    reference's own bf16 rounding error, the scale of the parity bar)."""
+    geo = cn.Geometry("bb72")
+    rng = np.random.default_rng(1405)
+    det_t, det_typ, det_site, logicals = synthetic_bb72_layout(geo, rng)
+    torch.manual_seed(1405)
+    m = cn.CascadeBB("bb72", 128, 2, det_t, det_typ, det_site, logicals, res="skip", conv_impl="torch")
+    with torch.no_grad():
+        for name, mod in m.named_modules():
+            if isinstance(mod, torch.nn.BatchNorm1d):
+                mod.running_mean.copy_(torch.as_tensor(rng.standard_normal(mod.num_features) * 0.1, dtype=torch.float32))
+                mod.running_var.copy_(torch.as_tensor(rng.uniform(0.5, 2.0, mod.num_features), dtype=torch.float32))
+                mod.weight.copy_(torch.as_tensor(rng.uniform(0.5, 1.5, mod.num_features), dtype=torch.float32))
+                mod.bias.copy_(torch.as_tensor(rng.standard_normal(mod.num_features) * 0.1, dtype=torch.float32))
+        m.mlp2.weight.copy_(torch.as_tensor(rng.standard_normal(m.mlp2.weight.shape), dtype=torch.float32))
+        m.mlp2.bias.copy_(torch.as_tensor(rng.standard_normal(1) * 0.1, dtype=torch.float32))
+        m.scatter.mul_(4.0)
+        for name, p in m.named_parameters():
+            if name.startswith("blocks.") and p.ndim == 2:
+                p.copy_(torch.as_tensor(round_bf16(p.numpy())))
+    m.eval()
+    det = (rng.random((16, len(det_t))) < 0.25).astype(np.uint8)
+    with torch.no_grad():
+        logits = m(torch.as_tensor(det))
+    o = {"det": det, "logits": logits.numpy(), "det_t": det_t, "det_typ": det_typ, "det_site": det_site,
+         "logicals": logicals, "H": 128, "L": 2, "res": "skip", "T": geo.T, "n2": geo.n2, "N": geo.N}
+    for k in range(2):
+        o[f"c2d{k}"] = np.asarray(geo.c2d[k], np.int32)
+        o[f"d2c{k}"] = np.asarray(geo.d2c[k], np.int32)
+    with torch.no_grad(), torch.autocast("cpu", dtype=torch.bfloat16):
+        o["logits_autocast"] = m(torch.as_tensor(det)).float().numpy()     # the reference's own bf16 run
+    o["tokens"] = m.tokens(torch.as_tensor(det)).numpy().astype(np.uint8)
+    o["pool"] = m.pool.numpy()
+    for name, v in m.state_dict().items():
+        o["sd." + name] = v.numpy()
+    np.savez_compressed(os.path.join(HERE, "cascade_net_bb72.npz"), **o)
+    print("cascade_net_bb72", det.shape, logits.shape, float(logits.abs().mean()), float(logits.std(0).mean()))
+
+
 if __name__ == "__main__":
     torch.manual_seed(0)
+    if len(sys.argv) > 1:
+        for name in sys.argv[1:]:
+            globals()[name]()
+        sys.exit(0)
     make_bb72()
     make_surface_gmm()
     make_predecoder()
     make_backward()
     make_cascade_block()
+    make_cascade_net()

@@ -1,9 +1,14 @@
 """The reference's bottleneck Block (cascade_net.py:236-259) on the B200 op: the fused inference path against the
 reference's own Block with the trained C14 block-0 weights (golden fixture), training mode (batch statistics,
-backward through the op) against an fp64 composition, and the time of a 14-block C14 stack.
+backward through the op) against an fp64 composition, and the time of a 14-block C14 stack.  The whole network
+(CascadeBB, cascade_net.py:262-343, as CascadeNet): eval logits against the reference's on seeded shots, and a
+training-mode step under bf16 autocast.
 
 Tolerances: relative to max |ref|; 2e-2 for the bf16 inference path (four bf16 roundings of bottleneck activations
-around an fp32 residual), 1e-4 for training mode in fp32."""
+around an fp32 residual), 1e-4 for training mode in fp32.  The whole network's logits: 2e-2 of max |ref|, and 5e-2
+of the largest shot-to-shot deviation for the logits less their mean over shots (the bf16 read-out GEMMs add their
+roundings to the blocks'), and neither above the same statistic of the reference's own bf16 autocast run against
+its fp32 run."""
 import os
 import time
 from types import SimpleNamespace
@@ -14,7 +19,7 @@ import torch
 import torch.nn.functional as F
 
 from codecoder_b200.geometry import RotatedSurface
-from codecoder_b200.modules import CascadeBlock, CascadeStack
+from codecoder_b200.modules import CascadeBlock, CascadeNet, CascadeStack
 from oracle import predecoder_oracle as orc
 
 pytestmark = pytest.mark.gpu
@@ -129,3 +134,53 @@ def test_cascade_c14_stack_time(c14):
             one = b(one)
         assert rel(blocks(h[:4]), one) < 1e-5
     print("C14 block stack (14 blocks, bb72, H=512): %.2f us/shot at 512 shots" % us)
+
+
+@pytest.fixture(scope="module")
+def cascade_net_z(golden_dir):
+    return dict(np.load(os.path.join(golden_dir, "cascade_net_bb72.npz")))
+
+
+def make_cascade_net(z, conv_z):
+    geo = bb72_geo(conv_z)
+    geo.T, geo.n2, geo.N = int(z["T"]), int(z["n2"]), int(z["N"])
+    net = CascadeNet(geo, int(z["H"]), int(z["L"]), z["det_t"], z["det_typ"], z["det_site"], z["logicals"],
+                     res=str(z["res"]))
+    net.load_state_dict({k[3:]: torch.as_tensor(v) for k, v in z.items() if k.startswith("sd.")})
+    return net.cuda()
+
+
+def test_cascade_net_inference_matches_reference_bb72(c14, cascade_net_z):
+    conv_z, _ = c14
+    z = cascade_net_z
+    net = make_cascade_net(z, conv_z).eval()
+    with torch.no_grad():
+        out = net(torch.as_tensor(z["det"]).cuda())
+    torch.cuda.synchronize()
+    ref = z["logits"]
+    assert out.shape == ref.shape and out.dtype == torch.float32
+    err = rel(out, ref)
+    dev = rel(out - out.mean(0), ref - ref.mean(0))
+    # the reference's own bf16 autocast run, against its fp32 run: the same two statistics
+    ra = z["logits_autocast"]
+    err_ref, dev_ref = rel(ra, ref), rel(ra - ra.mean(0), ref - ref.mean(0))
+    print("CascadeNet (H=128, L=2, bb72) vs the reference: rel err %.2e, of the shot deviations %.2e "
+          "(the reference's own bf16 run: %.2e, %.2e)" % (err, dev, err_ref, dev_ref))
+    assert err < 2e-2 and dev < 5e-2
+    assert err <= err_ref and dev <= dev_ref
+
+
+def test_cascade_net_training_step_under_autocast(c14, cascade_net_z):
+    conv_z, _ = c14
+    z = cascade_net_z
+    net = make_cascade_net(z, conv_z).train()
+    det = torch.as_tensor(z["det"]).cuda()
+    target = torch.randint(0, 2, (det.shape[0], int(net.k)), device="cuda").float()
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        logits = net(det)
+        loss = F.binary_cross_entropy_with_logits(logits.float(), target)
+    loss.backward()
+    assert torch.isfinite(loss)
+    for n, p in net.named_parameters():
+        assert p.grad is not None and bool(torch.isfinite(p.grad).all()), n
+    assert float(net.scatter.grad.abs().max()) > 0 and float(net.blocks[0].conv.w_c2d[0].grad.abs().max()) > 0
