@@ -53,7 +53,10 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-parity", action="store_true")
     ap.add_argument("--no-stream", action="store_true")
-    ap.add_argument("--no-configs", action="store_true", help="skip the d=5 fp32 and d=9 bf16 workloads")
+    ap.add_argument("--no-configs", action="store_true", help="skip the d=5 fp32, d=9 bf16 and Cascade workloads")
+    ap.add_argument("--cascade-only", action="store_true",
+                    help="time only the C14-size Cascade network (one JSON object; for launch lists and profiles)")
+    ap.add_argument("--cascade-shots", type=int, default=4096, help="shots of the Cascade network's batch")
     ap.add_argument("--stream-rounds", type=int, default=20000)
     ap.add_argument("--no-train", action="store_true")
     ap.add_argument("--train-steps", type=int, default=6)
@@ -318,7 +321,7 @@ def measure_cascade_net(tables_npz, dev, pk, shots=4096, steps=5, warmup=3):
         return s.elapsed_time(e) / steps
 
     ms = timed(lambda: net(det))
-    ms_blocks = timed(lambda: CascadeStack.forward_blocks(net.blocks, h0))
+    ms_blocks = timed(lambda: CascadeStack.forward_blocks(net.blocks, h0)[0])
     Hb, K = H // 4, int(z["c2d0"].shape[1])
     flop = L * (2 * 2 * N * K * Hb * Hb + 2 * 2 * N * H * Hb) + 2 * k * 2 * K * N * H + 2 * k * 2 * K * H * H \
         + 2 * k * (H * 2 * H + 2 * H)
@@ -329,10 +332,11 @@ def measure_cascade_net(tables_npz, dev, pk, shots=4096, steps=5, warmup=3):
             "backbone_us_per_shot": ms_blocks * 1000.0 / shots, "flop_per_shot": flop,
             "tflops": flop * shots / (ms * 1e-3) / 1e12, "tensor_frac_of_sustained": flop * shots / (ms * 1e-3) / 1e12
             / pk["bf16_tflops_sustained"],
-            "kernels": "stem (torch gather + embedding); per block: gmm_tc_kernel (down + BN2 + SiLU), gmm_wide_kernel "
-                       "x2 (two-type conv, conv + BN3 + SiLU), cuBLAS bf16 GEMM (up, a plain dense projection), "
-                       "residual_affine_silu_kernel (residual + next block's BN1 + SiLU, or bn_out + SiLU after the "
-                       "last); read-out: cuBLAS bf16 GEMMs (pooling, scatter, MLP)"}
+            "kernels": "stem (torch gather + embedding); first block's BN1 + SiLU (residual_affine_silu_kernel) and "
+                       "down + BN2 + SiLU (gmm_tc_kernel); per block: the two-type conv (gmm_wide_kernel check -> data, "
+                       "gmm_tc_kernel data -> check + BN3 + SiLU) and cascade_boundary_kernel (up, residual, the next "
+                       "block's BN1 + SiLU + down + BN2 + SiLU, or bn_out + SiLU after the last); read-out: cuBLAS "
+                       "bf16 GEMMs (pooling, scatter)"}
 
 
 def run_reference(args, cfg, g, params, rank, world):
@@ -397,6 +401,12 @@ def main():
         build()
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    if args.cascade_only:
+        if rank == 0:
+            print(json.dumps(measure_cascade_net(os.path.join(REPO, "tests", "golden", "bb72_c14_conv.npz"), dev,
+                                                 peaks(), shots=args.cascade_shots, steps=args.steps,
+                                                 warmup=args.warmup)))
+        return
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
         dist.barrier()

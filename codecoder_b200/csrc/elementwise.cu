@@ -47,14 +47,14 @@ __global__ void __launch_bounds__(256) residual_affine_silu_kernel(const float* 
       reinterpret_cast<float4*>(out)[2 * gi + 1] = make_float4(v[4], v[5], v[6], v[7]);
     }
     if (x) {
+      // SiLU on the hardware tanh (its result is rounded to bf16 right after), as the block-boundary kernel does
       uint4 o;
       uint32_t* op = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float s0 = silu_exact(fmaf(__ldg(a + c0 + 2 * e), v[2 * e], __ldg(b + c0 + 2 * e)));
-        const float s1 = silu_exact(fmaf(__ldg(a + c0 + 2 * e + 1), v[2 * e + 1], __ldg(b + c0 + 2 * e + 1)));
-        const __nv_bfloat162 p = __floats2bfloat162_rn(s0, s1);
-        op[e] = *reinterpret_cast<const uint32_t*>(&p);
+        const uint64_t av = f2_pack(__ldg(a + c0 + 2 * e), __ldg(a + c0 + 2 * e + 1));
+        const uint64_t bv = f2_pack(__ldg(b + c0 + 2 * e), __ldg(b + c0 + 2 * e + 1));
+        op[e] = f2_to_bf2(silu_tanh_fast2(f2_fma(av, f2_pack(v[2 * e], v[2 * e + 1]), bv)));
       }
       reinterpret_cast<uint4*>(x)[gi] = o;
     }

@@ -325,18 +325,57 @@ class CascadeStack(nn.Module):
             for b in self.blocks:
                 h = b(h)
             return h
-        return CascadeStack.forward_blocks(self.blocks, h)
+        return CascadeStack.forward_blocks(self.blocks, h)[0]
 
     @staticmethod
-    def forward_blocks(blocks, h):
-        """The fused inference path over a sequence of CascadeBlocks (eval mode, fp32 h on the GPU)."""
-        x = None
-        for i, b in enumerate(blocks):
+    def forward_blocks(blocks, h, final=None):
+        """The fused inference path over a sequence of CascadeBlocks (eval mode, fp32 h on the GPU) -> (h, x): the
+        residual stream after the last block, and with `final` = (scale, shift) of a folded BatchNorm, x =
+        bf16(SiLU(scale h + shift)) (then h is None: a caller that asks for x needs only x).
+        Blocks of H = 512 with a 128-channel bottleneck (the reference's C14 blocks) hand over in one launch per block
+        boundary (bpc_cascade_boundary: up, residual, the next block's BN1 + SiLU, down and BN2 + SiLU); other sizes
+        run the block-by-block fused path."""
+        for b in blocks:
             if b._cache is None or b._cache["a1"].device != h.device:
                 b.prepare_inference()
+        if all(tuple(b.up.weight.shape) == (512, 128) for b in blocks):
+            return CascadeStack._forward_boundaries(blocks, h, final)
+        x = None
+        for i, b in enumerate(blocks):
             nxt = blocks[i + 1] if i + 1 < len(blocks) else None
             h, x = b._fused(h, x, nxt)
-        return h
+        if final is None:
+            return h, None
+        _, x = residual_affine_silu(h.contiguous(), None, 1.0, 0.0, final[0], final[1], want_out=False)
+        return None, x
+
+    @staticmethod
+    def _forward_boundaries(blocks, h, final):
+        from .ops import cascade_boundary, gmm_ex
+        h = h.contiguous()
+        c = blocks[0]._cache
+        N = h.shape[1]
+        if c["ident"].numel() != N or c["ident"].device != h.device:
+            c["ident"] = torch.arange(N, dtype=torch.int32, device=h.device).view(N, 1)
+        _, x1 = residual_affine_silu(h, None, 1.0, 0.0, c["a1"], c["b1"], want_out=False)
+        x2 = gmm_ex(x1, c["ident"], c["down"], scale=c["a2"], shift=c["b2"])
+        stream, x = h, None
+        for i, b in enumerate(blocks):
+            c = b._cache
+            d = gmm_ex(x2, b.c2d_all, c["wc"], type_split=b._splits[0])
+            x3 = gmm_ex(d, b.d2c_all, c["wd"], type_split=b._splits[1], scale=c["a3"], shift=c["b3"])
+            sh, su = (1.0, b.scale) if b.res == "branch" else (b.scale, 1.0)
+            out = torch.empty_like(h) if stream is h else stream      # the caller's h is never written
+            if i + 1 < len(blocks):
+                n = blocks[i + 1]._cache
+                stream, x2 = cascade_boundary(x3, c["up"], stream, sh, su, n["a1"], n["b1"], n["down"], n["a2"],
+                                              n["b2"], h_out=out)
+            elif final is None:
+                stream, _ = cascade_boundary(x3, c["up"], stream, sh, su, h_out=out, want_y=False)
+            else:
+                _, x = cascade_boundary(x3, c["up"], stream, sh, su, final[0], final[1], h_out=None)
+                stream = None
+        return stream, x
 
 
 class CascadeNet(nn.Module):
@@ -411,7 +450,5 @@ class CascadeNet(nn.Module):
             for b in self.blocks:
                 h = b(h)
             return self.readout(F.silu(self.bn_out(h.reshape(-1, self.H)).view(h.shape)))
-        h = CascadeStack.forward_blocks(self.blocks, h.float().contiguous())
-        a, b = _fold_bn(self.bn_out)
-        _, x = residual_affine_silu(h, None, 1.0, 0.0, a, b, want_out=False)
+        _, x = CascadeStack.forward_blocks(self.blocks, h.float().contiguous(), final=_fold_bn(self.bn_out))
         return self.readout(x, torch.bfloat16)

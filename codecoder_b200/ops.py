@@ -103,6 +103,41 @@ def gmm_ex(a: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, type_split: int 
     return y
 
 
+def cascade_boundary(x3: torch.Tensor, w_up: torch.Tensor, h: torch.Tensor, scale_h: float, scale_u: float,
+                     a1: torch.Tensor | None = None, b1: torch.Tensor | None = None, w_down: torch.Tensor | None = None,
+                     a2: torch.Tensor | None = None, b2: torch.Tensor | None = None, h_out="new", want_y: bool = True):
+    """The boundary between two Cascade bottleneck blocks in one launch (C ABI bpc_cascade_boundary; H = 512, a
+    128-channel bottleneck): x3 (..., 128) bf16, w_up (512, 128) bf16, h (..., 512) fp32 ->
+    (h' = scale_h h + scale_u bf16(x3 w_up^T) fp32 or None,
+     y = bf16(SiLU(a2 (x1 w_down^T) + b2)) (..., 128) with w_down, else x1 = bf16(SiLU(a1 h' + b1)) (..., 512), or None).
+    h_out: "new" (allocate), a tensor to write (h itself updates in place), or None (h' not written)."""
+    _check_cuda(x3, w_up, h)
+    if x3.dtype != torch.bfloat16 or w_up.dtype != torch.bfloat16 or h.dtype != torch.float32:
+        raise TypeError("cascade_boundary: bf16 x3 and w_up, fp32 h")
+    H, Hb = w_up.shape
+    if x3.shape[-1] != Hb or h.shape[-1] != H or x3.shape[:-1] != h.shape[:-1]:
+        raise ValueError("cascade_boundary: x3 (..., Hb), w_up (H, Hb), h (..., H) with the same rows")
+    x3, w_up, h = x3.contiguous(), w_up.contiguous(), h.contiguous()
+    rows = h.numel() // H
+    out = torch.empty_like(h) if isinstance(h_out, str) else h_out
+    if out is not None and (out.shape != h.shape or out.dtype != torch.float32 or not out.is_contiguous()):
+        raise ValueError("cascade_boundary: h_out must be a contiguous fp32 tensor of h's shape")
+    vec = lambda t: None if t is None else t.to(h.device, torch.float32).contiguous()
+    a1, b1, a2, b2 = vec(a1), vec(b1), vec(a2), vec(b2)
+    y = None
+    if w_down is not None:
+        w_down = w_down.to(torch.bfloat16).contiguous()
+        y = torch.empty(*h.shape[:-1], w_down.shape[0], device=h.device, dtype=torch.bfloat16)
+    elif want_y and a1 is not None:
+        y = torch.empty(h.shape, device=h.device, dtype=torch.bfloat16)
+    ptr = lambda t: None if t is None else t.data_ptr()
+    rc = _lib.lib().bpc_cascade_boundary(x3.data_ptr(), w_up.data_ptr(), h.data_ptr(), ptr(out), float(scale_h),
+                                         float(scale_u), ptr(a1), ptr(b1), ptr(w_down), ptr(a2), ptr(b2), ptr(y),
+                                         rows, H, Hb, _stream_ptr(h.device))
+    _lib.check(rc, "bpc_cascade_boundary")
+    return out, y
+
+
 def residual_affine_silu(h: torch.Tensor, u: torch.Tensor | None, scale_h: float, scale_u: float,
                          a: torch.Tensor | None = None, b: torch.Tensor | None = None, want_out: bool = True):
     """One pass over an fp32 (..., H) stream (C ABI bpc_residual_affine_silu): v = scale_h h + scale_u u (u bf16 or

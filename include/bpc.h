@@ -67,6 +67,20 @@ BPC_API int bpc_gather_mm_fwd_ex(const void* x, const void* w, const int32_t* id
                                  int32_t epilogue, const float* scale, const float* shift, int32_t dtype,
                                  bpc_stream_t stream);
 
+/* The boundary between two Cascade bottleneck blocks in one launch (eval; H = 512 with a 128-channel bottleneck, the
+ * reference's C14 blocks, cascade_net.py:236-259): from the output x3 of one block's bipartite convolution to the
+ * input of the next block's convolution,
+ *   u = bf16(x3 W_up^T);  h' = scale_h h + scale_u u (fp32, written to h_out unless it is NULL; h_out may be h);
+ *   x1 = bf16(SiLU(a1 h' + b1));
+ *   w_down != NULL: y = bf16(SiLU(a2 (x1 W_down^T) + b2)) (rows, Hb): the next block's down projection + BN2 + SiLU;
+ *   w_down == NULL: y = x1 (rows, H), or nothing when y is NULL (after the last block: a1, b1 = bn_out).
+ * x3 (rows, Hb) bf16, w_up (H, Hb) bf16, h (rows, H) fp32, w_down (Hb, H) bf16; a1, b1 (H) and a2, b2 (Hb) fp32 (the
+ * folded inference BatchNorms).  The same bits as bpc_residual_affine_silu around a bf16 up GEMM and the op's
+ * affine + SiLU down projection.  Buffers 16-byte aligned (a2, b2: 8-byte). */
+BPC_API int bpc_cascade_boundary(const void* x3, const void* w_up, const float* h, float* h_out, float scale_h,
+                                 float scale_u, const float* a1, const float* b1, const void* w_down, const float* a2,
+                                 const float* b2, void* y, int64_t rows, int32_t H, int32_t Hb, bpc_stream_t stream);
+
 /* One memory-bound pass over a (rows, H) fp32 residual stream of the Cascade bottleneck block (no reference
  * counterpart as one call; it replaces the casts, scale, add and activation torch runs between the reference Block's
  * up projection and the next block's first BatchNorm, cascade_net.py:236-259):

@@ -9,6 +9,7 @@ around an fp32 residual), 1e-4 for training mode in fp32.  The whole network's l
 of the largest shot-to-shot deviation for the logits less their mean over shots (the bf16 read-out GEMMs add their
 roundings to the blocks'), and neither above the same statistic of the reference's own bf16 autocast run against
 its fp32 run."""
+import math
 import os
 import time
 from types import SimpleNamespace
@@ -184,3 +185,72 @@ def test_cascade_net_training_step_under_autocast(c14, cascade_net_z):
     for n, p in net.named_parameters():
         assert p.grad is not None and bool(torch.isfinite(p.grad).all()), n
     assert float(net.scatter.grad.abs().max()) > 0 and float(net.blocks[0].conv.w_c2d[0].grad.abs().max()) > 0
+
+
+def boundary_case(rows, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    r = lambda *s: torch.randn(*s, device="cuda", generator=g)
+    x3 = r(rows, 128).bfloat16()
+    w_up = (r(512, 128) / 11.3).bfloat16()
+    w_down = (r(128, 512) / 22.6).bfloat16()
+    h = r(rows, 512)
+    a1, b1 = 0.5 + r(512).abs(), 0.1 * r(512)
+    a2, b2 = 0.5 + r(128).abs(), 0.1 * r(128)
+    return x3, w_up, w_down, h, a1, b1, a2, b2
+
+
+@pytest.mark.parametrize("rows", [1512, 4096 * 3 + 77])
+def test_cascade_boundary_matches_the_unfused_launches(rows):
+    """bpc_cascade_boundary against the launches it replaces: the bf16 up GEMM (cuBLAS), the residual + BN1 + SiLU
+    pass and the op's down projection with the BN2 + SiLU epilogue.  The same operations in the same order: h' and x2
+    equal bit for bit wherever the two up GEMMs round u alike (all elements in practice; the bar allows one bf16 step
+    of u in h' and the resulting step in x2).  Ragged row counts (partial last tile), in-place h, and the last-block
+    mode that writes x1 instead of running the down projection."""
+    from codecoder_b200.ops import cascade_boundary, gmm_ex, residual_affine_silu
+    x3, w_up, w_down, h, a1, b1, a2, b2 = boundary_case(rows, rows)
+    sh, su = 1 / math.sqrt(28), 1.0
+    u = torch.matmul(x3, w_up.t())
+    h_ref, x1_ref = residual_affine_silu(h, u, sh, su, a1, b1)
+    ident = torch.zeros(1, 1, dtype=torch.int32, device="cuda")
+    x2_ref = gmm_ex(x1_ref.view(rows, 1, 512), ident, w_down, scale=a2, shift=b2).view(rows, 128)
+    h_new, x2 = cascade_boundary(x3, w_up, h, sh, su, a1, b1, w_down, a2, b2)
+    torch.cuda.synchronize()
+    dh = (h_new - h_ref).abs()
+    assert bool((dh <= su * u.float().abs() * 2 ** -7 + 1e-6).all())
+    exact_h = float((dh == 0).float().mean())
+    dx = (x2.float() - x2_ref.float()).abs()
+    exact_x = float((dx == 0).float().mean())
+    print("boundary rows=%d: h' exact %.6f, x2 exact %.6f" % (rows, exact_h, exact_x))
+    assert exact_h > 0.999 and exact_x > 0.99
+    assert rel(x2, x2_ref) < 2e-2
+    # in place, and the last-block mode (x1 out, no down projection)
+    h2 = h.clone()
+    out, x1 = cascade_boundary(x3, w_up, h2, sh, su, a1, b1, h_out=h2)
+    torch.cuda.synchronize()
+    assert out.data_ptr() == h2.data_ptr()
+    assert torch.equal(h2, h_new)
+    assert x1.shape == (rows, 512) and float(((x1.float() - x1_ref.float()).abs() > 0).float().mean()) < 1e-3
+    # h' only
+    out, none = cascade_boundary(x3, w_up, h, sh, su, want_y=False)
+    torch.cuda.synchronize()
+    assert none is None and torch.equal(out, h_new)
+
+
+def test_cascade_stack_of_one_block_matches_reference_c14(c14):
+    """The stack path (one launch per block boundary) on the reference Block's C14 block-0 fixture: the same bar as
+    the block-by-block path."""
+    conv_z, z = c14
+    blk = CascadeBlock(int(z["H"]), bb72_geo(conv_z), int(z["L"]), res=str(z["res"]))
+    load_block(blk, conv_z, z)
+    stack = CascadeStack([blk]).cuda().eval()
+    h = torch.as_tensor(bf16_to_f32(z["h_bf16"])).cuda()
+    h_in = h.clone()
+    with torch.no_grad():
+        out = stack(h)
+    torch.cuda.synchronize()
+    assert torch.equal(h, h_in)                     # the caller's stream is not written
+    err = rel(out, z["out"])
+    print("C14 block-0 through the boundary kernel vs the reference Block: rel err %.2e" % err)
+    assert err < 2e-2
+    with torch.no_grad():
+        assert rel(out, blk(h)) < 1e-5
