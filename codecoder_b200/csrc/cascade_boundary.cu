@@ -110,7 +110,9 @@ __global__ void __launch_bounds__(kBThreads, 1)
                             const __grid_constant__ CUtensorMap tmHo, const __grid_constant__ CUtensorMap tmY,
                             const BoundaryArgs a) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-byte aligned by offsetting within the shared array (so the compiler keeps these accesses in the shared
+  // space and knows they do not alias the global BatchNorm vectors)
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const uint32_t sb = smem_u32(smem);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
