@@ -494,6 +494,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int kCi = 64 * (NKB - 1) + 16 * KLAST;
   constexpr bool kLoadY = EPI == kEpiGeluResid || EPI == kEpiAdd;     // the epilogue reads y before writing it
   constexpr bool kGelu = EPI == kEpiGeluInit || EPI == kEpiGeluResid;
+  constexpr bool kAffine = EPI == kEpiAffineSilu;                    // SiLU(scale acc + shift) per output channel
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* scratch = smem + kWideStages * kWideStageBytes;
@@ -768,6 +769,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int e4 = 0; e4 < 4; ++e4) {
               uint64_t xx = f2_pack(x[8 * g + 2 * e4], x[8 * g + 2 * e4 + 1]);
               if (kGelu) xx = gelu_tanh_fast2(xx);
+              if (kAffine) {
+                const int colp = 32 * q + 16 * h + 8 * g + 2 * e4;
+                xx = silu_tanh_fast2(f2_fma(xx, *reinterpret_cast<const uint64_t*>(a.epi_scale + colp),
+                                            *reinterpret_cast<const uint64_t*>(a.epi_shift + colp)));
+              }
               if (kLoadY) xx = f2_add(xx, bf2_to_f2(hr[e4]));
               o[e4] = f2_to_bf2(xx);
             }
@@ -911,6 +917,7 @@ const void* wide_kernel_for(bool blocked, int epi, bool head, int Ci) {
   if (head) return nullptr;
   if (epi == kEpiStore) return wide_for_ci<false, kEpiStore, false>(Ci);
   if (epi == kEpiAdd) return wide_for_ci<false, kEpiAdd, false>(Ci);
+  if (epi == kEpiAffineSilu) return wide_for_ci<false, kEpiAffineSilu, false>(Ci);
   return nullptr;
 }
 
@@ -1061,10 +1068,11 @@ int gmm_tc_launch(const GmmProblem& p, const GmmMaps& maps, int* status, uint64_
   a.tmem_cols = cols;
   const bool head = p.head.head_w != nullptr;
   // wide tiles: C_out in {64, 96, 128} and C_in <= 128; blocked layout (C_in = C_out) with the GELU epilogues and
-  // the head, row layouts with contiguous channels and the store / add epilogues
+  // the head, row layouts with contiguous channels and the store / add / affine + SiLU epilogues
   const bool wide_shape = p.Co >= 64 && p.Co <= kWideM && p.Co % 32 == 0 && (p.Ci == 64 || p.Ci == 96 || p.Ci == 128);
   const bool wide_blocked = p.blocked && p.Ci == p.Co && (p.epi == kEpiGeluInit || p.epi == kEpiGeluResid);
-  const bool wide_rows = !p.blocked && !head && p.y_cg_stride == 8 && (p.epi == kEpiStore || p.epi == kEpiAdd);
+  const bool wide_rows = !p.blocked && !head && p.y_cg_stride == 8 &&
+                         (p.epi == kEpiStore || p.epi == kEpiAdd || p.epi == kEpiAffineSilu);
   if (wide_shape && (wide_blocked || wide_rows)) {
     const void* wf = wide_kernel_for(p.blocked, p.epi, head, p.Ci);
     if (!wf) return fail(2, "unsupported wide-tile configuration");

@@ -163,3 +163,27 @@ def test_gather_mm_dropin_signature():
     assert y32.dtype == torch.float32 and rel_err(y32.cpu().numpy(), ref) < 1e-4
     assert y16.dtype == torch.bfloat16 and rel_err(y16.float().cpu().numpy(), ref) < 2e-2
     assert torch.ops.cascade.gmm(x, idx.to(torch.int32), w, False).shape == (4, g.N_d, 64)
+
+
+@pytest.mark.parametrize("C,B", [(128, 300), (64, 257), (96, 130)])
+def test_affine_silu_epilogue_two_weight_sets(C, B):
+    """The op with two weight sets and the affine + SiLU epilogue (the Cascade block's data -> check convolution with
+    its BN3 + SiLU, bpc_gather_mm_fwd_ex): y = SiLU(scale * op(x) + shift), checked against an fp32 restatement on
+    the rotated-surface d = 9 graph; ragged batches (partial shot tiles).  Tolerance 2e-2 of max |ref|:
+    the bf16 output rounding plus the hardware-tanh SiLU."""
+    from codecoder_b200.ops import gmm_ex
+    g = RotatedSurface(9, 9)
+    gen = torch.Generator(device=DEV).manual_seed(C + B)
+    x = torch.randn(B, g.N_d, C, device=DEV, generator=gen).bfloat16()
+    w = (torch.randn(2, C, g.K * C, device=DEV, generator=gen) / (g.K * C) ** 0.5).bfloat16()
+    scale = 0.5 + torch.rand(C, device=DEV, generator=gen)
+    shift = 0.2 * torch.randn(C, device=DEV, generator=gen)
+    idx = torch.as_tensor(g.d2c_all, dtype=torch.int32, device=DEV)
+    split = g.T * g.nh
+    y = gmm_ex(x, idx, w, type_split=split, scale=scale, shift=shift)
+    torch.cuda.synchronize()
+    xp = torch.cat([x.float(), torch.zeros(B, 1, C, device=DEV)], 1)
+    gat = xp[:, idx.long()].reshape(B, idx.shape[0], g.K * C)
+    ref = torch.cat([gat[:, :split] @ w[0].float().t(), gat[:, split:] @ w[1].float().t()], 1)
+    ref = torch.nn.functional.silu(ref * scale + shift)
+    assert rel_err(y.float().cpu().numpy(), ref.cpu().numpy()) < 2e-2
