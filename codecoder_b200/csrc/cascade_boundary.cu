@@ -25,7 +25,8 @@
 //   warps 2-9   the middle stage, two warps per TMEM lane quarter (one row per thread, one 32-channel half of every
 //               64-channel chunk per warp): h arrives by TMA in 128-row x 32-channel fp32 boxes (128-byte swizzle,
 //               three chunks in flight), u comes from TMEM, h' goes back into the same box, x1 goes into the swizzled
-//               K-major operand of the down MMA (after the last block: a box for the TMA store); one barrier per chunk
+//               K-major operand of the down MMA (after the last block: a box for the TMA store); each warp signals
+//               its part of a chunk on mbarriers (no CTA barrier), so the warps run ahead of one another
 //   warps 10-13 the down epilogue: TMEM -> BN2 + SiLU -> bf16 rows of x2
 //   warp 14     the stores and the h loads: once the middle stage has finished a chunk it stores h' (and x1 after the
 //               last block) by TMA and, once the stores have read the boxes, refills the slot with the chunk three ahead
@@ -48,7 +49,6 @@ constexpr int kBB = 128;                // bottleneck channels
 constexpr int kBRows = 128;             // rows per tile (MMA M)
 constexpr int kBThreads = 480;
 constexpr int kMidWarp0 = 2, kMidWarps = 8, kEpiWarp0 = 10, kStoreWarp = 14;
-constexpr int kMidThreads = kMidWarps * 32;
 constexpr int kHSlots = 3;              // h chunks in flight
 constexpr uint32_t kBox = kBRows * 128;                 // one 128-row box of 128-byte rows: 16 KB
 constexpr uint32_t kOffX3 = 0;                          // 2 boxes: the tile's 128 channels of x3
@@ -66,7 +66,7 @@ enum : int {
   kDdF = 19, kDdE = 21, kDrain = 23, kDone = 24, kNumBars = 27
 };
 // kX1E: the x1 slot is free again -- after the down MMAs read it, or (last block) after its store read it
-// kDone: the middle stage has finished the chunk in an h slot (h' and x1 written)
+// kDone: the middle stage has finished the chunk in an h slot (h' and x1 written; one arrival per middle warp)
 
 struct BoundaryArgs {
   float scale_h, scale_u;
@@ -83,19 +83,6 @@ struct BoundaryArgs {
   uint64_t timeout_ns;
 };
 
-__device__ __forceinline__ void named_sync(int id, int count) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-// Barrier among `count` threads that also ANDs a predicate over them.
-__device__ __forceinline__ bool named_sync_and(int id, int count, bool pred) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, %2, %3, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(r)
-      : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(count)
-      : "memory");
-  return r != 0;
-}
 // Bounded wait used while leaving: every copy or MMA this thread issued signals its barrier; give up after the limit.
 __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, uint64_t limit) {
   const uint64_t t0 = globaltimer_ns();
@@ -125,7 +112,8 @@ __global__ void __launch_bounds__(kBThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < kNumBars; ++i) {
       uint32_t count = 1;
-      if (i == kDuE || i == kDuE + 1) count = kMidWarps;
+      if (i == kDuE || i == kDuE + 1 || i >= kDone) count = kMidWarps;
+      if (DOWN && (i == kX1F || i == kX1F + 1)) count = kMidWarps;
       if (i == kDdE || i == kDdE + 1) count = 4;
       mbar_init(bar(i), count);
     }
@@ -256,7 +244,6 @@ __global__ void __launch_bounds__(kBThreads, 1)
     const int half = (warp - kMidWarp0) >> 2;
     const int m = quarter * 32 + lane;                         // row of the tile = TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-    const bool elected = warp == kMidWarp0 && lane == 0;
     const bool x1_out = DOWN || a.store_x1;
     const uint64_t sh2 = f2_pack(a.scale_h, a.scale_h), su2 = f2_pack(a.scale_u, a.scale_u);
     bool ok = true;
@@ -265,11 +252,16 @@ __global__ void __launch_bounds__(kBThreads, 1)
         const int gq = 4 * i + q, b = gq & 1;
         for (int c = 0; c < 2; ++c) {
           const int kc = 2 * q + c, g = 8 * i + kc, hs = g % kHSlots, s = g & 1;
+          // every wait is decided for the whole warp, so no lane is left behind in a warp-collective instruction
           bool good = true;
           if (c == 0) good = mbar_wait(bar(kDuF + b), (gq >> 1) & 1, abort_flag, a.status, a.timeout_ns);
           good = good && mbar_wait(bar(kHF + hs), (g / kHSlots) & 1, abort_flag, a.status, a.timeout_ns);
           if (x1_out) good = good && mbar_wait(bar(kX1E + s), ((g >> 1) & 1) ^ 1, abort_flag, a.status, a.timeout_ns);
-          if (good) {
+          if (!__all_sync(0xffffffffu, good)) {
+            ok = false;
+            break;
+          }
+          {
             tc_fence_after();
             float acc[32];
             tmem_ld32(tbase + lane_base + static_cast<uint32_t>(b * kBB + c * 64 + half * 32), acc);
@@ -305,17 +297,11 @@ __global__ void __launch_bounds__(kBThreads, 1)
             fence_proxy_async_smem();                   // the TMA stores and the MMAs read what was written here
           }
           if (c == 1) tc_fence_before();                // the quarter's accumulator reads are done
-          if (!named_sync_and(1, kMidThreads, good)) {
-            ok = false;
-            break;
-          }
-          if (c == 1) {
-            __syncwarp();
-            if (lane == 0) mbar_arrive(bar(kDuE + b));
-          }
-          if (elected) {
+          __syncwarp();
+          if (lane == 0) {                              // this warp's rows of the chunk are written
             if (DOWN) mbar_arrive(bar(kX1F + s));
             mbar_arrive(bar(kDone + hs));
+            if (c == 1) mbar_arrive(bar(kDuE + b));
           }
         }
       }
