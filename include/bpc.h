@@ -85,7 +85,8 @@ BPC_API int bpc_cascade_boundary(const void* x3, const void* w_up, const float* 
  * counterpart as one call; it replaces the casts, scale, add and activation torch runs between the reference Block's
  * up projection and the next block's first BatchNorm, cascade_net.py:236-259):
  *   v = scale_h h + scale_u u (u bf16 (rows, H), may be NULL);  out = v (fp32, may be NULL);
- *   x = SiLU(a[c] v + b[c]) (bf16, may be NULL; a, b fp32 (H,): an inference BatchNorm folded to scale and shift).
+ *   x = SiLU(a[c] v + b[c]) (bf16, may be NULL; a, b fp32 (H,): an inference BatchNorm folded to scale and shift;
+ *   SiLU as x/2 + x/2 tanh(x/2) on the hardware tanh, its result rounded to bf16).
  * H % 8 == 0; every pointer 16-byte aligned. */
 BPC_API int bpc_residual_affine_silu(const float* h, const void* u, float* out, void* x, int64_t rows, int32_t H,
                                      float scale_h, float scale_u, const float* a, const float* b, bpc_stream_t stream);
