@@ -230,8 +230,9 @@ def measure_config(name, shots, steps, warmup, dev, pk, cpu_seconds):
     achieved = sum(step_flops) / (tc_ms / 1000.0) / 1e12
     f32 = cfg.dtype == "f32"
     if f32:
+        narrow = cfg.channels in (8, 16, 32)        # equal widths <= 32: the resident-weight CUDA-core kernel
         peak, peak_kind, kernel, bound = FP32_FMA_PEAK_TFLOPS, "nominal FP32 FMA (148 SMs x 128 FMA/clk x 2 x 1965 MHz)", \
-            "gmm_fma_kernel<float>", "fma"
+            (f"gmm_fma_narrow_kernel<float, {cfg.channels}>" if narrow else "gmm_fma_kernel<float>"), "fma"
     else:
         peak, peak_kind, kernel, bound = pk["bf16_tflops_sustained"], f"{pk['source']} sustained bf16 (cuBLAS)", \
             "gmm_wide_kernel", "tensor"
@@ -334,9 +335,9 @@ def measure_cascade_net(tables_npz, dev, pk, shots=4096, steps=5, warmup=3):
             / pk["bf16_tflops_sustained"],
             "kernels": "stem (torch gather + embedding); first block's BN1 + SiLU (residual_affine_silu_kernel) and "
                        "down + BN2 + SiLU (gmm_tc_kernel); per block: the two-type conv (gmm_wide_kernel check -> data, "
-                       "gmm_tc_kernel data -> check + BN3 + SiLU) and cascade_boundary_kernel (up, residual, the next "
-                       "block's BN1 + SiLU + down + BN2 + SiLU, or bn_out + SiLU after the last); read-out: cuBLAS "
-                       "bf16 GEMMs (pooling, scatter)"}
+                       "gmm_wide_kernel data -> check + BN3 + SiLU) and cascade_boundary_kernel (up, residual, the "
+                       "next block's BN1 + SiLU + down + BN2 + SiLU, or bn_out + SiLU after the last); read-out: "
+                       "cuBLAS bf16 GEMMs (pooling, scatter)"}
 
 
 def run_reference(args, cfg, g, params, rank, world):
@@ -594,7 +595,8 @@ def main():
     configs = None
     if rank == 0 and world == 1 and not args.no_configs:
         # the d = 5 fp32 (CUDA-core) and d = 9 bf16 workloads at their stated batches
-        configs = {"d5_fp32": measure_config("d5_fp32", 1024, max(args.steps, 5), max(args.warmup, 3), dev, pk, 4.0),
+        # the d = 5 step is ~1.5 ms: time 20 of them so that clock ramps and launch jitter average out
+        configs = {"d5_fp32": measure_config("d5_fp32", 1024, max(args.steps, 20), max(args.warmup, 3), dev, pk, 4.0),
                    "d9_bf16": measure_config("d9_bf16", 65536, max(args.steps, 5), max(args.warmup, 3), dev, pk, 6.0)}
 
     train = None
