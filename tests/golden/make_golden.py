@@ -288,6 +288,32 @@ def make_cascade_net():
     print("cascade_net_bb72", det.shape, logits.shape, float(logits.abs().mean()), float(logits.std(0).mean()))
 
 
+def make_cascade_net_h512():
+    """The reference's CascadeBB at C14's width (H = 512, the 128-channel bottleneck; L = 2 blocks, res = 'skip') on
+    the BB72 graph with the synthetic layout, every weight drawn by tests/cascade_weights.cascade_state (seed 512, so
+    the test rebuilds them instead of the fixture storing ~9 M parameters); fp32 and CPU bf16 autocast logits of 16
+    seeded shots at detector density 0.25."""
+    sys.path.insert(0, os.path.dirname(HERE))
+    from cascade_weights import cascade_state
+    geo = cn.Geometry("bb72")
+    rng = np.random.default_rng(512)
+    det_t, det_typ, det_site, logicals = synthetic_bb72_layout(geo, rng)
+    m = cn.CascadeBB("bb72", 512, 2, det_t, det_typ, det_site, logicals, res="skip", conv_impl="torch")
+    state = cascade_state({k: tuple(v.shape) for k, v in m.state_dict().items()}, 512)
+    m.load_state_dict({k: torch.as_tensor(v) for k, v in state.items()})
+    m.eval()
+    det = (rng.random((16, len(det_t))) < 0.25).astype(np.uint8)
+    with torch.no_grad():
+        logits = m(torch.as_tensor(det))
+        with torch.autocast("cpu", dtype=torch.bfloat16):
+            logits_ac = m(torch.as_tensor(det)).float()
+    np.savez_compressed(os.path.join(HERE, "cascade_net_bb72_h512.npz"), det=det, logits=logits.numpy(),
+                        logits_autocast=logits_ac.numpy(), det_t=det_t, det_typ=det_typ, det_site=det_site,
+                        logicals=logicals, H=512, L=2, res="skip", seed=512, T=geo.T, n2=geo.n2, N=geo.N)
+    print("cascade_net_bb72_h512", det.shape, logits.shape, float(logits.abs().mean()), float(logits.std(0).mean()),
+          float((logits_ac - logits).abs().max() / logits.abs().max()))
+
+
 if __name__ == "__main__":
     torch.manual_seed(0)
     if len(sys.argv) > 1:
@@ -300,3 +326,4 @@ if __name__ == "__main__":
     make_backward()
     make_cascade_block()
     make_cascade_net()
+    make_cascade_net_h512()

@@ -77,3 +77,24 @@ def test_cascade_net_pooled_readout_matches_the_paper_form(fixtures):
         got = net.readout(torch.as_tensor(h, dtype=torch.float32)).double().numpy()
     ref = readout_paper(net, h, [z["c2d0"], z["c2d1"]], int(z["T"]), int(z["n2"]))
     assert np.max(np.abs(got - ref)) / np.max(np.abs(ref)) < 1e-5
+
+
+def test_seeded_weights_fit_cascade_net_at_c14_width(golden_dir, fixtures):
+    """The H = 512 fixture's network is rebuilt from seeded weights (tests/cascade_weights.py): they load strictly
+    into CascadeNet and are the same on every call."""
+    from cascade_weights import cascade_state
+    _, conv_z = fixtures
+    z = dict(np.load(os.path.join(golden_dir, "cascade_net_bb72_h512.npz")))
+    net = CascadeNet(net_geo_h512(z, conv_z), int(z["H"]), int(z["L"]), z["det_t"], z["det_typ"], z["det_site"],
+                     z["logicals"], res=str(z["res"]))
+    shapes = {k: tuple(v.shape) for k, v in net.state_dict().items()}
+    a, b = cascade_state(shapes, int(z["seed"])), cascade_state(shapes, int(z["seed"]))
+    net.load_state_dict({k: torch.as_tensor(v) for k, v in a.items()}, strict=True)
+    assert all(np.array_equal(a[k], b[k]) for k in a)
+
+
+def net_geo_h512(z, conv_z):
+    return SimpleNamespace(T=int(z["T"]), n2=int(z["n2"]), N=int(z["N"]), c2d=[conv_z["c2d0"], conv_z["c2d1"]],
+                           d2c=[conv_z["d2c0"], conv_z["d2c1"]],
+                           inv_c2d=[conv_z["inv_c2d0"].astype(np.int64), conv_z["inv_c2d1"].astype(np.int64)],
+                           inv_d2c=[conv_z["inv_d2c0"].astype(np.int64), conv_z["inv_d2c1"].astype(np.int64)])

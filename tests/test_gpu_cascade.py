@@ -254,3 +254,30 @@ def test_cascade_stack_of_one_block_matches_reference_c14(c14):
     assert err < 2e-2
     with torch.no_grad():
         assert rel(out, blk(h)) < 1e-5
+
+
+def test_cascade_net_c14_width_matches_reference(golden_dir, c14):
+    """The whole network at C14's width (H = 512, 128-channel bottleneck, 2 blocks) through the block-boundary
+    kernel and the wide-tile convolutions, against the reference's own CascadeBB (fp32 CPU) with the same seeded
+    weights (tests/cascade_weights.py rebuilds them).  Bars: 2e-2 of max |ref| and 5e-2 of the largest shot-to-shot
+    deviation, and each at most twice the same statistic of the reference's own bf16 autocast run."""
+    from cascade_weights import cascade_state
+    conv_z, _ = c14
+    z = dict(np.load(os.path.join(golden_dir, "cascade_net_bb72_h512.npz")))
+    geo = bb72_geo(conv_z)
+    geo.T, geo.n2, geo.N = int(z["T"]), int(z["n2"]), int(z["N"])
+    net = CascadeNet(geo, int(z["H"]), int(z["L"]), z["det_t"], z["det_typ"], z["det_site"], z["logicals"],
+                     res=str(z["res"]))
+    state = cascade_state({k: tuple(v.shape) for k, v in net.state_dict().items()}, int(z["seed"]))
+    net.load_state_dict({k: torch.as_tensor(v) for k, v in state.items()})
+    net = net.cuda().eval()
+    with torch.no_grad():
+        out = net(torch.as_tensor(z["det"]).cuda())
+    torch.cuda.synchronize()
+    ref, ra = z["logits"], z["logits_autocast"]
+    err, dev = rel(out, ref), rel(out - out.mean(0), ref - ref.mean(0))
+    err_ref, dev_ref = rel(ra, ref), rel(ra - ra.mean(0), ref - ref.mean(0))
+    print("CascadeNet (H=512, L=2, bb72) vs the reference: rel err %.2e, of the shot deviations %.2e "
+          "(the reference's own bf16 run: %.2e, %.2e)" % (err, dev, err_ref, dev_ref))
+    assert err < 2e-2 and dev < 5e-2
+    assert err <= 2 * err_ref and dev <= 2 * dev_ref
