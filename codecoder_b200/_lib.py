@@ -38,6 +38,10 @@ SIGNATURES = {
     "bpc_route_workspace_size": (ctypes.c_size_t, [c_i64]),
     "bpc_cascade_boundary": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, ctypes.c_float, ctypes.c_float, c_vp, c_vp, c_vp,
                                             c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_vp]),
+    "bpc_cascade_boundary_tokens": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i32, c_i32, c_vp,
+                                                   ctypes.c_float, ctypes.c_float, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
+                                                   c_i64, c_i32, c_i32, c_vp]),
+    "bpc_cascade_stem": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_i32, c_i32, c_vp, c_vp, c_vp, c_i64, c_i32, c_vp]),
     "bpc_residual_affine_silu": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, ctypes.c_float, ctypes.c_float,
                                                 c_vp, c_vp, c_vp]),
     "bpc_gelu_residual_fwd": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_i32, c_i32, c_vp]),

@@ -79,9 +79,26 @@ struct BoundaryArgs {
   int num_tiles;
   int store_h;                  // write h' (through the h_out map)
   int store_x1;                 // x1 mode: write x1 (through the y map)
+  // token mode (the first block of a network): h is the embedding of each row's detector token, h[row] =
+  // E[tbase[node] + det[shot, gidx[node]]] (gidx = D: no detector), row = shot N + node; no h is read from memory
+  int tokens;
+  const uint8_t* det;           // (B, D)
+  const int32_t* gidx;          // (N)
+  const int32_t* tbase;         // (N)
+  const float* E;               // (5, 512)
+  int D, N;
   int* status;
   uint64_t timeout_ns;
 };
+
+// Token of a row of the network's stream (token mode); rows past the batch take the absent token.
+__device__ __forceinline__ int row_token(const BoundaryArgs& a, int64_t row) {
+  if (row >= a.rows) return 4;
+  const int64_t shot = row / a.N;
+  const int node = static_cast<int>(row - shot * a.N);
+  const int g = __ldg(a.gidx + node);
+  return __ldg(a.tbase + node) + (g < a.D ? (__ldg(a.det + shot * a.D + g) & 1) : 0);
+}
 
 // Bounded wait used while leaving: every copy or MMA this thread issued signals its barrier; give up after the limit.
 __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, uint64_t limit) {
@@ -248,6 +265,9 @@ __global__ void __launch_bounds__(kBThreads, 1)
     const uint64_t sh2 = f2_pack(a.scale_h, a.scale_h), su2 = f2_pack(a.scale_u, a.scale_u);
     bool ok = true;
     for (int i = 0; i < nt && ok; ++i) {
+      const float* erow = a.tokens ? a.E + static_cast<int64_t>(row_token(
+                                             a, static_cast<int64_t>(blockIdx.x + i * gridDim.x) * kBRows + m)) * kBH
+                                   : nullptr;
       for (int q = 0; q < 4 && ok; ++q) {
         const int gq = 4 * i + q, b = gq & 1;
         for (int c = 0; c < 2; ++c) {
@@ -271,7 +291,7 @@ __global__ void __launch_bounds__(kBThreads, 1)
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
               float4* p = reinterpret_cast<float4*>(hrow + ((j ^ (m & 7)) << 4));
-              const float4 hv = *p;
+              const float4 hv = erow ? __ldg(reinterpret_cast<const float4*>(erow + ch0) + j) : *p;
               // u = bf16(acc); v = fmaf(scale_u, u, scale_h h), as packed pairs
               const uint64_t u0 = bf2_to_f2(f2_to_bf2(f2_pack(acc[4 * j], acc[4 * j + 1])));
               const uint64_t u1 = bf2_to_f2(f2_to_bf2(f2_pack(acc[4 * j + 2], acc[4 * j + 3])));
@@ -315,6 +335,10 @@ __global__ void __launch_bounds__(kBThreads, 1)
       auto h_load = [&](int g) {
         const int tile = static_cast<int>(blockIdx.x) + (g >> 3) * static_cast<int>(gridDim.x), kc = g & 7,
                   slot = g % kHSlots;
+        if (a.tokens) {                                 // nothing to load: the slot is free for the middle stage
+          mbar_arrive(bar(kHF + slot));
+          return;
+        }
         mbar_arrive_expect_tx(bar(kHF + slot), 2 * kBox);
         for (int bx = 0; bx < 2; ++bx)
           tma_load_2d(sb + kOffH + (slot * 2 + bx) * kBox, &tmH, kc * 64 + 32 * bx, tile * kBRows, bar(kHF + slot));
@@ -401,29 +425,42 @@ int encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64
 
 using namespace bpc;
 
-extern "C" int bpc_cascade_boundary(const void* x3, const void* w_up, const float* h, float* h_out, float scale_h,
-                                    float scale_u, const float* a1, const float* b1, const void* w_down,
-                                    const float* a2, const float* b2, void* y, int64_t rows, int32_t H, int32_t Hb,
-                                    bpc_stream_t stream) {
+namespace bpc {
+namespace {
+
+struct TokenSource {
+  const uint8_t* det = nullptr;
+  const int32_t* gidx = nullptr;
+  const int32_t* tbase = nullptr;
+  const float* E = nullptr;
+  int D = 0, N = 0;
+};
+
+int launch_boundary(const void* x3, const void* w_up, const float* h, const TokenSource* tok, float* h_out,
+                    float scale_h, float scale_u, const float* a1, const float* b1, const void* w_down,
+                    const float* a2, const float* b2, void* y, int64_t rows, int32_t H, int32_t Hb,
+                    bpc_stream_t stream) {
   if (H != kBH || Hb != kBB) return fail(BPC_ERR_ARG, "the block boundary supports H = 512 with a 128-channel bottleneck");
   if (rows < 0 || rows > (static_cast<int64_t>(1) << 30)) return fail(BPC_ERR_ARG, "rows must be in [0, 2^30]");
   const bool down = w_down != nullptr;
   if (down && (!a1 || !b1 || !a2 || !b2 || !y)) return fail(BPC_ERR_ARG, "the down projection needs a1, b1, a2, b2 and y");
   if (!down && y && (!a1 || !b1)) return fail(BPC_ERR_ARG, "x1 needs a1 and b1");
   if (rows == 0) return 0;
-  if (!x3 || !w_up || !h) return fail(BPC_ERR_ARG, "null buffer");
+  if (!x3 || !w_up || (!h && !tok)) return fail(BPC_ERR_ARG, "null buffer");
   const uintptr_t al16 = reinterpret_cast<uintptr_t>(x3) | reinterpret_cast<uintptr_t>(w_up) |
                          reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(h_out) |
                          reinterpret_cast<uintptr_t>(w_down) | reinterpret_cast<uintptr_t>(y) |
-                         reinterpret_cast<uintptr_t>(a1) | reinterpret_cast<uintptr_t>(b1);
+                         reinterpret_cast<uintptr_t>(a1) | reinterpret_cast<uintptr_t>(b1) |
+                         reinterpret_cast<uintptr_t>(tok ? tok->E : nullptr);
   const uintptr_t al8 = reinterpret_cast<uintptr_t>(a2) | reinterpret_cast<uintptr_t>(b2);
   if ((al16 & 15) || (al8 & 7)) return fail(BPC_ERR_ARG, "buffers must be 16-byte aligned (a2, b2: 8-byte)");
 
-  CUtensorMap mX3, mWup, mWdn{}, mH, mHo{}, mY{};
+  CUtensorMap mX3, mWup, mWdn{}, mH{}, mHo{}, mY{};
   const uint64_t R = static_cast<uint64_t>(rows);
   if (int e = encode_2d(&mX3, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x3, kBB, R, kBB * 2, 64, "x3")) return e;
   if (int e = encode_2d(&mWup, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, w_up, kBB, kBH, kBB * 2, 64, "w_up")) return e;
-  if (int e = encode_2d(&mH, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, h, kBH, R, kBH * 4, 32, "h")) return e;
+  if (!tok)
+    if (int e = encode_2d(&mH, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, h, kBH, R, kBH * 4, 32, "h")) return e;
   if (h_out)
     if (int e = encode_2d(&mHo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, h_out, kBH, R, kBH * 4, 32, "h_out")) return e;
   if (down) {
@@ -431,7 +468,7 @@ extern "C" int bpc_cascade_boundary(const void* x3, const void* w_up, const floa
   } else if (y) {
     if (int e = encode_2d(&mY, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, y, kBH, R, kBH * 2, 64, "x1")) return e;
   }
-  BoundaryArgs a;
+  BoundaryArgs a{};
   a.scale_h = scale_h;
   a.scale_u = scale_u;
   a.a1 = a1;
@@ -443,6 +480,15 @@ extern "C" int bpc_cascade_boundary(const void* x3, const void* w_up, const floa
   a.num_tiles = static_cast<int>((rows + kBRows - 1) / kBRows);
   a.store_h = h_out != nullptr;
   a.store_x1 = !down && y != nullptr;
+  if (tok) {
+    a.tokens = 1;
+    a.det = tok->det;
+    a.gidx = tok->gidx;
+    a.tbase = tok->tbase;
+    a.E = tok->E;
+    a.D = tok->D;
+    a.N = tok->N;
+  }
   a.status = op_status_ptr();
   a.timeout_ns = 2000000000ull;
   const void* fn = down ? reinterpret_cast<const void*>(&cascade_boundary_kernel<true>)
@@ -453,5 +499,82 @@ extern "C" int bpc_cascade_boundary(const void* x3, const void* w_up, const floa
   cudaError_t le = cudaLaunchKernel(fn, dim3(static_cast<unsigned>(grid)), dim3(kBThreads), args, kSmemBytes,
                                     reinterpret_cast<cudaStream_t>(stream));
   if (le != cudaSuccess) return fail(BPC_ERR_LAUNCH, std::string("cascade_boundary_kernel launch: ") + cudaGetErrorString(le));
+  return 0;
+}
+
+// The network's stem and the first block's BN1 + SiLU in one pass, 8 channels per thread:
+// x1[shot, node, c] = bf16(SiLU(a1[c] E[token, c] + b1[c])), token = tbase[node] + det[shot, gidx[node]] (gidx = D: none)
+__global__ void __launch_bounds__(256) cascade_stem_kernel(const uint8_t* __restrict__ det,
+                                                           const int32_t* __restrict__ gidx,
+                                                           const int32_t* __restrict__ tbase,
+                                                           const float* __restrict__ E, const float* __restrict__ a,
+                                                           const float* __restrict__ b, __nv_bfloat16* __restrict__ x,
+                                                           int64_t groups, int D, int N, int H8) {
+  for (int64_t gi = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; gi < groups;
+       gi += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = gi / H8;
+    const int c0 = static_cast<int>(gi - row * H8) * 8;
+    const int64_t shot = row / N;
+    const int node = static_cast<int>(row - shot * N);
+    const int g = __ldg(gidx + node);
+    const int tok = __ldg(tbase + node) + (g < D ? (__ldg(det + shot * D + g) & 1) : 0);
+    const float* e = E + static_cast<int64_t>(tok) * (8 * H8) + c0;
+    uint4 o;
+    uint32_t* op = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      // v = 1 * h, as the residual pass computes it; SiLU on the hardware tanh, rounded to bf16
+      const uint64_t v = f2_mul(f2_pack(__ldg(e + 2 * k), __ldg(e + 2 * k + 1)), f2_pack(1.f, 1.f));
+      const uint64_t av = f2_pack(__ldg(a + c0 + 2 * k), __ldg(a + c0 + 2 * k + 1));
+      const uint64_t bv = f2_pack(__ldg(b + c0 + 2 * k), __ldg(b + c0 + 2 * k + 1));
+      op[k] = f2_to_bf2(silu_tanh_fast2(f2_fma(av, v, bv)));
+    }
+    reinterpret_cast<uint4*>(x)[gi] = o;
+  }
+}
+
+}  // namespace
+}  // namespace bpc
+
+extern "C" int bpc_cascade_boundary(const void* x3, const void* w_up, const float* h, float* h_out, float scale_h,
+                                    float scale_u, const float* a1, const float* b1, const void* w_down,
+                                    const float* a2, const float* b2, void* y, int64_t rows, int32_t H, int32_t Hb,
+                                    bpc_stream_t stream) {
+  return launch_boundary(x3, w_up, h, nullptr, h_out, scale_h, scale_u, a1, b1, w_down, a2, b2, y, rows, H, Hb,
+                         stream);
+}
+
+extern "C" int bpc_cascade_boundary_tokens(const void* x3, const void* w_up, const uint8_t* det, const int32_t* gidx,
+                                           const int32_t* tbase, const float* E, int32_t D, int32_t N, float* h_out,
+                                           float scale_h, float scale_u, const float* a1, const float* b1,
+                                           const void* w_down, const float* a2, const float* b2, void* y, int64_t B,
+                                           int32_t H, int32_t Hb, bpc_stream_t stream) {
+  if (B < 0 || D < 0 || N < 1) return fail(BPC_ERR_ARG, "B >= 0, D >= 0, N >= 1");
+  if (B > 0 && (!det && D > 0)) return fail(BPC_ERR_ARG, "null det");
+  if (B > 0 && (!gidx || !tbase || !E)) return fail(BPC_ERR_ARG, "null token tables");
+  TokenSource t;
+  t.det = det;
+  t.gidx = gidx;
+  t.tbase = tbase;
+  t.E = E;
+  t.D = D;
+  t.N = N;
+  return launch_boundary(x3, w_up, nullptr, &t, h_out, scale_h, scale_u, a1, b1, w_down, a2, b2, y, B * N, H, Hb,
+                         stream);
+}
+
+extern "C" int bpc_cascade_stem(const uint8_t* det, const int32_t* gidx, const int32_t* tbase, const float* E,
+                                int32_t D, int32_t N, const float* a1, const float* b1, void* x1, int64_t B, int32_t H,
+                                bpc_stream_t stream) {
+  if (B < 0 || D < 0 || N < 1 || H < 8 || H % 8) return fail(BPC_ERR_ARG, "B >= 0, D >= 0, N >= 1, H a multiple of 8");
+  if (B == 0) return 0;
+  if ((!det && D > 0) || !gidx || !tbase || !E || !a1 || !b1 || !x1) return fail(BPC_ERR_ARG, "null buffer");
+  if (reinterpret_cast<uintptr_t>(x1) & 15) return fail(BPC_ERR_ARG, "x1 must be 16-byte aligned");
+  const int64_t groups = B * N * (H / 8);
+  const int blocks = static_cast<int>(std::min<int64_t>((groups + 255) / 256, static_cast<int64_t>(num_sms()) * 16));
+  cascade_stem_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      det, gidx, tbase, E, a1, b1, static_cast<__nv_bfloat16*>(x1), groups, D, N, H / 8);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(BPC_ERR_LAUNCH, std::string("cascade_stem_kernel: ") + cudaGetErrorString(e));
   return 0;
 }

@@ -328,18 +328,27 @@ class CascadeStack(nn.Module):
         return CascadeStack.forward_blocks(self.blocks, h)[0]
 
     @staticmethod
-    def forward_blocks(blocks, h, final=None):
+    def boundary_path(blocks) -> bool:
+        """Blocks of H = 512 with a 128-channel bottleneck (the reference's C14 and C6 blocks) take the one-launch
+        block boundary."""
+        return all(tuple(b.up.weight.shape) == (512, 128) for b in blocks)
+
+    @staticmethod
+    def forward_blocks(blocks, h, final=None, tokens=None):
         """The fused inference path over a sequence of CascadeBlocks (eval mode, fp32 h on the GPU) -> (h, x): the
         residual stream after the last block, and with `final` = (scale, shift) of a folded BatchNorm, x =
         bf16(SiLU(scale h + shift)) (then h is None: a caller that asks for x needs only x).
         Blocks of H = 512 with a 128-channel bottleneck (the reference's C14 blocks) hand over in one launch per block
         boundary (bpc_cascade_boundary: up, residual, the next block's BN1 + SiLU, down and BN2 + SiLU); other sizes
         run the block-by-block fused path."""
+        dev = h.device if h is not None else tokens[3].device
         for b in blocks:
-            if b._cache is None or b._cache["a1"].device != h.device:
+            if b._cache is None or b._cache["a1"].device != dev:
                 b.prepare_inference()
-        if all(tuple(b.up.weight.shape) == (512, 128) for b in blocks):
-            return CascadeStack._forward_boundaries(blocks, h, final)
+        if CascadeStack.boundary_path(blocks):
+            return CascadeStack._forward_boundaries(blocks, h, final, tokens)
+        if h is None:
+            raise ValueError("forward_blocks: the token source needs blocks of the boundary path")
         x = None
         for i, b in enumerate(blocks):
             nxt = blocks[i + 1] if i + 1 < len(blocks) else None
@@ -350,14 +359,22 @@ class CascadeStack(nn.Module):
         return None, x
 
     @staticmethod
-    def _forward_boundaries(blocks, h, final):
-        from .ops import cascade_boundary, gmm_ex
-        h = h.contiguous()
+    def _forward_boundaries(blocks, h, final, tokens=None):
+        """tokens = (det (B, D) uint8, gidx (N), tbase (N), E (5, H)): the stream before the first block is the
+        embedding of the detector tokens, which the first block's kernels compute where they read it (bpc_cascade_stem,
+        bpc_cascade_boundary_tokens) instead of it being written and read back."""
+        from .ops import cascade_boundary, cascade_boundary_tokens, cascade_stem, gmm_ex
         c = blocks[0]._cache
-        N = h.shape[1]
-        if c["ident"].numel() != N or c["ident"].device != h.device:
-            c["ident"] = torch.arange(N, dtype=torch.int32, device=h.device).view(N, 1)
-        _, x1 = residual_affine_silu(h, None, 1.0, 0.0, c["a1"], c["b1"], want_out=False)
+        if tokens is None:
+            h = h.contiguous()
+            N, dev = h.shape[1], h.device
+            _, x1 = residual_affine_silu(h, None, 1.0, 0.0, c["a1"], c["b1"], want_out=False)
+        else:
+            det, gidx, tbase, E = tokens
+            N, dev = gidx.shape[0], E.device
+            x1 = cascade_stem(det, gidx, tbase, E, c["a1"], c["b1"])
+        if c["ident"].numel() != N or c["ident"].device != dev:
+            c["ident"] = torch.arange(N, dtype=torch.int32, device=dev).view(N, 1)
         x2 = gmm_ex(x1, c["ident"], c["down"], scale=c["a2"], shift=c["b2"])
         stream, x = h, None
         for i, b in enumerate(blocks):
@@ -365,6 +382,17 @@ class CascadeStack(nn.Module):
             d = gmm_ex(x2, b.c2d_all, c["wc"], type_split=b._splits[0])
             x3 = gmm_ex(d, b.d2c_all, c["wd"], type_split=b._splits[1], scale=c["a3"], shift=c["b3"])
             sh, su = (1.0, b.scale) if b.res == "branch" else (b.scale, 1.0)
+            if i == 0 and tokens is not None:
+                last = len(blocks) == 1
+                n = None if last else blocks[1]._cache
+                if not last:
+                    stream, x2 = cascade_boundary_tokens(x3, c["up"], *tokens, sh, su, n["a1"], n["b1"], n["down"],
+                                                         n["a2"], n["b2"])
+                elif final is None:
+                    stream, _ = cascade_boundary_tokens(x3, c["up"], *tokens, sh, su, want_y=False)
+                else:
+                    _, x = cascade_boundary_tokens(x3, c["up"], *tokens, sh, su, final[0], final[1], want_h=False)
+                continue
             out = torch.empty_like(h) if stream is h else stream      # the caller's h is never written
             if i + 1 < len(blocks):
                 n = blocks[i + 1]._cache
@@ -390,9 +418,10 @@ class CascadeNet(nn.Module):
       blocks    L CascadeBlocks (the fused inference path of CascadeStack in eval mode on the GPU)
       read-out  SiLU(bn_out(h)); per observable the pooled sources of its support's check -> data relations
                 (a fixed (24 k, N) pooling matrix), the scatter projection (24 H -> H), mlp1, SiLU, mlp2
-    Eval on the GPU: the blocks on the B200 kernels; bn_out + SiLU in one pass (bpc_residual_affine_silu); the
-    read-out's pooling and scatter are plain dense GEMMs (cuBLAS) in bf16 as under the reference's autocast, its MLP
-    in fp32."""
+    Eval on the GPU: the blocks on the B200 kernels (with C14-size blocks the embedded stream is never written: the
+    stem and the first block's kernels read the embedding table by token, and the last block boundary writes
+    SiLU(bn_out(h))); the read-out's pooling and scatter are plain dense GEMMs (cuBLAS) in bf16 as under the
+    reference's autocast, its MLP in fp32."""
 
     def __init__(self, geo, H, L, det_t, det_typ, det_site, logicals, res="branch"):
         super().__init__()
@@ -431,6 +460,7 @@ class CascadeNet(nn.Module):
         self.scatter = nn.Parameter(torch.randn(H, 2 * K * H) / math.sqrt(K * H))
         self.mlp1 = nn.Linear(H, 2 * H)
         self.mlp2 = nn.Linear(2 * H, 1)
+        self._tables = None                         # int32 copies of gidx / tbase for the kernels
 
     def tokens(self, det: torch.Tensor) -> torch.Tensor:
         det = F.pad(det.to(torch.uint8), (0, 1))
@@ -445,10 +475,18 @@ class CascadeNet(nn.Module):
         return self.mlp2(F.silu(self.mlp1(z))).squeeze(-1)
 
     def forward(self, det: torch.Tensor) -> torch.Tensor:
-        h = self.embed(self.tokens(det))
-        if self.training or not h.is_cuda:
+        if self.training or not det.is_cuda:
+            h = self.embed(self.tokens(det))
             for b in self.blocks:
                 h = b(h)
             return self.readout(F.silu(self.bn_out(h.reshape(-1, self.H)).view(h.shape)))
-        _, x = CascadeStack.forward_blocks(self.blocks, h.float().contiguous(), final=_fold_bn(self.bn_out))
+        if CascadeStack.boundary_path(self.blocks):
+            # the stem's embedding is computed by the first block's kernels, never written
+            if self._tables is None or self._tables[0].device != det.device:
+                self._tables = (self.gidx.to(torch.int32), self.tbase.to(torch.int32))
+            tokens = (det.to(torch.uint8).contiguous(), *self._tables, self.embed.weight.float().contiguous())
+            _, x = CascadeStack.forward_blocks(self.blocks, None, final=_fold_bn(self.bn_out), tokens=tokens)
+        else:
+            h = self.embed(self.tokens(det))
+            _, x = CascadeStack.forward_blocks(self.blocks, h.float().contiguous(), final=_fold_bn(self.bn_out))
         return self.readout(x, torch.bfloat16)

@@ -138,6 +138,63 @@ def cascade_boundary(x3: torch.Tensor, w_up: torch.Tensor, h: torch.Tensor, scal
     return out, y
 
 
+def cascade_boundary_tokens(x3: torch.Tensor, w_up: torch.Tensor, det: torch.Tensor, gidx: torch.Tensor,
+                            tbase: torch.Tensor, E: torch.Tensor, scale_h: float, scale_u: float,
+                            a1: torch.Tensor | None = None, b1: torch.Tensor | None = None,
+                            w_down: torch.Tensor | None = None, a2: torch.Tensor | None = None,
+                            b2: torch.Tensor | None = None, want_h: bool = True, want_y: bool = True):
+    """cascade_boundary for the first block of a network (C ABI bpc_cascade_boundary_tokens): the stream h is the
+    embedding E (5, 512) of the detector tokens (det (B, D) uint8, gidx / tbase (N) int32), never materialised.
+    x3 (B, N, 128) -> (h' (B, N, 512) fp32 or None, y or None) as cascade_boundary."""
+    _check_cuda(x3, w_up, det, gidx, tbase, E)
+    B, D = det.shape
+    N = gidx.shape[0]
+    H, Hb = w_up.shape
+    if x3.shape != (B, N, Hb) or E.shape != (5, H):
+        raise ValueError("cascade_boundary_tokens: x3 (B, N, Hb), E (5, H)")
+    dev = x3.device
+    x3, w_up = x3.contiguous(), w_up.contiguous()
+    det = det.to(torch.uint8).contiguous()
+    gidx, tbase = gidx.to(torch.int32).contiguous(), tbase.to(torch.int32).contiguous()
+    E = E.to(torch.float32).contiguous()
+    vec = lambda t: None if t is None else t.to(dev, torch.float32).contiguous()
+    a1, b1, a2, b2 = vec(a1), vec(b1), vec(a2), vec(b2)
+    out = torch.empty(B, N, H, device=dev, dtype=torch.float32) if want_h else None
+    y = None
+    if w_down is not None:
+        w_down = w_down.to(torch.bfloat16).contiguous()
+        y = torch.empty(B, N, w_down.shape[0], device=dev, dtype=torch.bfloat16)
+    elif want_y and a1 is not None:
+        y = torch.empty(B, N, H, device=dev, dtype=torch.bfloat16)
+    ptr = lambda t: None if t is None else t.data_ptr()
+    rc = _lib.lib().bpc_cascade_boundary_tokens(x3.data_ptr(), w_up.data_ptr(), det.data_ptr(), gidx.data_ptr(),
+                                                tbase.data_ptr(), E.data_ptr(), D, N, ptr(out), float(scale_h),
+                                                float(scale_u), ptr(a1), ptr(b1), ptr(w_down), ptr(a2), ptr(b2),
+                                                ptr(y), B, H, Hb, _stream_ptr(dev))
+    _lib.check(rc, "bpc_cascade_boundary_tokens")
+    return out, y
+
+
+def cascade_stem(det: torch.Tensor, gidx: torch.Tensor, tbase: torch.Tensor, E: torch.Tensor, a1: torch.Tensor,
+                 b1: torch.Tensor) -> torch.Tensor:
+    """The Cascade network's stem and first BN1 + SiLU (C ABI bpc_cascade_stem): det (B, D) uint8 ->
+    x1 = bf16(SiLU(a1 E[token] + b1)) (B, N, H), the embedded stream itself not written."""
+    _check_cuda(det, gidx, tbase, E)
+    B, D = det.shape
+    N = gidx.shape[0]
+    H = E.shape[1]
+    dev = E.device
+    det = det.to(torch.uint8).contiguous()
+    gidx, tbase = gidx.to(torch.int32).contiguous(), tbase.to(torch.int32).contiguous()
+    E = E.to(torch.float32).contiguous()
+    a1, b1 = a1.to(dev, torch.float32).contiguous(), b1.to(dev, torch.float32).contiguous()
+    x1 = torch.empty(B, N, H, device=dev, dtype=torch.bfloat16)
+    rc = _lib.lib().bpc_cascade_stem(det.data_ptr(), gidx.data_ptr(), tbase.data_ptr(), E.data_ptr(), D, N,
+                                     a1.data_ptr(), b1.data_ptr(), x1.data_ptr(), B, H, _stream_ptr(dev))
+    _lib.check(rc, "bpc_cascade_stem")
+    return x1
+
+
 def residual_affine_silu(h: torch.Tensor, u: torch.Tensor | None, scale_h: float, scale_u: float,
                          a: torch.Tensor | None = None, b: torch.Tensor | None = None, want_out: bool = True):
     """One pass over an fp32 (..., H) stream (C ABI bpc_residual_affine_silu): v = scale_h h + scale_u u (u bf16 or

@@ -81,6 +81,23 @@ BPC_API int bpc_cascade_boundary(const void* x3, const void* w_up, const float* 
                                  float scale_u, const float* a1, const float* b1, const void* w_down, const float* a2,
                                  const float* b2, void* y, int64_t rows, int32_t H, int32_t Hb, bpc_stream_t stream);
 
+/* bpc_cascade_boundary for the first block of a Cascade network, whose stream is the embedding of the detector tokens
+ * (CascadeBB.tokens / backbone, cascade_net.py:310-318): h[shot, node] = E[tbase[node] + det[shot, gidx[node]]]
+ * (gidx[node] == D: no detector, token tbase[node]) is read from the 5 x H table instead of memory.  det (B, D) uint8,
+ * gidx, tbase (N) int32, E (5, H) fp32 16-byte aligned; rows = B N; the rest as bpc_cascade_boundary. */
+BPC_API int bpc_cascade_boundary_tokens(const void* x3, const void* w_up, const uint8_t* det, const int32_t* gidx,
+                                        const int32_t* tbase, const float* E, int32_t D, int32_t N, float* h_out,
+                                        float scale_h, float scale_u, const float* a1, const float* b1,
+                                        const void* w_down, const float* a2, const float* b2, void* y, int64_t B,
+                                        int32_t H, int32_t Hb, bpc_stream_t stream);
+
+/* The Cascade network's stem and its first block's BN1 + SiLU in one pass (cascade_net.py:279-285,310-318 and the
+ * Block's first BatchNorm): x1[shot, node, :] = bf16(SiLU(a1 E[token] + b1)) with the token as in
+ * bpc_cascade_boundary_tokens, without writing the embedded stream.  x1 (B, N, H) bf16 16-byte aligned, H % 8 == 0. */
+BPC_API int bpc_cascade_stem(const uint8_t* det, const int32_t* gidx, const int32_t* tbase, const float* E, int32_t D,
+                             int32_t N, const float* a1, const float* b1, void* x1, int64_t B, int32_t H,
+                             bpc_stream_t stream);
+
 /* One memory-bound pass over a (rows, H) fp32 residual stream of the Cascade bottleneck block (no reference
  * counterpart as one call; it replaces the casts, scale, add and activation torch runs between the reference Block's
  * up projection and the next block's first BatchNorm, cascade_net.py:236-259):

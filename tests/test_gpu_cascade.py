@@ -281,3 +281,35 @@ def test_cascade_net_c14_width_matches_reference(golden_dir, c14):
           "(the reference's own bf16 run: %.2e, %.2e)" % (err, dev, err_ref, dev_ref))
     assert err < 2e-2 and dev < 5e-2
     assert err <= 2 * err_ref and dev <= 2 * dev_ref
+
+
+def test_token_stem_and_boundary_match_the_embedded_stream():
+    """bpc_cascade_stem and bpc_cascade_boundary_tokens read the embedding table by detector token instead of an
+    embedded stream: both give the same bits as the residual pass and the boundary kernel on the materialised
+    stream h0 = E[token] (tokens as CascadeBB.tokens: 2 type + bit at a detector's node, 4 elsewhere)."""
+    from codecoder_b200.ops import cascade_boundary, cascade_boundary_tokens, cascade_stem, residual_affine_silu
+    B, D, N = 5, 360, 504
+    cpu = torch.Generator().manual_seed(77)
+    nodes = torch.randperm(N, generator=cpu)[:D]
+    gidx = torch.full((N,), D, dtype=torch.int32)
+    gidx[nodes] = torch.arange(D, dtype=torch.int32)
+    tbase = torch.full((N,), 4, dtype=torch.int32)
+    tbase[nodes] = 2 * torch.randint(0, 2, (D,), generator=cpu, dtype=torch.int32)
+    det = (torch.rand(B, D, generator=cpu) < 0.3).to(torch.uint8)
+    E = torch.randn(5, 512, generator=cpu)
+    det, gidx, tbase, E = det.cuda(), gidx.cuda(), tbase.cuda(), E.cuda()
+    tok = tbase.long() + F.pad(det, (0, 1))[:, gidx.long()].long()
+    h0 = E[tok].contiguous()
+    x3, w_up, w_down, _, a1, b1, a2, b2 = boundary_case(B * N, 9)
+    x3 = x3.view(B, N, 128)
+    sh, su = 1 / math.sqrt(28), 1.0
+    x1 = cascade_stem(det, gidx, tbase, E, a1, b1)
+    _, x1_ref = residual_affine_silu(h0, None, 1.0, 0.0, a1, b1, want_out=False)
+    h_t, x2_t = cascade_boundary_tokens(x3, w_up, det, gidx, tbase, E, sh, su, a1, b1, w_down, a2, b2)
+    h_r, x2_r = cascade_boundary(x3, w_up, h0, sh, su, a1, b1, w_down, a2, b2)
+    _, xl_t = cascade_boundary_tokens(x3, w_up, det, gidx, tbase, E, sh, su, a1, b1, want_h=False)
+    _, xl_r = cascade_boundary(x3, w_up, h0, sh, su, a1, b1, h_out=None)
+    torch.cuda.synchronize()
+    assert torch.equal(x1, x1_ref)
+    assert torch.equal(h_t, h_r) and torch.equal(x2_t, x2_r)
+    assert torch.equal(xl_t, xl_r)
