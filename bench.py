@@ -333,11 +333,12 @@ def measure_cascade_net(tables_npz, dev, pk, shots=4096, steps=5, warmup=3):
             "backbone_us_per_shot": ms_blocks * 1000.0 / shots, "flop_per_shot": flop,
             "tflops": flop * shots / (ms * 1e-3) / 1e12, "tensor_frac_of_sustained": flop * shots / (ms * 1e-3) / 1e12
             / pk["bf16_tflops_sustained"],
-            "kernels": "stem (torch gather + embedding); first block's BN1 + SiLU (residual_affine_silu_kernel) and "
-                       "down + BN2 + SiLU (gmm_tc_kernel); per block: the two-type conv (gmm_wide_kernel check -> data, "
-                       "gmm_wide_kernel data -> check + BN3 + SiLU) and cascade_boundary_kernel (up, residual, the "
-                       "next block's BN1 + SiLU + down + BN2 + SiLU, or bn_out + SiLU after the last); read-out: "
-                       "cuBLAS bf16 GEMMs (pooling, scatter)"}
+            "kernels": "cascade_stem_kernel (tokens -> the first block's BN1 + SiLU, the embedded stream not written) "
+                       "and gmm_tc_kernel (down + BN2 + SiLU); per block: the two-type conv (gmm_wide_kernel check -> "
+                       "data, gmm_wide_kernel data -> check + BN3 + SiLU) and cascade_boundary_kernel (up, residual, "
+                       "the next block's BN1 + SiLU + down + BN2 + SiLU, or bn_out + SiLU after the last; the first "
+                       "reads the embedding by token); read-out: cuBLAS GEMMs (bf16 pooling and scatter, fp32 MLP); "
+                       "backbone_us_per_shot: the 14 blocks from a materialised stream"}
 
 
 def run_reference(args, cfg, g, params, rank, world):
