@@ -9,7 +9,9 @@
 //
 // Unfused these are four launches that move ~8.5 KB per node row through HBM (u and x1 are written and read back);
 // here one kernel reads x3 (256 B) and h (2 KB) and writes h' (2 KB) and x2 (256 B) per row.  After the last block
-// the same kernel writes x1 (the stream after bn_out + SiLU) instead of running a down projection.
+// the same kernel writes x1 (the stream after bn_out + SiLU) instead of running a down projection.  For the first
+// block of a network (token mode) h is not read at all: it is the embedding table's row for each node's detector
+// token (CascadeBB.tokens, cascade_net.py:310-312), and cascade_stem_kernel below writes that block's BN1 + SiLU.
 //
 // The arithmetic is the unfused path's, in the same order: the MMAs accumulate in K order; u is rounded to bf16
 // before the residual; h' = fmaf(scale_u, u, scale_h h); x1 = SiLU, rounded to bf16; x2 = the op
@@ -30,6 +32,7 @@
 //   warps 10-13 the down epilogue: TMEM -> BN2 + SiLU -> bf16 rows of x2
 //   warp 14     the stores and the h loads: once the middle stage has finished a chunk it stores h' (and x1 after the
 //               last block) by TMA and, once the stores have read the boxes, refills the slot with the chunk three ahead
+//               (token mode: hands the slot back to the middle stage without a load)
 // Every wait is bounded (mbar_wait); on a timeout the status word is set, each role leaves its loop, waits (bounded)
 // for the copies and MMAs it issued, and the CTA returns.
 #include <algorithm>
