@@ -140,9 +140,10 @@ class PreDecoder:
     def forward_host(self, det_host: torch.Tensor, logits_host: torch.Tensor, residual_host: torch.Tensor,
                      slice_shots: int | None = None) -> None:
         """Host buffers in, host buffers out (pinned memory): det (B, N_c) uint8 -> logits (B, N_d, 2) fp32,
-        residual (B, N_c) uint8.  The batch goes through in slices of `slice_shots` (default: the pass size), with
-        the copies of one slice on a copy stream overlapping the forward pass of the previous one (two device buffer
-        sets).  Synchronises before returning."""
+        residual (B, N_c) uint8.  The batch goes through in slices of `slice_shots` (default: the pass size) with two
+        device buffer sets: the next slice's detectors go up on one copy stream while the current slice runs, and the
+        finished slice's results come down on another, so the forward passes follow one another without waiting for
+        the copies.  Synchronises before returning."""
         B = det_host.shape[0]
         if B == 0:
             return
@@ -158,32 +159,42 @@ class PreDecoder:
                      torch.empty(S, self.geo.N_d, 2, dtype=torch.float32, device=dev),
                      torch.empty(S, self.geo.N_c, dtype=torch.uint8, device=dev)) for _ in range(2)]
             self._host_bufs = bufs
-            self._copy_stream = torch.cuda.Stream(device=dev)
+            self._copy_streams = (torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev))
         comp = torch.cuda.current_stream(dev)
-        copy = self._copy_stream
-        done = [None, None]                     # event: slice buffers free again (outputs copied out)
+        up, down = self._copy_streams
+        starts = list(range(0, B, S))
+        ready = [None, None]                    # event: the slice's detectors are on the device
+        done = [None, None]                     # event: the slice buffers are free again (results copied out)
+
+        def upload(i):
+            b0, k = starts[i], i % 2
+            n = min(S, B - b0)
+            with torch.cuda.stream(up):
+                if done[k] is not None:
+                    up.wait_event(done[k])
+                bufs[k][0][:n].copy_(det_host[b0:b0 + n], non_blocking=True)
+                ready[k] = torch.cuda.Event()
+                ready[k].record(up)
+
         with torch.cuda.device(dev):
-            for i, b0 in enumerate(range(0, B, S)):
+            upload(0)
+            for i, b0 in enumerate(starts):
                 n = min(S, B - b0)
                 k = i % 2
                 d_det, d_lg, d_rs = (t[:n] for t in bufs[k])
-                with torch.cuda.stream(copy):
-                    if done[k] is not None:
-                        copy.wait_event(done[k])
-                    d_det.copy_(det_host[b0:b0 + n], non_blocking=True)
-                    ready = torch.cuda.Event()
-                    ready.record(copy)
-                comp.wait_event(ready)
+                comp.wait_event(ready[k])
                 self.forward_into(d_det, d_lg, d_rs)
                 computed = torch.cuda.Event()
                 computed.record(comp)
-                with torch.cuda.stream(copy):
-                    copy.wait_event(computed)
+                if i + 1 < len(starts):
+                    upload(i + 1)               # overlaps this slice's forward pass
+                with torch.cuda.stream(down):
+                    down.wait_event(computed)
                     logits_host[b0:b0 + n].copy_(d_lg, non_blocking=True)
                     residual_host[b0:b0 + n].copy_(d_rs, non_blocking=True)
                     done[k] = torch.cuda.Event()
-                    done[k].record(copy)
-            comp.wait_stream(copy)
+                    done[k].record(down)
+            comp.wait_stream(down)
         torch.cuda.synchronize(dev)
 
     def record_step_events(self, pairs) -> None:
