@@ -258,15 +258,18 @@ __global__ void __launch_bounds__(256) embed_tokens_fwd_kernel(const uint8_t* __
 
 // The backward as two sums per check type t, because a token is 2 t + det and det = 1 is rare: S_t over every row of
 // type t and D_t over its rows with det = 1, so dE[2 t + 1] = D_t and dE[2 t] = S_t - D_t.  Each warp takes a fixed
-// run of rows, one row per step with four rows' loads in flight; lane l holds channels 4 l .. 4 l + 3 (+ 128), read as
+// run of rows, one row per step with eight (C <= 128) or four rows' loads in flight; lane l holds channels
+// 4 l .. 4 l + 3 (+ 128), read as
 // one 16-byte (fp32) and one 8-byte (bf16) vector; the type and det branches are uniform across the warp.  The
 // block's warps are added in order in shared memory: deterministic, no atomics.
+// SLOTS: 128-channel slots per row (C <= 128 SLOTS); ROWS: rows whose loads are in flight per warp.
+template <int SLOTS, int ROWS>
 __global__ void __launch_bounds__(kEmbBwdThreads) embed_tokens_bwd_partial_kernel(
     const uint8_t* __restrict__ det, const uint8_t* __restrict__ ctype, const float* __restrict__ g,
     const __nv_bfloat16* __restrict__ g16, float* __restrict__ partial, int64_t rows, int N, int C) {
   __shared__ float red[kEmbBwdThreads / 32][4][kEmbMaxC];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  constexpr int kSlots = kEmbMaxC / 128;                 // 4 channels per lane per slot
+  constexpr int kSlots = SLOTS;                          // 4 channels per lane per slot
   float S[2][kSlots][4], D[2][kSlots][4];
 #pragma unroll
   for (int t = 0; t < 2; ++t)
@@ -279,11 +282,11 @@ __global__ void __launch_bounds__(kEmbBwdThreads) embed_tokens_bwd_partial_kerne
   const int64_t per_warp = (r1 - r0 + kEmbBwdThreads / 32 - 1) / (kEmbBwdThreads / 32);
   const int64_t w0 = r0 + warp * per_warp, w1 = min(r1, w0 + per_warp);
   int n = w0 < w1 ? static_cast<int>(w0 % N) : 0;      // node of row w0; advanced without a division per row
-  for (int64_t r = w0; r < w1; r += 4) {
-    float v[4][kSlots][4];
-    int ty[4], dt[4];
+  for (int64_t r = w0; r < w1; r += ROWS) {
+    float v[ROWS][kSlots][4];
+    int ty[ROWS], dt[ROWS];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < ROWS; ++u) {
       const int64_t rr = r + u;
       int nn = n + u;
       while (nn >= N) nn -= N;
@@ -311,7 +314,7 @@ __global__ void __launch_bounds__(kEmbBwdThreads) embed_tokens_bwd_partial_kerne
       }
     }
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < ROWS; ++u) {
 #pragma unroll
       for (int j = 0; j < kSlots; ++j)
 #pragma unroll
@@ -329,7 +332,7 @@ __global__ void __launch_bounds__(kEmbBwdThreads) embed_tokens_bwd_partial_kerne
           }
       }
     }
-    n += 4;
+    n += ROWS;
     while (n >= N) n -= N;
   }
 #pragma unroll
@@ -492,7 +495,8 @@ extern "C" int bpc_embed_tokens_bwd(const uint8_t* det, const uint8_t* check_typ
     return fail(BPC_ERR_ARG, "g must be 16-byte and g_bf16 8-byte aligned");
   if (workspace_bytes < bpc_embed_tokens_bwd_workspace_size(C)) return fail(BPC_ERR_SPACE, "embedding workspace too small");
   float* partial = static_cast<float*>(workspace);
-  embed_tokens_bwd_partial_kernel<<<kEmbBwdBlocks, kEmbBwdThreads, 0, s>>>(
+  auto partial_kernel = C <= 128 ? embed_tokens_bwd_partial_kernel<1, 8> : embed_tokens_bwd_partial_kernel<2, 4>;
+  partial_kernel<<<kEmbBwdBlocks, kEmbBwdThreads, 0, s>>>(
       det, check_type, g, static_cast<const __nv_bfloat16*>(g_bf16), partial, B * N, N, C);
   embed_tokens_bwd_sum_kernel<<<(4 * C + 127) / 128, 128, 0, s>>>(partial, dE, 4 * C, kEmbBwdBlocks);
   cudaError_t le = cudaGetLastError();
