@@ -48,6 +48,10 @@ SIGNATURES = {
     "bpc_gelu_residual_bwd": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_i32, c_i32, c_vp]),
     "bpc_embed_tokens_fwd": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_vp]),
     "bpc_embed_tokens_bwd_workspace_size": (ctypes.c_size_t, [c_i32]),
+    "bpc_head_bce_workspace_size": (ctypes.c_size_t, [c_i32]),
+    "bpc_head_bce_fwd": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, ctypes.c_size_t, c_i64, c_i32, c_vp]),
+    "bpc_head_bce_bwd": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, ctypes.c_size_t, c_i64,
+                                        c_i32, c_vp]),
     "bpc_embed_tokens_bwd": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, ctypes.c_size_t, c_i64, c_i32, c_i32,
                                             c_vp]),
     "bpc_gather_mm_dgrad": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_i32, c_i32, c_i32,

@@ -440,6 +440,52 @@ class EmbedTokensB200(torch.autograd.Function):
         return None, None, dE
 
 
+class HeadBCEB200(torch.autograd.Function):
+    """The training network's head and loss (C ABI bpc_head_bce_fwd / _bwd): hd (..., C) bf16 data stream, W (2, C)
+    and b (2) fp32, labels (..., 2) 0/1 -> the mean BCE-with-logits of the bf16 logits linear(hd, W, b), the value
+    and the gradients of torch's bf16 autocast composition (F.linear, then binary_cross_entropy_with_logits on the
+    logits in fp32) without the logits tensor or the head GEMMs."""
+
+    @staticmethod
+    def forward(ctx, hd, W, b, labels):
+        C = hd.shape[-1]
+        hd = hd.to(torch.bfloat16).contiguous()
+        labels = labels.to(torch.uint8).contiguous()
+        Wf, bf = W.float().contiguous(), b.float().contiguous()
+        rows = hd.numel() // C
+        L = _lib.lib()
+        ws = torch.empty(int(L.bpc_head_bce_workspace_size(C)), device=hd.device, dtype=torch.uint8)
+        loss = torch.empty((), device=hd.device, dtype=torch.float32)
+        rc = L.bpc_head_bce_fwd(hd.data_ptr(), Wf.data_ptr(), bf.data_ptr(), labels.data_ptr(), loss.data_ptr(),
+                                ws.data_ptr(), ws.numel(), rows, C, _stream_ptr(hd.device))
+        _lib.check(rc, "bpc_head_bce_fwd")
+        ctx.save_for_backward(hd, Wf, bf, labels)
+        ctx.dtypes = (W.dtype, b.dtype)
+        return loss
+
+    @staticmethod
+    def backward(ctx, go):
+        hd, Wf, bf, labels = ctx.saved_tensors
+        C = hd.shape[-1]
+        rows = hd.numel() // C
+        L = _lib.lib()
+        ws = torch.empty(int(L.bpc_head_bce_workspace_size(C)), device=hd.device, dtype=torch.uint8)
+        go = go.float().contiguous()
+        dh = torch.empty_like(hd)
+        dW = torch.empty_like(Wf)
+        db = torch.empty_like(bf)
+        rc = L.bpc_head_bce_bwd(hd.data_ptr(), Wf.data_ptr(), bf.data_ptr(), labels.data_ptr(), go.data_ptr(),
+                                dh.data_ptr(), dW.data_ptr(), db.data_ptr(), ws.data_ptr(), ws.numel(), rows, C,
+                                _stream_ptr(hd.device))
+        _lib.check(rc, "bpc_head_bce_bwd")
+        return dh, dW.to(ctx.dtypes[0]), db.to(ctx.dtypes[1]), None
+
+
+def head_bce(hd, W, b, labels):
+    """HeadBCEB200.apply (see there)."""
+    return HeadBCEB200.apply(hd, W, b, labels)
+
+
 def embed_tokens(det, check_type, E):
     """EmbedTokensB200.apply (see there)."""
     return EmbedTokensB200.apply(det, check_type, E)

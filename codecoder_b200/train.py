@@ -24,7 +24,7 @@ import torch
 import torch.nn.functional as F
 from torch import nn
 
-from .ops import bipartite_step, embed_tokens, gather_mm, target_table
+from .ops import bipartite_step, embed_tokens, gather_mm, head_bce, target_table
 from .params import N_TOKENS
 
 
@@ -74,12 +74,19 @@ class PreDecoderNet(nn.Module):
         for c in range(2):
             self.w_d2c[2 * (L - 1) + c].requires_grad_(False)
 
-    def forward(self, det: torch.Tensor) -> torch.Tensor:
-        """det (B, N_c) uint8 -> logits (B, N_d, 2) (bf16 under autocast)."""
+    def forward(self, det: torch.Tensor, labels: torch.Tensor | None = None) -> torch.Tensor:
+        """det (B, N_c) uint8 -> logits (B, N_d, 2) (bf16 under autocast); with labels (B, N_d, 2) 0/1 -> the mean
+        BCE-with-logits loss of those logits (the training step's loss, cascade_train.py:292-320)."""
         if (self.fused and self._fused_ok and self.gmm is gather_mm and det.is_cuda and
                 torch.is_autocast_enabled("cuda") and torch.get_autocast_dtype("cuda") == torch.bfloat16 and
                 self.cfg.channels % 8 == 0):
-            return self._forward_fused(det)
+            return self._forward_fused(det, labels)
+        z = self._forward_unfused(det)
+        if labels is None:
+            return z
+        return F.binary_cross_entropy_with_logits(z.float(), labels.float())
+
+    def _forward_unfused(self, det: torch.Tensor) -> torch.Tensor:
         tok = 2 * self.check_type + det.long()
         hc = F.embedding(tok, self.embed)
         hd = None
@@ -93,7 +100,7 @@ class PreDecoderNet(nn.Module):
             hc = hc + F.gelu(a, approximate="tanh")
         return F.linear(hd, self.head_w, self.head_b)
 
-    def _forward_fused(self, det: torch.Tensor) -> torch.Tensor:
+    def _forward_fused(self, det: torch.Tensor, labels: torch.Tensor | None = None) -> torch.Tensor:
         """The same network under bf16 autocast through ops.bipartite_step: each step is the op's forward kernels
         plus one GELU + residual pass (forward) and one GELU-gradient pass (backward), the check stream fp32 with its
         bf16 copy made in the same pass, the data stream bf16."""
@@ -106,7 +113,11 @@ class PreDecoderNet(nn.Module):
             if l == self.cfg.layers - 1:
                 break
             hc, hc16 = bipartite_step(hd, hc, d2c, self.w_d2c[2 * l], self.w_d2c[2 * l + 1])
-        return F.linear(hd, self.head_w, self.head_b)
+        if labels is not None and self.cfg.channels <= 128:
+            # head and loss in one pass each way, the logits never materialised (ops.HeadBCEB200)
+            return head_bce(hd, self.head_w, self.head_b, labels)
+        z = F.linear(hd, self.head_w, self.head_b)
+        return z if labels is None else F.binary_cross_entropy_with_logits(z.float(), labels.float())
 
 
 class Trainer:
@@ -135,8 +146,7 @@ class Trainer:
         """det (B, N_c) uint8, err (B, N_d, 2) 0/1 labels -> the batch loss (a device scalar, not synchronised)."""
         ctx = torch.autocast("cuda", dtype=torch.bfloat16) if self.autocast else nullcontext()
         with ctx:
-            z = self.net(det)
-        loss = F.binary_cross_entropy_with_logits(z.float(), err.float())
+            loss = self.net(det, err)            # logits and loss (fused on the GPU path)
         loss.backward()
         torch.nn.utils.clip_grad_norm_(self.params, self.clip)
         self.opt.step()

@@ -136,6 +136,21 @@ BPC_API int bpc_embed_tokens_bwd(const uint8_t* det, const uint8_t* check_type, 
                                  float* dE, void* workspace, size_t workspace_bytes, int64_t B, int32_t N, int32_t C,
                                  bpc_stream_t stream);
 
+/* The training network's X/Z head and its loss, one pass each way (the head linear(h_d, W, b) under bf16 autocast and
+ * the mean BCE-with-logits of the reference's training step, cascade_train.py:292-320):
+ *   forward:  z_j = bf16(sum_c hd[r, c] W[j, c] + b[j]) (W, b rounded to bf16);  *loss = mean over r, j of
+ *             BCE-with-logits(z_j, labels[r, j])
+ *   backward: g_j = bf16((sigmoid(z_j) - labels[r, j]) *grad_loss / n);  dh[r, c] = bf16(g_0 W[0, c] + g_1 W[1, c]);
+ *             dW[j, c] = bf16(sum_r g_j hd[r, c]);  db[j] = bf16(sum_r g_j)   (n = 2 rows; fixed-order fp32 sums)
+ * hd, dh (rows, C) bf16 8-byte aligned, C % 4 == 0 and C <= 128; W (2, C), b (2), loss, grad_loss, dW, db fp32 device
+ * memory; labels (rows, 2) uint8 0/1; workspace of bpc_head_bce_workspace_size(C) bytes; rows > 0. */
+BPC_API size_t bpc_head_bce_workspace_size(int32_t C);
+BPC_API int bpc_head_bce_fwd(const void* hd, const float* W, const float* b, const uint8_t* labels, float* loss,
+                             void* workspace, size_t workspace_bytes, int64_t rows, int32_t C, bpc_stream_t stream);
+BPC_API int bpc_head_bce_bwd(const void* hd, const float* W, const float* b, const uint8_t* labels,
+                             const float* grad_loss, void* dh, float* dW, float* db, void* workspace,
+                             size_t workspace_bytes, int64_t rows, int32_t C, bpc_stream_t stream);
+
 /* Input gradient of bpc_gather_mm_fwd through the target table:
  *   gx[b, s, :] = sum_r gy[b, tgt[s, r], :] W_r,   tgt (NS, K) int32, NT (or any value outside [0, NT)) = none
  * gy (B, NT, Co), gx (B, NS, Ci), W (Co, K*Ci) as in the forward.  tgt[s, r] is the target that reads source s

@@ -155,3 +155,33 @@ def test_embed_tokens_match_torch():
     (h16.float() * gh16.float()).sum().backward()
     (h_ref * (gh + gh16.float())).sum().backward()
     assert rel(E.grad, E_ref.grad) < 1e-5
+
+
+def test_head_loss_matches_the_torch_composition():
+    """ops.head_bce (the training network's head and loss in one pass each way) against F.linear under bf16 autocast
+    followed by binary_cross_entropy_with_logits on the logits in fp32: the loss within 1e-3 relative (bf16 logits
+    whose fp32 sums run in another order may round one step apart), the input, weight and bias gradients within
+    2e-2 of max |ref| (bf16 outputs); an upstream gradient of 2 doubles them."""
+    from codecoder_b200.ops import head_bce
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    rows, C = 5000, 96
+    hd = torch.randn(rows, C, device="cuda", generator=gen).bfloat16()
+    W0 = torch.randn(2, C, device="cuda", generator=gen) / C ** 0.5
+    b0 = 0.1 * torch.randn(2, device="cuda", generator=gen)
+    y = (torch.rand(rows, 2, device="cuda", generator=gen) < 0.1).to(torch.uint8)
+    out = []
+    for fused in (True, False):
+        h = hd.clone().requires_grad_()
+        W = W0.clone().requires_grad_()
+        b = b0.clone().requires_grad_()
+        if fused:
+            loss = head_bce(h, W, b, y)
+        else:
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                z = F.linear(h, W, b)
+            loss = F.binary_cross_entropy_with_logits(z.float(), y.float())
+        (2.0 * loss).backward()
+        out.append((loss.detach(), h.grad, W.grad, b.grad))
+    (lf, hf, Wf, bf), (lu, hu, Wu, bu) = out
+    assert abs(float(lf) - float(lu)) <= 1e-3 * abs(float(lu))
+    assert rel(hf, hu) < 2e-2 and rel(Wf, Wu) < 2e-2 and rel(bf, bu) < 2e-2, (rel(hf, hu), rel(Wf, Wu), rel(bf, bu))
