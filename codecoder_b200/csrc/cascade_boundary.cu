@@ -445,10 +445,10 @@ int launch_boundary(const void* x3, const void* w_up, const float* h, const Toke
                     bpc_stream_t stream) {
   if (H != kBH || Hb != kBB) return fail(BPC_ERR_ARG, "the block boundary supports H = 512 with a 128-channel bottleneck");
   if (rows < 0 || rows > (static_cast<int64_t>(1) << 30)) return fail(BPC_ERR_ARG, "rows must be in [0, 2^30]");
+  if (rows == 0) return 0;                      // nothing to do (empty buffers may be null)
   const bool down = w_down != nullptr;
   if (down && (!a1 || !b1 || !a2 || !b2 || !y)) return fail(BPC_ERR_ARG, "the down projection needs a1, b1, a2, b2 and y");
   if (!down && y && (!a1 || !b1)) return fail(BPC_ERR_ARG, "x1 needs a1 and b1");
-  if (rows == 0) return 0;
   if (!x3 || !w_up || (!h && !tok)) return fail(BPC_ERR_ARG, "null buffer");
   const uintptr_t al16 = reinterpret_cast<uintptr_t>(x3) | reinterpret_cast<uintptr_t>(w_up) |
                          reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(h_out) |

@@ -482,7 +482,7 @@ class CascadeNet(nn.Module):
         observables' MLP (k rows per shot, a negligible share of the work) in fp32."""
         B, dt = x.shape[0], dt or x.dtype
         pooled = torch.matmul(self.pool.to(dt), x.to(dt))                      # (B, 24 k, H)
-        z = (pooled.view(B, self.k, -1) @ self.scatter.t().to(dt)).float()     # (B, k, H)
+        z = (pooled.view(B, self.k, self.scatter.shape[1]) @ self.scatter.t().to(dt)).float()     # (B, k, H)
         return self.mlp2(F.silu(self.mlp1(z))).squeeze(-1)
 
     def forward(self, det: torch.Tensor) -> torch.Tensor:

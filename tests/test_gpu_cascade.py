@@ -313,3 +313,26 @@ def test_token_stem_and_boundary_match_the_embedded_stream():
     assert torch.equal(x1, x1_ref)
     assert torch.equal(h_t, h_r) and torch.equal(x2_t, x2_r)
     assert torch.equal(xl_t, xl_r)
+
+
+def test_cascade_net_single_shot_and_empty_batch(golden_dir, c14):
+    """The C14-width network on one shot (504 node rows: a partial last tile in every kernel) gives that shot's logits
+    of a larger batch, and an empty batch gives an empty result."""
+    from cascade_weights import cascade_state
+    conv_z, _ = c14
+    z = dict(np.load(os.path.join(golden_dir, "cascade_net_bb72_h512.npz")))
+    geo = bb72_geo(conv_z)
+    geo.T, geo.n2, geo.N = int(z["T"]), int(z["n2"]), int(z["N"])
+    net = CascadeNet(geo, int(z["H"]), int(z["L"]), z["det_t"], z["det_typ"], z["det_site"], z["logicals"],
+                     res=str(z["res"]))
+    state = cascade_state({k: tuple(v.shape) for k, v in net.state_dict().items()}, int(z["seed"]))
+    net.load_state_dict({k: torch.as_tensor(v) for k, v in state.items()})
+    net = net.cuda().eval()
+    det = torch.as_tensor(z["det"]).cuda()
+    with torch.no_grad():
+        many = net(det)
+        one = net(det[5:6])
+        none = net(det[:0])
+    torch.cuda.synchronize()
+    assert one.shape == (1, many.shape[1]) and none.shape == (0, many.shape[1])
+    assert rel(one[0], many[5]) < 1e-5
