@@ -567,18 +567,43 @@ def main():
         sd = StreamingDecoder(scfg.d, scfg.rounds, scfg, sparams, device=dev)
         lat_g = sd.latency(rounds[:min(len(rounds), 5200)], warmup=200)
         del sd
-        ps = PersistentStreamingDecoder(scfg.d, scfg.rounds, scfg, sparams, device=dev)
-        try:
-            ps.start()
-            lat = ps.latency(rounds, warmup=200)
-            ps.stop()
-        finally:
-            ps.close()
+        # the resident kernel in both layouts; the headline is the one the default (auto) layout runs: the 8 clusters
+        lats, used = {}, {}
+        for layout in ("clusters", "one_cluster"):
+            ps = PersistentStreamingDecoder(scfg.d, scfg.rounds, scfg, sparams, device=dev, layout=layout)
+            try:
+                ps.start()
+                used[layout] = ps.layout()
+                lats[layout] = ps.latency(rounds if layout == "clusters" else rounds[:5200], warmup=200)
+                ps.stop()
+            except RuntimeError as e:
+                used[layout] = f"unavailable: {e}"
+            finally:
+                ps.close()
+        # the kernels' own phase stamps of one round (tracing on, a short run of each layout)
+        phases = {}
+        for layout in lats:
+            ps = PersistentStreamingDecoder(scfg.d, scfg.rounds, scfg, sparams, device=dev, layout=layout, trace=True)
+            try:
+                ps.latency(rounds[:600], warmup=100)
+                ps.stop()
+                tab = ps.phase_table()
+                keys = list(PersistentStreamingDecoder.PHASES) + ["total"]
+                phases[layout] = {"median_ns_per_step": {k: float(np.median([st[k] for st in tab["steps"]]))
+                                                         for k in keys},
+                                  "round_ns": tab["round"], "steps": len(tab["steps"])}
+            finally:
+                ps.close()
+        head = "clusters" if "clusters" in lats else "one_cluster"
+        lat = lats[head]
         sg = ps.geo
         sflop = flops_per_shot(scfg, sg.N_c, sg.N_d)
+        sms = {"one_cluster": f"one cluster of {2 * max((sg.N_d + 127) // 128, 2 * ((sg.nh * scfg.rounds + 127) // 128))}"
+                              f" CTAs", "clusters": "8 clusters x 8 CTAs"}
         stream = {"config": f"d={scfg.d}, window {scfg.rounds} rounds, batch 1, {scfg.layers} layers, C={scfg.channels},"
-                            f" {scfg.dtype}, p={scfg.p}; one resident kernel (64 SMs) served through a request line in "
-                            f"mapped host memory (C ABI bpc_stream_run)",
+                            f" {scfg.dtype}, p={scfg.p}; one resident kernel ({sms[head]}) served through a request "
+                            f"line in mapped host memory (C ABI bpc_stream_run)",
+                  "layout": head,
                   "rounds": int(len(lat)), "p50_us": float(np.percentile(lat, 50)),
                   "p99_us": float(np.percentile(lat, 99)), "mean_us": float(lat.mean()),
                   "clock": "host wall clock in the library's loop, from writing a round's request to reading its "
@@ -586,6 +611,10 @@ def main():
                   "graph_replay": {"p50_us": float(np.percentile(lat_g, 50)), "p99_us": float(np.percentile(lat_g, 99)),
                                    "rounds": int(len(lat_g)),
                                    "how": "StreamingDecoder: one CUDA-graph replay per round (node-tiled kernels)"},
+                  "phases": phases,
+                  "layouts": {k: ({"p50_us": float(np.percentile(v, 50)), "p99_us": float(np.percentile(v, 99)),
+                                   "rounds": int(len(v)), "kernel": sms[k]} if k in lats else used[k])
+                              for k, v in list(lats.items()) + [(k, None) for k in used if k not in lats]},
                   "flop_per_round": sflop, "roofline_us_all_sms": sflop / (pk["bf16_tflops"] * 1e12) * 1e6}
 
     cascade = None

@@ -72,11 +72,15 @@ SIGNATURES = {
     "bpc_predecoder_destroy": (None, [c_vp]),
     "bpc_predecoder_forward_noalloc": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_vp]),
     "bpc_stream_create": (ctypes.c_int, [c_vp, c_i32, c_i32, c_i32, c_i32, ctypes.POINTER(c_vp)]),
+    "bpc_stream_create_ex": (ctypes.c_int, [c_vp, c_i32, c_i32, c_i32, c_i32, c_i32, ctypes.POINTER(c_vp)]),
     "bpc_stream_start": (ctypes.c_int, [c_vp]),
     "bpc_stream_round": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_i64]),
     "bpc_stream_run": (ctypes.c_int, [c_vp, c_vp, c_i64, c_vp, c_vp, c_vp, c_i64]),
     "bpc_stream_stop": (ctypes.c_int, [c_vp]),
     "bpc_stream_status": (ctypes.c_int, [c_vp]),
+    "bpc_stream_layout": (ctypes.c_int, [c_vp]),
+    "bpc_stream_trace": (ctypes.c_int, [c_vp, c_i32]),
+    "bpc_stream_trace_read": (ctypes.c_int, [c_vp, c_vp, c_i64]),
     "bpc_stream_destroy": (None, [c_vp]),
     "bpc_noalloc_scratch_bytes": (ctypes.c_size_t, []),
 }

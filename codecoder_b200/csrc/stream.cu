@@ -78,7 +78,17 @@ struct StreamArgs {
   volatile uint8_t* req;
   volatile uint8_t* resp;
   uint64_t idle_ns, step_ns;
+  unsigned long long* trace;    // phase stamps of the rounds served, or null (off)
 };
+
+// Tracing: thread 0 of every CTA stamps the global timer at the phase boundaries of each step into
+// trace[CTA][step][k] (slot kTraceSlots - 1: the round's request, embedding and publication), overwritten round after
+// round, so that after a run the buffer holds the last round served.  Off (no stores) when the pointer is null.
+constexpr int kTraceCtas = 64, kTraceSlots = 16, kTraceK = 8;
+__device__ __forceinline__ void trace_stamp(const StreamArgs& a, int cta, int slot, int k) {
+  if (a.trace != nullptr && threadIdx.x == 0)
+    a.trace[(static_cast<int64_t>(cta) * kTraceSlots + slot) * kTraceK + k] = globaltimer_ns();
+}
 
 __device__ __forceinline__ uint64_t ld_volatile_u64(volatile const uint8_t* p) {
   return *reinterpret_cast<volatile const unsigned long long*>(p);
@@ -210,6 +220,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
   }
 
   while (!*cta_abort) {
+    trace_stamp(a, blockIdx.x, kTraceSlots - 1, 0);
     // ------------------------------------------------------------------ the next request (idle watchdog)
     // CTA 0 polls the host line, copies the detectors into device memory and releases the round on a device flag;
     // the other CTAs poll that flag in L2 (one reader of host memory instead of 64)
@@ -259,6 +270,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
     }
     __syncthreads();
     if (*s_cmd != kCmdRound) break;
+    trace_stamp(a, blockIdx.x, kTraceSlots - 1, 1);
     ++tag;
     for (int e = t; e < 2 * a.nh; e += kSThreads) s_new[e] = __ldcg(a.dev_req + e) & 1;
     __syncthreads();
@@ -291,7 +303,9 @@ __global__ void __launch_bounds__(kSThreads, 1)
           a.ring[(ty * a.W + (head + a.W - 1) % a.W) * a.nh + s] = s_new[e];
         }
     }
+    trace_stamp(a, blockIdx.x, kTraceSlots - 1, 2);
     if (!grid_sync(a, nbar++, cta_abort)) break;
+    trace_stamp(a, blockIdx.x, kTraceSlots - 1, 3);
     // ------------------------------------------------------------------ L check -> data and L - 1 data -> check steps
     bool failed = false;
     for (int step = 0; step < 2 * L - 1 && !failed; ++step) {
@@ -299,6 +313,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
       const bool c2d = (step & 1) == 0;
       const bool active = c2d ? has_c2d : has_d2c;
       const bool last = step == 2 * L - 2;
+      trace_stamp(a, blockIdx.x, step, 0);
       if (active) {
         const CUtensorMap* tm = c2d ? &tmHc : &tmHd;
         const int src = c2d ? src_c2d : src_d2c;
@@ -323,6 +338,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
         bool good = true;
         if (t == 0) {
           good = mbar_wait(smem_u32(full), ph_full, cta_abort, nullptr, a.step_ns);
+          trace_stamp(a, blockIdx.x, step, 1);
           if (good) {
             tc_fence_after();
             const uint64_t ad = sdesc_k_sw128(smem_u32(sA));
@@ -332,10 +348,12 @@ __global__ void __launch_bounds__(kSThreads, 1)
               tc_mma_ss(tmem_base, ad + ((k * 32) >> 4), bd + ((k * 32) >> 4), idesc, k ? 1u : 0u);
           }
           tc_commit(smem_u32(accf));
+          trace_stamp(a, blockIdx.x, step, 2);
         }
         ph_full ^= 1u;
         good = mbar_wait(smem_u32(accf), ph_acc, cta_abort, nullptr, a.step_ns) && good && !*cta_abort;
         ph_acc ^= 1u;
+        trace_stamp(a, blockIdx.x, step, 3);
         if (good) {
           tc_fence_after();
 #pragma unroll
@@ -372,6 +390,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
           }
         }
         ph_recv ^= 1u;
+        trace_stamp(a, blockIdx.x, step, 4);
         float sum[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) sum[e] = 0.f;
@@ -433,7 +452,9 @@ __global__ void __launch_bounds__(kSThreads, 1)
           *cta_abort = 1;
         }
       }
+      trace_stamp(a, blockIdx.x, step, 5);
       if (!grid_sync(a, nbar++, cta_abort)) failed = true;
+      trace_stamp(a, blockIdx.x, step, 6);
     }
     if (failed || *cta_abort) break;
     // ------------------------------------------------------------------ publish: results in 16-byte stores, then the tag
@@ -453,6 +474,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
         __threadfence_system();
       }
     }
+    trace_stamp(a, blockIdx.x, kTraceSlots - 1, 4);
     head = (head + 1) % a.W;
   }
   if (blockIdx.x == 0 && t == 0) {
@@ -473,6 +495,484 @@ __global__ void __launch_bounds__(kSThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// One-cluster layout: the whole round inside one thread-block cluster of 2 x (tiles per step) CTAs (16 at d = 17,
+// window 3), so that no step hand-off goes through an L2 flag.  CTA pair (tile, half) splits a tile's relations:
+// the low CTA gathers and multiplies relations 0-3, the high CTA relations 4-7, each into four TMEM accumulators (one
+// per relation, as the per-relation partials of the grid layout).  The low CTA adds its four in relation order and
+// pushes the 128 x 64 fp32 sum to the high CTA in one bulk shared -> distributed-shared copy; the high CTA adds its
+// own four to it in order -- the same fp32 sum, in the same order, as the grid layout's owner -- and runs the
+// epilogue (GELU, residual, head, XOR) for all 128 rows.  The relation matrices do not fit in shared memory for every
+// layer, so each step's four are loaded into one of two buffers while the step before runs.  Steps are separated by
+// a cluster barrier made of two alternating mbarriers that every CTA arrives on remotely (bounded waits, unlike the
+// hardware cluster barrier, so a CTA that gives up cannot leave its peers waiting forever); CTA 0 hands each round's
+// command and detectors to its peers with stores into their shared memory and one remote arrival each.
+constexpr int kQThreads = 256;
+constexpr int kQRel = 4;                                 // relations per CTA: a pair splits the 8
+constexpr int kQMaxCtas = 16;
+constexpr uint32_t kQWBuf = kQRel * kSWBytes;            // 32 KB: one step's four relation matrices
+constexpr uint32_t kQA = kQRel * kSABytes;               // 64 KB: four relations' gathered rows
+constexpr uint32_t kQX = kSRows * kSC * 4;               // 32 KB: fp32 sum of relations 0-3 for 128 rows
+constexpr uint32_t kQoW = 0;
+constexpr uint32_t kQoA = kQoW + 2 * kQWBuf;
+constexpr uint32_t kQoX = kQoA + kQA;
+constexpr uint32_t kQoIdx = kQoX + kQX;                  // int32 [step type][relation][row]
+constexpr uint32_t kQoLg = kQoIdx + 2 * kQRel * kSRows * 4;
+constexpr uint32_t kQoNew = kQoLg + kSRows * 8;          // the round's detectors (2 nh <= 1024 bytes)
+constexpr uint32_t kQoBar = kQoNew + 1024;
+constexpr int kQSmem = static_cast<int>(kQoBar) + 256 + 1024;
+
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr_cluster, uint4 v) {
+  asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr_cluster), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ void fence_acq_rel_cluster() { asm volatile("fence.acq_rel.cluster;" ::: "memory"); }
+
+// Bounded wait (cluster-scope acquire) on an mbarrier that takes remote arrivals: false after `limit_ns` or once any
+// CTA has set the kernel's abort flag.
+__device__ bool cl_wait(uint32_t bar, uint32_t parity, const int* abort_flag, uint64_t limit_ns) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((i & 31) == 31 && *reinterpret_cast<volatile const int*>(abort_flag)) return false;
+    if (globaltimer_ns() - t0 > limit_ns) return false;
+  }
+}
+
+// Cluster barrier: every CTA arrives on barrier `k & 1` of every CTA (lane j of warp 0 on CTA j's, after a
+// cluster-scope fence that orders this CTA's earlier writes, global and shared, before the peers' acquire), then
+// waits (bounded) on its own.  Two barriers alternate so that an arrival for the next step can never land in the
+// phase of this one.  False once this CTA or any other has given up.
+__device__ bool cl_sync(uint32_t bars2, uint32_t& phases, int& k, int nct, const StreamArgs& a,
+                        volatile int* cta_abort) {
+  tc_fence_before();
+  __syncthreads();
+  const int t = threadIdx.x;
+  const uint32_t bar = bars2 + 8 * (k & 1);
+  if (t < nct) {
+    fence_acq_rel_cluster();
+    mbar_arrive_remote(map_to_cta(bar, t));
+  }
+  if (t == 0 && !*cta_abort && !cl_wait(bar, (phases >> (k & 1)) & 1, a.abort_flag, a.step_ns)) {
+    atomicExch(a.abort_flag, 1);
+    *cta_abort = 1;
+  }
+  phases ^= 1u << (k & 1);
+  ++k;
+  __syncthreads();
+  tc_fence_after();
+  return !*cta_abort;
+}
+
+__global__ void __launch_bounds__(kQThreads, 1)
+    stream_cluster_kernel(const __grid_constant__ CUtensorMap tmWc, const __grid_constant__ CUtensorMap tmWd,
+                          const __grid_constant__ CUtensorMap tmHc, const __grid_constant__ CUtensorMap tmHd,
+                          const StreamArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint8_t* sW = smem + kQoW;
+  uint8_t* sA = smem + kQoA;
+  uint8_t* sX = smem + kQoX;
+  int32_t* sIdx = reinterpret_cast<int32_t*>(smem + kQoIdx);
+  float2* sLg = reinterpret_cast<float2*>(smem + kQoLg);
+  uint8_t* sNew = smem + kQoNew;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kQoBar);
+  const uint32_t b_wfull = smem_u32(bars);               // 2: the two weight buffers
+  const uint32_t b_full = smem_u32(bars + 2);            // 4: one per relation's gathered rows
+  const uint32_t b_acc = smem_u32(bars + 6);
+  const uint32_t b_recv = smem_u32(bars + 7);            // the high CTA's: the low CTA's sum arrived
+  const uint32_t b_step = smem_u32(bars + 8);            // 2: the alternating cluster barriers
+  const uint32_t b_go = smem_u32(bars + 10);             // CTA 0 handed over a command
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  volatile int* cta_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile uint32_t* s_cmd = reinterpret_cast<volatile uint32_t*>(tmem_slot + 2);
+
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int rank = static_cast<int>(cluster_ctarank());
+  const int nct = static_cast<int>(gridDim.x);           // the grid is one cluster
+  const int tile = rank >> 1, half = rank & 1;           // relations 4 half .. 4 half + 3 of tile `tile`
+  const int L = a.layers, S = 2 * L - 1;
+  const int nx = a.W * a.nh;
+  const bool has_c2d = tile < a.tiles_c2d;
+  const int c2d_begin = tile * kSRows, c2d_end = min(a.N_d, c2d_begin + kSRows);
+  const bool zt = tile >= a.tiles_x;
+  const bool has_d2c = tile < 2 * a.tiles_x;
+  const int d2c_begin = zt ? nx + (tile - a.tiles_x) * kSRows : tile * kSRows;
+  const int d2c_end = zt ? min(a.N_c, d2c_begin + kSRows) : min(nx, d2c_begin + kSRows);
+  // the epilogue's rows and channels: TMEM lane quarter warp % 4 (rows 32 (warp % 4) + lane), channel half warp / 4
+  const int row = 32 * (warp & 3) + lane, hh = warp >> 2;
+
+  // source rows of this CTA's four relations for both step types (pads and rows past the tile read the zero row
+  // past the map's end)
+  for (int e = t; e < 2 * kQRel * kSRows; e += kQThreads) {
+    const int ty = e / (kQRel * kSRows), j = (e / kSRows) % kQRel, rr = e % kSRows;
+    const bool c2d = ty == 0;
+    const int b = c2d ? c2d_begin : d2c_begin, en = c2d ? c2d_end : d2c_end, nsrc = c2d ? a.N_c : a.N_d;
+    int src = -1;
+    if ((c2d ? has_c2d : has_d2c) && b + rr < en)
+      src = __ldg((c2d ? a.c2d : a.d2c) + static_cast<int64_t>(b + rr) * kSRel + kQRel * half + j);
+    sIdx[e] = (src >= 0 && src < nsrc) ? src : nsrc;
+  }
+  if (t == 0) {
+    mbar_init(b_wfull, 1);
+    mbar_init(b_wfull + 8, 1);
+    for (int j = 0; j < kQRel; ++j) mbar_init(b_full + 8 * j, 1);
+    mbar_init(b_acc, 1);
+    mbar_init(b_recv, 1);
+    mbar_init(b_step, nct);
+    mbar_init(b_step + 8, nct);
+    mbar_init(b_go, 1);
+    if (half == 1) mbar_arrive_expect_tx(b_recv, kQX);   // armed for the first step; the partner sends after a barrier
+    *cta_abort = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmWc);
+    tma_prefetch_desc(&tmWd);
+    tma_prefetch_desc(&tmHc);
+    tma_prefetch_desc(&tmHd);
+  }
+  if (warp == 0) {
+    tmem_alloc(smem_u32(tmem_slot), 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_arrive_release();                              // every CTA's barriers exist before any remote arrival
+  cluster_wait_acquire();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  if (rank == 0 && t == 0) {
+    *reinterpret_cast<volatile uint32_t*>(a.resp + 8) = kStReady;
+    __threadfence_system();
+  }
+  auto active = [&](int step) { return (step & 1) == 0 ? has_c2d : has_d2c; };
+  // thread 0: the four relation matrices of `step` into weight buffer step % 2
+  auto load_w = [&](int step) {
+    const int l = step >> 1, b = step & 1;
+    const uint32_t dst = smem_u32(sW + b * kQWBuf), bar = b_wfull + 8 * b;
+    mbar_arrive_expect_tx(bar, kQWBuf);
+    for (int j = 0; j < kQRel; ++j) {
+      if ((step & 1) == 0)
+        tma_load_3d(dst + j * kSWBytes, &tmWc, 0, kQRel * half + j, l * kSC, bar);
+      else
+        tma_load_3d(dst + j * kSWBytes, &tmWd, 0, kQRel * half + j, (2 * l + (zt ? 1 : 0)) * kSC, bar);
+    }
+  };
+  uint32_t wph = 0, ph_full = 0, ph_acc = 0, ph_recv = 0, sph = 0, ph_go = 0;
+  int nsync = 0;
+  bool w_pending[2] = {false, false};                    // thread 0: weight loads not yet waited for
+  uint32_t drain_full = 0;                               // thread 0: 1 + the phase of gathers given up on
+  uint64_t tag = 0;
+  int head = 0;
+  const uint32_t idesc = idesc_bf16_f32(kSRows, kSC);
+  const int nchunk = (2 * a.nh + 15) / 16;
+
+  while (!*cta_abort) {
+    trace_stamp(a, rank, kTraceSlots - 1, 0);
+    // the first step's relation matrices do not depend on the round: load them while waiting for it
+    if (t == 0 && active(0)) {
+      load_w(0);
+      w_pending[0] = true;
+    }
+    // ------------------------------------------------------------------ the next request (idle watchdog)
+    if (rank == 0) {
+      if (t == 0) {
+        const uint64_t t0 = globaltimer_ns();
+        uint32_t cmd = kCmdStop;
+        while (true) {
+          const uint64_t v = ld_volatile_u64(a.req);
+          if (v == tag + 1) {
+            __threadfence_system();
+            cmd = *reinterpret_cast<volatile const uint32_t*>(a.req + 8);
+            break;
+          }
+          if (*reinterpret_cast<volatile int*>(a.abort_flag)) break;
+          if (globaltimer_ns() - t0 > a.idle_ns) {
+            *reinterpret_cast<volatile uint32_t*>(a.resp + 8) = kStIdle;
+            break;
+          }
+        }
+        *s_cmd = cmd;
+      }
+      __syncthreads();
+      if (*s_cmd == kCmdRound)
+        for (int e = t; e < nchunk; e += kQThreads)
+          reinterpret_cast<uint4*>(sNew)[e] = ld_volatile_u4(a.req + kReqDets + 16 * e);
+      __syncthreads();
+      // one thread per CTA: the command and the detectors into that CTA's shared memory, then its go arrival (the
+      // arrival releases this thread's stores)
+      if (t < nct) {
+        const uint32_t cmd = *s_cmd;
+        if (t != 0) {
+          if (cmd == kCmdRound)
+            for (int e = 0; e < nchunk; ++e)
+              st_cluster_v4(map_to_cta(smem_u32(sNew) + 16 * e, t), reinterpret_cast<const uint4*>(sNew)[e]);
+          st_cluster_u32(map_to_cta(smem_u32(const_cast<uint32_t*>(s_cmd)), t), cmd);
+        }
+        fence_acq_rel_cluster();
+        mbar_arrive_remote(map_to_cta(b_go, t));
+      }
+    }
+    if (t == 0 && !cl_wait(b_go, ph_go, a.abort_flag, a.idle_ns + 1000000000ull)) *s_cmd = kCmdStop;
+    ph_go ^= 1u;
+    __syncthreads();
+    if (*s_cmd != kCmdRound) break;
+    trace_stamp(a, rank, kTraceSlots - 1, 1);
+    ++tag;
+    // ------------------------------------------------------------------ embed the window and reset the residual
+    for (int g = rank * kQThreads + t; g < a.N_c * 8; g += nct * kQThreads) {
+      const int n = g >> 3, j = g & 7;
+      const int ty = n / nx, tt = (n / a.nh) % a.W, s = n % a.nh;
+      const uint8_t det = tt == a.W - 1 ? (sNew[ty * a.nh + s] & 1)
+                                        : (__ldcg(a.ring + (ty * a.W + (head + tt) % a.W) * a.nh + s) & 1);
+      reinterpret_cast<uint4*>(a.hc + static_cast<int64_t>(n) * kSC)[j] =
+          __ldg(reinterpret_cast<const uint4*>(a.embed + (2 * ty + det) * kSC) + j);
+      if (j == 0 && (n & 3) == 0) {
+        uint32_t w = 0;
+        for (int k = 0; k < 4 && n + k < a.N_c; ++k) {
+          const int m = n + k;
+          const int tym = m / nx, ttm = (m / a.nh) % a.W, sm = m % a.nh;
+          const uint8_t dm = ttm == a.W - 1 ? (sNew[tym * a.nh + sm] & 1)
+                                            : (__ldcg(a.ring + (tym * a.W + (head + ttm) % a.W) * a.nh + sm) & 1);
+          w |= static_cast<uint32_t>(dm) << (8 * k);
+        }
+        a.res[n >> 2] = w;
+      }
+    }
+    // the new round enters the ring (the newest slot of this window; no CTA reads it this round)
+    if (rank == 0)
+      for (int e = t; e < 2 * a.nh; e += kQThreads) {
+        const int ty = e / a.nh, s = e % a.nh;
+        a.ring[(ty * a.W + (head + a.W - 1) % a.W) * a.nh + s] = sNew[e] & 1;
+      }
+    trace_stamp(a, rank, kTraceSlots - 1, 2);
+    if (!cl_sync(b_step, sph, nsync, nct, a, cta_abort)) break;
+    trace_stamp(a, rank, kTraceSlots - 1, 3);
+    // ------------------------------------------------------------------ L check -> data and L - 1 data -> check steps
+    bool failed = false;
+    for (int step = 0; step < S && !failed; ++step) {
+      const int l = step >> 1;
+      const bool c2d = (step & 1) == 0;
+      const bool last = step == S - 1;
+      const bool next_w = step + 1 < S && active(step + 1);
+      trace_stamp(a, rank, step, 0);
+      if (active(step)) {
+        const CUtensorMap* tm = c2d ? &tmHc : &tmHd;
+        const int ob = c2d ? c2d_begin : d2c_begin, oe = c2d ? c2d_end : d2c_end;
+        __nv_bfloat16* y = c2d ? a.hd : a.hc;
+        const bool resid = !(c2d && l == 0);
+        const int on = ob + row;
+        const bool o_ok = on < oe;
+        // warp j < 4 gathers relation j's 128 source rows, four per lane
+        if (warp < kQRel) {
+          fence_proxy_async_global();                  // the gathers read what earlier steps stored
+          const int32_t* ix = sIdx + ((c2d ? 0 : 1) * kQRel + warp) * kSRows + 4 * lane;
+          if (lane == 0) mbar_arrive_expect_tx(b_full + 8 * warp, kSABytes);
+          __syncwarp();
+          tma_gather4(smem_u32(sA + warp * kSABytes + lane * 512), tm, 0, ix[0], ix[1], ix[2], ix[3],
+                      b_full + 8 * warp);
+        }
+        // the high CTA's residual rows (outputs of earlier steps, through L2)
+        uint4 res[4] = {};
+        if (half == 1 && resid && o_ok)
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            res[q] = __ldcg(reinterpret_cast<const uint4*>(y + static_cast<int64_t>(on) * kSC + 32 * hh) + q);
+        bool good = true;
+        if (t == 0) {
+          const int b = step & 1;
+          good = mbar_wait(b_wfull + 8 * b, (wph >> b) & 1, cta_abort, nullptr, a.step_ns);
+          trace_stamp(a, rank, step, 1);
+          wph ^= 1u << b;
+          if (good) w_pending[b] = false;
+          for (int j = 0; j < kQRel && good; ++j) {
+            good = mbar_wait(b_full + 8 * j, ph_full, cta_abort, nullptr, a.step_ns);
+            if (good) {
+              tc_fence_after();
+              const uint64_t ad = sdesc_k_sw128(smem_u32(sA + j * kSABytes));
+              const uint64_t bd = sdesc_k_sw128(smem_u32(sW + b * kQWBuf + j * kSWBytes));
+#pragma unroll
+              for (int k = 0; k < 4; ++k)
+                tc_mma_ss(tmem_base + 64 * j, ad + ((k * 32) >> 4), bd + ((k * 32) >> 4), idesc, k ? 1u : 0u);
+            }
+          }
+          trace_stamp(a, rank, step, 2);
+          tc_commit(b_acc);
+          if (!good) drain_full = ph_full + 1;         // gathers of this step may still be landing
+          // the next step's matrices go to the other buffer, whose last reader (the step before) has completed
+          if (next_w && good) {
+            load_w(step + 1);
+            w_pending[(step + 1) & 1] = true;
+          }
+        }
+        ph_full ^= 1u;
+        good = mbar_wait(b_acc, ph_acc, cta_abort, nullptr, a.step_ns) && good && !*cta_abort;
+        ph_acc ^= 1u;
+        trace_stamp(a, rank, step, 3);
+        tc_fence_after();
+        const uint32_t tl = tmem_base + (static_cast<uint32_t>(32 * (warp & 3)) << 16) + 32 * hh;
+        float s[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) s[e] = 0.f;
+        if (half == 0) {
+          // relations 0-3 added in order, as float4 chunks (channels 4c .. 4c + 3) of every row, to the partner
+#pragma unroll
+          for (int j = 0; j < kQRel; ++j) {
+            float v[32];
+            tmem_ld32(tl + 64 * j, v);
+#pragma unroll
+            for (int e = 0; e < 32; ++e) s[e] += v[e];
+          }
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            *reinterpret_cast<float4*>(sX + ((8 * hh + q) * kSRows + row) * 16) =
+                make_float4(s[4 * q], s[4 * q + 1], s[4 * q + 2], s[4 * q + 3]);
+          tc_fence_before();
+          fence_proxy_async_smem();
+          __syncthreads();
+          if (t == 0 && good)
+            bulk_s2cluster(map_to_cta(smem_u32(sX), rank + 1), smem_u32(sX), kQX, map_to_cta(b_recv, rank + 1));
+          trace_stamp(a, rank, step, 4);
+        } else {
+          const bool rec = cl_wait(b_recv, ph_recv, a.abort_flag, a.step_ns);
+          trace_stamp(a, rank, step, 4);
+          ph_recv ^= 1u;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 v = *reinterpret_cast<const float4*>(sX + ((8 * hh + q) * kSRows + row) * 16);
+            s[4 * q] = v.x;
+            s[4 * q + 1] = v.y;
+            s[4 * q + 2] = v.z;
+            s[4 * q + 3] = v.w;
+          }
+#pragma unroll
+          for (int j = 0; j < kQRel; ++j) {
+            float v[32];
+            tmem_ld32(tl + 64 * j, v);
+#pragma unroll
+            for (int e = 0; e < 32; ++e) s[e] += v[e];
+          }
+          uint32_t o[16];
+          const uint32_t* hres = reinterpret_cast<const uint32_t*>(res);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            uint64_t xv = gelu_tanh_fast2(f2_pack(s[2 * e], s[2 * e + 1]));
+            if (resid) xv = f2_add(xv, bf2_to_f2(hres[e]));
+            o[e] = f2_to_bf2(xv);
+          }
+          if (o_ok && rec)
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              reinterpret_cast<uint4*>(y + static_cast<int64_t>(on) * kSC + 32 * hh)[q] =
+                  make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+          if (last) {
+            // the head over 8-channel groups (pairs in order, then the two halves of each pair), the groups added
+            // as a tree: ((g0 + g1) + (g2 + g3)) + ((g4 + g5) + (g6 + g7)); this thread holds groups 4 hh .. 4 hh + 3
+            float p0[4], p1[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint64_t lg0 = 0, lg1 = 0;
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const uint64_t f = bf2_to_f2(o[4 * q + e]);
+                const int col = 32 * hh + 8 * q + 2 * e;
+                lg0 = f2_fma(f, *reinterpret_cast<const uint64_t*>(a.head_w + col), lg0);
+                lg1 = f2_fma(f, *reinterpret_cast<const uint64_t*>(a.head_w + kSC + col), lg1);
+              }
+              p0[q] = f2_lo(lg0) + f2_hi(lg0);
+              p1[q] = f2_lo(lg1) + f2_hi(lg1);
+            }
+            const float q0 = (p0[0] + p0[1]) + (p0[2] + p0[3]), q1 = (p1[0] + p1[1]) + (p1[2] + p1[3]);
+            if (hh == 1) sLg[row] = make_float2(q0, q1);
+            __syncthreads();
+            if (hh == 0 && o_ok && rec) {
+              const float2 u = sLg[row];
+              float l0 = q0 + u.x, l1 = q1 + u.y;
+              l0 += __ldg(a.head_b);
+              l1 += __ldg(a.head_b + 1);
+              const int newest = (a.W - 1) * a.nq;
+              if (on >= newest)
+                *reinterpret_cast<float2*>(a.dev_out + ((a.N_c + 15) & ~15) + static_cast<int64_t>(on - newest) * 8) =
+                    make_float2(l0, l1);
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const bool flip = (k >> 1) ? (l1 > 0.f) : (l0 > 0.f);
+                const int32_t cidx = __ldg(a.xor_nbr + static_cast<int64_t>(on) * 4 + k);
+                if (flip && cidx >= 0) atomicXor(a.res + (cidx >> 2), 1u << (8 * (cidx & 3)));
+              }
+            }
+          }
+          __syncthreads();                             // every thread is past its wait before the barrier is re-armed
+          if (t == 0) mbar_arrive_expect_tx(b_recv, kQX);
+          if (!rec) good = false;
+        }
+        if (!good) {
+          if (t == 0) atomicExch(a.abort_flag, 1);
+          *cta_abort = 1;
+        }
+      } else if (t == 0 && next_w) {
+        load_w(step + 1);
+        w_pending[(step + 1) & 1] = true;
+      }
+      trace_stamp(a, rank, step, 5);
+      if (!cl_sync(b_step, sph, nsync, nct, a, cta_abort)) failed = true;
+      trace_stamp(a, rank, step, 6);
+    }
+    if (failed || *cta_abort) break;
+    // ------------------------------------------------------------------ publish: results in 16-byte stores, then the tag
+    if (rank == 0) {
+      const int nres = (a.N_c + 15) / 16, nlg = (a.nq * 8 + 15) / 16;
+      volatile uint8_t* rp = a.resp + kRespData;
+      for (int e = t; e < nres + nlg; e += kQThreads) {
+        const uint4 v = e < nres ? __ldcg(reinterpret_cast<const uint4*>(a.res) + e)
+                                 : __ldcg(reinterpret_cast<const uint4*>(a.dev_out + ((a.N_c + 15) & ~15)) + (e - nres));
+        st_volatile_u4(rp + 16 * e, v);
+      }
+      __threadfence_system();
+      __syncthreads();
+      if (t == 0) {
+        *reinterpret_cast<volatile unsigned long long*>(a.resp) = tag;
+        __threadfence_system();
+      }
+    }
+    trace_stamp(a, rank, kTraceSlots - 1, 4);
+    head = (head + 1) % a.W;
+  }
+  if (rank == 0 && t == 0) {
+    const int ab = *reinterpret_cast<volatile int*>(a.abort_flag);
+    volatile uint32_t* st = reinterpret_cast<volatile uint32_t*>(a.resp + 8);
+    if (ab) *st = kStWatchdog;
+    else if (*st != kStIdle) *st = kStStopped;
+    __threadfence_system();
+  }
+  // copies into this CTA's shared memory still in flight land before it is given up (bounded): a weight load issued
+  // for a round that never came; after a watchdog, gathers given up on and the partner's sum
+  if (t == 0) {
+    const uint64_t t0 = globaltimer_ns();
+    for (int b = 0; b < 2; ++b)
+      if (w_pending[b])
+        while (!mbar_try_wait(b_wfull + 8 * b, (wph >> b) & 1) && globaltimer_ns() - t0 < 100000000ull) {
+        }
+    if (drain_full)
+      for (int j = 0; j < kQRel; ++j)
+        while (!mbar_try_wait(b_full + 8 * j, (drain_full - 1) & 1) && globaltimer_ns() - t0 < 100000000ull) {
+        }
+    if (half == 1 && *reinterpret_cast<volatile int*>(a.abort_flag))
+      while (!mbar_try_wait_cluster(b_recv, ph_recv) && globaltimer_ns() - t0 < 2000000ull) {
+      }
+  }
+  // every CTA is done with its peers' shared memory before any leaves
+  cluster_arrive_release();
+  cluster_wait_acquire();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 256);
+  }
+}
+
 }  // namespace
 }  // namespace bpc
 
@@ -490,6 +990,11 @@ struct bpc_stream {
   bool desynced = false;        // a round was given up before its response: later rounds fail until stop / start
   uint64_t tag = 0;
   int smem = 0;
+  int layout = BPC_STREAM_AUTO; // requested
+  unsigned long long* trace = nullptr;  // device trace buffer (part of dev)
+  bool tracing = false;
+  int running_layout = 0;       // the layout of the kernel that runs (or ran last)
+  int nct = 0;                  // CTAs of the one-cluster layout
 };
 
 namespace {
@@ -528,8 +1033,15 @@ volatile uint32_t* resp_status(bpc_stream* s) { return reinterpret_cast<volatile
 
 extern "C" int bpc_stream_create(const bpc_predecoder* h, int32_t window, int32_t nh, int32_t nq,
                                  int32_t idle_timeout_ms, bpc_stream** out) {
+  return bpc_stream_create_ex(h, window, nh, nq, idle_timeout_ms, BPC_STREAM_AUTO, out);
+}
+
+extern "C" int bpc_stream_create_ex(const bpc_predecoder* h, int32_t window, int32_t nh, int32_t nq,
+                                    int32_t idle_timeout_ms, int32_t layout, bpc_stream** out) {
   if (!h || !out) return fail(BPC_ERR_ARG, "null argument");
   *out = nullptr;
+  if (layout != BPC_STREAM_AUTO && layout != BPC_STREAM_CLUSTERS && layout != BPC_STREAM_ONE_CLUSTER)
+    return fail(BPC_ERR_ARG, "layout must be BPC_STREAM_AUTO, BPC_STREAM_CLUSTERS or BPC_STREAM_ONE_CLUSTER");
   bpc_predecoder_config c{};
   const void *embed, *wc, *wd;
   const float *hw, *hb;
@@ -547,6 +1059,8 @@ extern "C" int bpc_stream_create(const bpc_predecoder* h, int32_t window, int32_
     return fail(BPC_ERR_ARG, "the request or response does not fit its line");
   auto* s = new bpc_stream();
   s->pd = h;
+  s->layout = layout;
+  s->nct = 2 * std::max(tiles_c2d, 2 * tiles_x);
   StreamArgs& a = s->args;
   a.embed = static_cast<const __nv_bfloat16*>(embed);
   a.head_w = hw;
@@ -569,7 +1083,8 @@ extern "C" int bpc_stream_create(const bpc_predecoder* h, int32_t window, int32_
   const size_t o_bar = (o_res + ((a.N_c + 15) / 16) * 16 + 255) & ~size_t(255);
   const size_t o_req = o_bar + 256;
   const size_t o_out = o_req + 1024;
-  const size_t total = o_out + ((a.N_c + 15) & ~15) + static_cast<size_t>(nq) * 8 + 16;
+  const size_t o_trace = (o_out + ((a.N_c + 15) & ~15) + static_cast<size_t>(nq) * 8 + 16 + 255) & ~size_t(255);
+  const size_t total = o_trace + sizeof(unsigned long long) * kTraceCtas * kTraceSlots * kTraceK;
   auto bail = [&](int code, const std::string& msg) {
     bpc_stream_destroy(s);
     return fail(code, msg);
@@ -586,6 +1101,8 @@ extern "C" int bpc_stream_create(const bpc_predecoder* h, int32_t window, int32_
   a.round_flag = reinterpret_cast<unsigned long long*>(d + o_bar + 128);
   a.dev_req = d + o_req;
   a.dev_out = d + o_out;
+  s->trace = reinterpret_cast<unsigned long long*>(d + o_trace);
+  a.trace = nullptr;
   if (cudaHostAlloc(reinterpret_cast<void**>(&s->host), 65536, cudaHostAllocMapped) != cudaSuccess)
     return bail(BPC_ERR_LAUNCH, "cudaHostAlloc of the request / response lines failed");
   std::memset(s->host, 0, 65536);
@@ -607,16 +1124,71 @@ extern "C" int bpc_stream_create(const bpc_predecoder* h, int32_t window, int32_
   return 0;
 }
 
+namespace {
+
+int wait_ready(bpc_stream* s);
+
+// The one-cluster kernel, if a cluster of s->nct CTAs with its shared memory can be resident on this device:
+// 0 launched, 1 not possible here (nothing launched), otherwise an error code.
+int launch_one_cluster(bpc_stream* s, void** args) {
+  const void* fn = reinterpret_cast<const void*>(&stream_cluster_kernel);
+  if (s->nct > kQMaxCtas) return 1;
+  if (int e = allow_smem(fn, kQSmem)) return e;
+  if (s->nct > 8 && cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
+    cudaGetLastError();
+    return 1;
+  }
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3(s->nct);
+  lc.blockDim = dim3(kQThreads);
+  lc.dynamicSmemBytes = static_cast<size_t>(kQSmem);
+  lc.stream = s->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = s->nct;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  int max_clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&max_clusters, fn, &lc) != cudaSuccess || max_clusters < 1) {
+    cudaGetLastError();
+    return 1;
+  }
+  const cudaError_t le = cudaLaunchKernelExC(&lc, fn, args);
+  if (le != cudaSuccess)
+    return fail(BPC_ERR_LAUNCH, std::string("one-cluster stream kernel launch: ") + cudaGetErrorString(le));
+  return 0;
+}
+
+}  // namespace
+
 extern "C" int bpc_stream_start(bpc_stream* s) {
   if (!s) return fail(BPC_ERR_ARG, "null stream");
   if (s->running) return fail(BPC_ERR_ARG, "the stream kernel already runs");
-  if (int e = allow_smem(reinterpret_cast<const void*>(&stream_kernel), s->smem)) return e;
   std::memset(s->host, 0, 65536);
   s->tag = 0;
   s->desynced = false;
   if (cudaMemsetAsync(s->args.bar, 0, 256, s->stream) != cudaSuccess ||
       cudaMemsetAsync(s->args.ring, 0, 2 * s->args.W * s->args.nh, s->stream) != cudaSuccess)
     return fail(BPC_ERR_LAUNCH, "cudaMemsetAsync failed");
+  s->args.trace = s->tracing ? s->trace : nullptr;
+  if (s->tracing &&
+      cudaMemsetAsync(s->trace, 0, sizeof(unsigned long long) * kTraceCtas * kTraceSlots * kTraceK, s->stream) !=
+          cudaSuccess)
+    return fail(BPC_ERR_LAUNCH, "cudaMemsetAsync failed");
+  void* args[] = {&s->maps[0], &s->maps[1], &s->maps[2], &s->maps[3], &s->args};
+  // BPC_STREAM_AUTO runs the 8-cluster layout: measured faster on B200 (the one-cluster layout pulls four relations'
+  // gathered rows through each of its 16 SMs)
+  if (s->layout == BPC_STREAM_ONE_CLUSTER) {
+    const int e = launch_one_cluster(s, args);
+    if (e > 1) return e;
+    if (e == 1)
+      return fail(BPC_ERR_LAUNCH, "a cluster of " + std::to_string(s->nct) + " CTAs cannot be resident on this device");
+    s->running_layout = BPC_STREAM_ONE_CLUSTER;
+    return wait_ready(s);
+  }
+  if (int e = allow_smem(reinterpret_cast<const void*>(&stream_kernel), s->smem)) return e;
   // all 64 CTAs must be resident at once (the grid barrier waits for every one): a cooperative launch guarantees
   // it or fails
   cudaLaunchConfig_t lc = {};
@@ -633,7 +1205,6 @@ extern "C" int bpc_stream_start(bpc_stream* s) {
   attr[1].val.cooperative = 1;
   lc.attrs = attr;
   lc.numAttrs = 2;
-  void* args[] = {&s->maps[0], &s->maps[1], &s->maps[2], &s->maps[3], &s->args};
   cudaError_t le = cudaLaunchKernelExC(&lc, reinterpret_cast<const void*>(&stream_kernel), args);
   if (le != cudaSuccess) {
     // a cluster launch that cannot also be cooperative: launch plainly if the occupancy calculator confirms that
@@ -649,6 +1220,13 @@ extern "C" int bpc_stream_start(bpc_stream* s) {
     le = cudaLaunchKernelExC(&lc, reinterpret_cast<const void*>(&stream_kernel), args);
     if (le != cudaSuccess) return fail(BPC_ERR_LAUNCH, std::string("stream kernel launch: ") + cudaGetErrorString(le));
   }
+  s->running_layout = BPC_STREAM_CLUSTERS;
+  return wait_ready(s);
+}
+
+namespace {
+
+int wait_ready(bpc_stream* s) {
   s->running = true;
   // wait (bounded) for the kernel to report READY
   const auto t0 = std::chrono::steady_clock::now();
@@ -662,6 +1240,27 @@ extern "C" int bpc_stream_start(bpc_stream* s) {
       return fail(BPC_ERR_DEVICE, std::string("the stream kernel ended before ready: ") + cudaGetErrorString(q));
     }
   }
+  return 0;
+}
+
+}  // namespace
+
+extern "C" int bpc_stream_layout(const bpc_stream* s) { return s ? s->running_layout : -1; }
+
+extern "C" int bpc_stream_trace(bpc_stream* s, int32_t on) {
+  if (!s) return fail(BPC_ERR_ARG, "null stream");
+  if (s->running) return fail(BPC_ERR_ARG, "tracing is set before start");
+  s->tracing = on != 0;
+  return 0;
+}
+
+extern "C" int bpc_stream_trace_read(const bpc_stream* s, uint64_t* out, int64_t n) {
+  if (!s || !out) return fail(BPC_ERR_ARG, "null argument");
+  if (s->running) return fail(BPC_ERR_ARG, "the trace is read after stop");
+  const int64_t total = static_cast<int64_t>(kTraceCtas) * kTraceSlots * kTraceK;
+  if (n < total) return fail(BPC_ERR_SPACE, "the trace holds " + std::to_string(total) + " values");
+  if (cudaMemcpy(out, s->trace, sizeof(unsigned long long) * total, cudaMemcpyDeviceToHost) != cudaSuccess)
+    return fail(BPC_ERR_LAUNCH, "cudaMemcpy of the trace failed");
   return 0;
 }
 

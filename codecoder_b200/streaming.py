@@ -112,23 +112,32 @@ class StreamingDecoder:
 class PersistentStreamingDecoder:
     """The same sliding-window decoder served by one resident kernel (C ABI bpc_stream_*): rounds go in and results
     come out through a request line in mapped host memory, no launch per round.  bf16 networks with C = 64 and K = 8
-    (the d = 17 streaming workload); the kernel occupies 64 SMs while it runs and leaves after `idle_timeout_ms`
-    without a request, on stop(), or when a wait inside a round exceeds its watchdog.  Same bits as StreamingDecoder
+    (the d = 17 streaming workload).  `layout`: "one_cluster" (one thread-block cluster of two CTAs per 128-node tile,
+    16 SMs at d = 17, cluster barriers between the steps), "clusters" (8 clusters x 8 CTAs on 64 SMs, a grid barrier
+    between the steps) or "auto" (the first where its cluster can be resident).  The kernel leaves after
+    `idle_timeout_ms` without a request, on stop(), or when a wait inside a round exceeds its watchdog.  Same bits as StreamingDecoder
     (whose small-batch steps run the same relation-split arithmetic).  While it runs nothing may synchronise the
     whole device (torch.cuda.synchronize() would wait for the resident kernel until its idle limit): synchronise
     streams or events instead."""
 
-    def __init__(self, d: int, window: int, cfg, params, device="cuda", idle_timeout_ms: int = 5000):
+    LAYOUTS = {"auto": 0, "clusters": 1, "one_cluster": 2}
+
+    def __init__(self, d: int, window: int, cfg, params, device="cuda", idle_timeout_ms: int = 5000,
+                 layout: str = "auto", trace: bool = False):
         import ctypes
         from . import _lib
+        if layout not in self.LAYOUTS:
+            raise ValueError(f"layout must be one of {sorted(self.LAYOUTS)}")
         self.geo = g = RotatedSurface(d, window)
         self.pd = PreDecoder(g, cfg, params, device=device, chunk_shots=256)
         self.device = self.pd.device
         self.W, self.nh, self.nq = window, g.nh, g.n_data_round
         h = ctypes.c_void_p()
-        _lib.check(_lib.lib().bpc_stream_create(self.pd._h, window, g.nh, g.n_data_round, int(idle_timeout_ms),
-                                                ctypes.byref(h)), "bpc_stream_create")
+        _lib.check(_lib.lib().bpc_stream_create_ex(self.pd._h, window, g.nh, g.n_data_round, int(idle_timeout_ms),
+                                                   self.LAYOUTS[layout], ctypes.byref(h)), "bpc_stream_create_ex")
         self._s = h
+        if trace:
+            _lib.check(_lib.lib().bpc_stream_trace(h, 1), "bpc_stream_trace")
         self.residual = np.zeros(g.N_c, np.uint8)
         self.logits = np.zeros((self.nq, 2), np.float32)
         self.running = False
@@ -165,6 +174,46 @@ class PersistentStreamingDecoder:
     def status(self) -> int:
         from . import _lib
         return int(_lib.lib().bpc_stream_status(self._s))
+
+    def layout(self) -> str:
+        """The layout of the kernel that runs or ran last ("clusters", "one_cluster"; "" before the first start)."""
+        from . import _lib
+        return {1: "clusters", 2: "one_cluster"}.get(int(_lib.lib().bpc_stream_layout(self._s)), "")
+
+    PHASES = ("ready", "mma_issued", "accumulated", "exchanged", "epilogue", "barrier")
+
+    def trace(self) -> np.ndarray:
+        """After stop(), with trace=True: the global-timer stamps (ns) of the last round served, (64 CTAs, 16 slots,
+        8) int64 -- slots 0 .. 2L - 2 the steps (start, weights / gathered rows ready, MMAs issued, accumulators
+        ready, partials exchanged, epilogue done, past the barrier), slot 15 the round (waiting for the request,
+        accepted, window embedded, past the barrier, published); 0 where a CTA did not pass."""
+        from . import _lib
+        out = np.zeros((64, 16, 8), np.uint64)
+        _lib.check(_lib.lib().bpc_stream_trace_read(self._s, out.ctypes.data, out.size), "bpc_stream_trace_read")
+        return out.astype(np.int64)
+
+    def phase_table(self) -> dict:
+        """Per step of the last round served, the median over the CTAs that worked on it of each phase's duration in
+        ns (from the previous stamp; "barrier" from the end of the epilogue to past the barrier), and the step's
+        critical path (start of the step to past its barrier, the same on every CTA)."""
+        tr = self.trace()
+        steps = []
+        for st in range(2 * self.pd.cfg.layers - 1):
+            x = tr[:, st]
+            ok = (x[:, 0] > 0) & (x[:, 5] > 0) & (x[:, 3] > 0)
+            if not ok.any():
+                continue
+            y = x[ok]
+            d = np.diff(y[:, :7], axis=1)
+            steps.append({"step": st, **{p: float(np.median(d[:, i])) for i, p in enumerate(self.PHASES)},
+                          "total": float(np.median(y[:, 6] - y[:, 0])), "ctas": int(ok.sum())})
+        r = tr[:, 15]
+        r = r[r[:, 1] > 0]
+        rnd = {"embed": float(np.median(r[:, 2] - r[:, 1])), "embed_barrier": float(np.median(r[:, 3] - r[:, 2]))}
+        r0 = tr[0, 15]
+        if r0[4] > 0:
+            rnd["publish"] = float(r0[4] - tr[0, 2 * self.pd.cfg.layers - 2, 6])
+        return {"steps": steps, "round": rnd}
 
     def stop(self):
         from . import _lib

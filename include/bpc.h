@@ -259,13 +259,24 @@ BPC_API int bpc_predecoder_forward_noalloc(bpc_predecoder* h, const uint8_t* det
  * the round's detectors, a response with the same tag, a stop command, and watchdogs (an idle limit while waiting
  * for requests, a step limit on every wait inside a round) that end the kernel with a status instead of a hang.
  * Served networks: bf16, C = 64, K = 8, at most 8 layers, at most 8 tiles of 128 nodes per step (d = 17 with a
- * window of 3 rounds is 7 and 8).  The kernel occupies 64 SMs while it runs. */
+ * window of 3 rounds is 7 and 8).  Two layouts of the same arithmetic (the same bits):
+ *   BPC_STREAM_CLUSTERS     8 clusters x 8 CTAs (64 SMs), one relation per CTA, a bounded grid barrier per step;
+ *   BPC_STREAM_ONE_CLUSTER  one cluster of 2 x (tiles per step) CTAs (16 SMs at d = 17), a CTA pair per tile, bounded
+ *                           cluster barriers on mbarriers: no step hand-off through L2 flags;
+ *   BPC_STREAM_AUTO         the layout measured faster on B200: the 8 clusters (per step ~4.5 us against ~6 us; the
+ *                           one-cluster layout pulls four relations' gathered rows through each of its SMs). */
 typedef struct bpc_stream bpc_stream;
+#define BPC_STREAM_AUTO 0
+#define BPC_STREAM_CLUSTERS 1
+#define BPC_STREAM_ONE_CLUSTER 2
 
 /* The pre-decoder's tables and weights (device, not copied: keep h alive), the window and the detectors (nh per
  * check type) and data qubits (nq) per round.  Allocates the device state and the mapped lines. */
 BPC_API int bpc_stream_create(const bpc_predecoder* h, int32_t window, int32_t nh, int32_t nq, int32_t idle_timeout_ms,
                               bpc_stream** out);
+/* bpc_stream_create with a layout (BPC_STREAM_*); bpc_stream_create is BPC_STREAM_AUTO. */
+BPC_API int bpc_stream_create_ex(const bpc_predecoder* h, int32_t window, int32_t nh, int32_t nq,
+                                 int32_t idle_timeout_ms, int32_t layout, bpc_stream** out);
 /* Launches the resident kernel on the handle's own non-blocking stream and waits for it to report ready. */
 BPC_API int bpc_stream_start(bpc_stream* s);
 /* One round: round_dets (2 nh) host bytes, this round's X then Z detectors -> residual (N_c bytes) of the window and
@@ -281,6 +292,17 @@ BPC_API int bpc_stream_run(bpc_stream* s, const uint8_t* rounds, int64_t n_round
 BPC_API int bpc_stream_stop(bpc_stream* s);
 /* The kernel's status word: 0 starting, 1 ready / serving, 2 stopped, 3 watchdog fired, 4 idle limit reached. */
 BPC_API int bpc_stream_status(const bpc_stream* s);
+/* The layout of the kernel that runs or ran last (BPC_STREAM_CLUSTERS or BPC_STREAM_ONE_CLUSTER; 0 before the first
+ * start). */
+BPC_API int bpc_stream_layout(const bpc_stream* s);
+/* Tracing (set before bpc_stream_start): thread 0 of every CTA stamps the device global timer (ns) at the phase
+ * boundaries of each step, overwritten round after round.  bpc_stream_trace_read (after bpc_stream_stop) copies the
+ * stamps of the last round served: n >= 64 x 16 x 8 values, [CTA][slot][k]; slots 0 .. 2 L - 2 are the steps (k: 0
+ * start, 1 weights / gathered rows ready, 2 MMAs issued, 3 accumulators ready, 4 partials exchanged, 5 epilogue
+ * done, 6 past the barrier), slot 15 the round (0 waiting for the request, 1 request accepted, 2 window embedded, 3
+ * past the barrier, 4 response published); 0 where a CTA did not pass. */
+BPC_API int bpc_stream_trace(bpc_stream* s, int32_t on);
+BPC_API int bpc_stream_trace_read(const bpc_stream* s, uint64_t* out, int64_t n);
 BPC_API void bpc_stream_destroy(bpc_stream* s);
 
 /* Routing to a fallback decoder and its hand-off (the reference's decoder.route / decode and the router's matcher
