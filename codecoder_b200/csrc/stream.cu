@@ -139,7 +139,7 @@ __device__ __forceinline__ void fence_proxy_async_global() {
 __global__ void __launch_bounds__(kSThreads, 1)
     stream_kernel(const __grid_constant__ CUtensorMap tmWc, const __grid_constant__ CUtensorMap tmWd,
                   const __grid_constant__ CUtensorMap tmHc, const __grid_constant__ CUtensorMap tmHd,
-                  const StreamArgs a) {
+                  const __grid_constant__ CUtensorMap tmEmb, const StreamArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int L = a.layers;
@@ -156,7 +156,8 @@ __global__ void __launch_bounds__(kSThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4);
   volatile int* cta_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile uint32_t* s_cmd = reinterpret_cast<volatile uint32_t*>(tmem_slot + 2);
-  uint8_t* s_new = reinterpret_cast<uint8_t*>(bars + 8);   // the new round's detectors (2 nh bytes)
+  uint8_t* s_ring = reinterpret_cast<uint8_t*>(bars + 8);  // the window's detectors [type][ring slot][nh] (each CTA
+                                                          // keeps its own copy: no L2 reads to embed a round)
 
   const int t = threadIdx.x;
   const int warp = t >> 5, lane = t & 31;
@@ -174,6 +175,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
   const int src_c2d = (has_c2d && c2d_begin + t < c2d_end) ? __ldg(a.c2d + static_cast<int64_t>(c2d_begin + t) * kSRel + r) : -1;
   const int src_d2c = (has_d2c && d2c_begin + t < d2c_end) ? __ldg(a.d2c + static_cast<int64_t>(d2c_begin + t) * kSRel + r) : -1;
   const int orow = t >> 3;
+  for (int e = t; e < 2 * a.W * a.nh; e += kSThreads) s_ring[e] = 0;
 
   if (t == 0) {
     mbar_init(smem_u32(wfull), 1);
@@ -187,6 +189,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
     tma_prefetch_desc(&tmWd);
     tma_prefetch_desc(&tmHc);
     tma_prefetch_desc(&tmHd);
+    tma_prefetch_desc(&tmEmb);
   }
   if (warp == 0) {
     tmem_alloc(smem_u32(tmem_slot), 64);
@@ -218,6 +221,27 @@ __global__ void __launch_bounds__(kSThreads, 1)
     *reinterpret_cast<volatile uint32_t*>(a.resp + 8) = kStReady;
     __threadfence_system();
   }
+  // check node n of the window -> its detector (this CTA's copy of the window) and its embedding row 2 type + det
+  auto window_det = [&](int n) -> uint32_t {
+    const int ty = n / nx, tt = (n / a.nh) % a.W, sidx = n % a.nh;
+    return s_ring[(ty * a.W + (head + tt) % a.W) * a.nh + sidx];
+  };
+  auto window_token = [&](int n) -> int32_t { return 2 * (n / nx) + static_cast<int32_t>(window_det(n)); };
+  // this CTA's share of the stored window embedding (read by the data -> check steps' residuals and the later
+  // check -> data gathers) and of the residual words
+  auto embed_share = [&]() {
+    const int g = blockIdx.x * kSThreads + t;           // node g / 8, 16-byte chunk g % 8
+    const int n = g >> 3, j = g & 7;
+    if (n < a.N_c) {
+      reinterpret_cast<uint4*>(a.hc + static_cast<int64_t>(n) * kSC)[j] =
+          __ldg(reinterpret_cast<const uint4*>(a.embed + window_token(n) * kSC) + j);
+      if (j == 0 && (n & 3) == 0) {
+        uint32_t w = 0;
+        for (int k = 0; k < 4 && n + k < a.N_c; ++k) w |= window_det(n + k) << (8 * k);
+        a.res[n >> 2] = w;
+      }
+    }
+  };
 
   while (!*cta_abort) {
     trace_stamp(a, blockIdx.x, kTraceSlots - 1, 0);
@@ -272,40 +296,13 @@ __global__ void __launch_bounds__(kSThreads, 1)
     if (*s_cmd != kCmdRound) break;
     trace_stamp(a, blockIdx.x, kTraceSlots - 1, 1);
     ++tag;
-    for (int e = t; e < 2 * a.nh; e += kSThreads) s_new[e] = __ldcg(a.dev_req + e) & 1;
-    __syncthreads();
-    // ------------------------------------------------------------------ embed the window and reset the residual
-    {
-      const int g = blockIdx.x * kSThreads + t;         // node g / 8, 16-byte chunk g % 8
-      const int n = g >> 3, j = g & 7;
-      if (n < a.N_c) {
-        const int ty = n / nx, tt = (n / a.nh) % a.W, s = n % a.nh;
-        const uint8_t det = tt == a.W - 1 ? s_new[ty * a.nh + s]
-                                          : (__ldcg(a.ring + (ty * a.W + (head + tt) % a.W) * a.nh + s) & 1);
-        reinterpret_cast<uint4*>(a.hc + static_cast<int64_t>(n) * kSC)[j] =
-            __ldg(reinterpret_cast<const uint4*>(a.embed + (2 * ty + det) * kSC) + j);
-        if (j == 0 && (n & 3) == 0) {
-          uint32_t w = 0;
-          for (int k = 0; k < 4 && n + k < a.N_c; ++k) {
-            const int m = n + k;
-            const int tym = m / nx, ttm = (m / a.nh) % a.W, sm = m % a.nh;
-            const uint8_t dm = ttm == a.W - 1 ? s_new[tym * a.nh + sm]
-                                              : (__ldcg(a.ring + (tym * a.W + (head + ttm) % a.W) * a.nh + sm) & 1);
-            w |= static_cast<uint32_t>(dm) << (8 * k);
-          }
-          a.res[n >> 2] = w;
-        }
-      }
-      // the new round enters the ring (its slot is the newest in this window; no CTA reads it this round)
-      if (blockIdx.x == 0)
-        for (int e = t; e < 2 * a.nh; e += kSThreads) {
-          const int ty = e / a.nh, s = e % a.nh;
-          a.ring[(ty * a.W + (head + a.W - 1) % a.W) * a.nh + s] = s_new[e];
-        }
+    // the new round enters this CTA's copy of the window (its newest slot; the oldest round leaves)
+    for (int e = t; e < 2 * a.nh; e += kSThreads) {
+      const int ty = e / a.nh, sidx = e % a.nh;
+      s_ring[(ty * a.W + (head + a.W - 1) % a.W) * a.nh + sidx] = __ldcg(a.dev_req + e) & 1;
     }
+    __syncthreads();
     trace_stamp(a, blockIdx.x, kTraceSlots - 1, 2);
-    if (!grid_sync(a, nbar++, cta_abort)) break;
-    trace_stamp(a, blockIdx.x, kTraceSlots - 1, 3);
     // ------------------------------------------------------------------ L check -> data and L - 1 data -> check steps
     bool failed = false;
     for (int step = 0; step < 2 * L - 1 && !failed; ++step) {
@@ -315,17 +312,20 @@ __global__ void __launch_bounds__(kSThreads, 1)
       const bool last = step == 2 * L - 2;
       trace_stamp(a, blockIdx.x, step, 0);
       if (active) {
-        const CUtensorMap* tm = c2d ? &tmHc : &tmHd;
+        // the first step reads the embedded check nodes straight from the embedding table: row 2 type + det of the
+        // source node (a pad reads row 4, past the table: zeros); later steps read the stored features
+        const CUtensorMap* tm = step == 0 ? &tmEmb : c2d ? &tmHc : &tmHd;
         const int src = c2d ? src_c2d : src_d2c;
         const int nsrc = c2d ? a.N_c : a.N_d;
         fence_proxy_async_global();                    // the gathers read what earlier steps stored
-        const int32_t xr = (src >= 0 && src < nsrc) ? src : nsrc;
+        const int32_t xr = (src < 0 || src >= nsrc) ? (step == 0 ? 4 : nsrc) : step == 0 ? window_token(src) : src;
         const int q4 = lane & ~3;
         const int32_t i0 = __shfl_sync(0xffffffffu, xr, q4), i1 = __shfl_sync(0xffffffffu, xr, q4 + 1),
                       i2 = __shfl_sync(0xffffffffu, xr, q4 + 2), i3 = __shfl_sync(0xffffffffu, xr, q4 + 3);
         if (lane == 0) mbar_arrive_expect_tx(smem_u32(full), 32 * 128);
         __syncwarp();
         if ((lane & 3) == 0) tma_gather4(smem_u32(sA + t * 128), tm, 0, i0, i1, i2, i3, smem_u32(full));
+        if (step == 0) embed_share();                  // while the gathers run
         // the residual rows this thread owns (outputs of earlier steps)
         const int ob = c2d ? c2d_begin : d2c_begin, oe = c2d ? c2d_end : d2c_end;
         const int on = ob + r * 16 + orow;
@@ -451,6 +451,8 @@ __global__ void __launch_bounds__(kSThreads, 1)
           if (t == 0) atomicExch(a.abort_flag, 1);
           *cta_abort = 1;
         }
+      } else if (step == 0) {
+        embed_share();
       }
       trace_stamp(a, blockIdx.x, step, 5);
       if (!grid_sync(a, nbar++, cta_abort)) failed = true;
@@ -981,7 +983,7 @@ using namespace bpc;
 struct bpc_stream {
   const bpc_predecoder* pd = nullptr;
   StreamArgs args{};
-  CUtensorMap maps[4];
+  CUtensorMap maps[5];          // W_c2d, W_d2c, h_c rows, h_d rows, embedding rows
   uint8_t* host = nullptr;      // mapped: request at 0, response at kRespOff
   uint8_t* host_dev = nullptr;
   void* dev = nullptr;          // hc, hd, ring, res, barrier, abort
@@ -1055,7 +1057,8 @@ extern "C" int bpc_stream_create_ex(const bpc_predecoder* h, int32_t window, int
   const int tiles_c2d = (c.n_data + kSRows - 1) / kSRows, tiles_x = (window * nh + kSRows - 1) / kSRows;
   if (tiles_c2d > kSClusters || 2 * tiles_x > kSClusters)
     return fail(BPC_ERR_ARG, "the window is larger than 8 tiles of 128 nodes per step");
-  if (2 * nh > 1024 || 2 * nh + kReqDets > kRespOff || kRespData + ((c.n_checks + 15) & ~15) + nq * 8 > 65536 - kRespOff)
+  if (reinterpret_cast<uintptr_t>(embed) & 15) return fail(BPC_ERR_ARG, "the embedding table is not 16-byte aligned");
+  if (2 * window * nh > 2048 || 2 * nh > 1024 || 2 * nh + kReqDets > kRespOff || kRespData + ((c.n_checks + 15) & ~15) + nq * 8 > 65536 - kRespOff)
     return fail(BPC_ERR_ARG, "the request or response does not fit its line");
   auto* s = new bpc_stream();
   s->pd = h;
@@ -1113,11 +1116,12 @@ extern "C" int bpc_stream_create_ex(const bpc_predecoder* h, int32_t window, int
   int e = 0;
   if ((e = map3(&s->maps[0], wc, kSC, kSRel, static_cast<cuuint64_t>(kSC) * c.layers, kSC)) ||
       (e = map3(&s->maps[1], wd, kSC, kSRel, static_cast<cuuint64_t>(kSC) * 2 * c.layers, kSC)) ||
-      (e = rows2(&s->maps[2], a.hc, a.N_c)) || (e = rows2(&s->maps[3], a.hd, a.N_d))) {
+      (e = rows2(&s->maps[2], a.hc, a.N_c)) || (e = rows2(&s->maps[3], a.hd, a.N_d)) ||
+      (e = rows2(&s->maps[4], embed, 4))) {
     bpc_stream_destroy(s);
     return e;
   }
-  s->smem = 1024 + 2 * c.layers * kSWBytes + kSABytes + 2 * kSPart + 64 + 1024;
+  s->smem = 1024 + 2 * c.layers * kSWBytes + kSABytes + 2 * kSPart + 64 + 2048;
   if (cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking) != cudaSuccess)
     return bail(BPC_ERR_LAUNCH, "cudaStreamCreate failed");
   *out = s;
@@ -1177,10 +1181,10 @@ extern "C" int bpc_stream_start(bpc_stream* s) {
       cudaMemsetAsync(s->trace, 0, sizeof(unsigned long long) * kTraceCtas * kTraceSlots * kTraceK, s->stream) !=
           cudaSuccess)
     return fail(BPC_ERR_LAUNCH, "cudaMemsetAsync failed");
-  void* args[] = {&s->maps[0], &s->maps[1], &s->maps[2], &s->maps[3], &s->args};
   // BPC_STREAM_AUTO runs the 8-cluster layout: measured faster on B200 (the one-cluster layout pulls four relations'
   // gathered rows through each of its 16 SMs)
   if (s->layout == BPC_STREAM_ONE_CLUSTER) {
+    void* args[] = {&s->maps[0], &s->maps[1], &s->maps[2], &s->maps[3], &s->args};
     const int e = launch_one_cluster(s, args);
     if (e > 1) return e;
     if (e == 1)
@@ -1189,6 +1193,7 @@ extern "C" int bpc_stream_start(bpc_stream* s) {
     return wait_ready(s);
   }
   if (int e = allow_smem(reinterpret_cast<const void*>(&stream_kernel), s->smem)) return e;
+  void* args[] = {&s->maps[0], &s->maps[1], &s->maps[2], &s->maps[3], &s->maps[4], &s->args};
   // all 64 CTAs must be resident at once (the grid barrier waits for every one): a cooperative launch guarantees
   // it or fails
   cudaLaunchConfig_t lc = {};

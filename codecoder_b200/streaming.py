@@ -209,7 +209,9 @@ class PersistentStreamingDecoder:
                           "total": float(np.median(y[:, 6] - y[:, 0])), "ctas": int(ok.sum())})
         r = tr[:, 15]
         r = r[r[:, 1] > 0]
-        rnd = {"embed": float(np.median(r[:, 2] - r[:, 1])), "embed_barrier": float(np.median(r[:, 3] - r[:, 2]))}
+        rnd = {"embed": float(np.median(r[:, 2] - r[:, 1]))}
+        if (r[:, 3] > 0).all():                          # a barrier after the embedding (one-cluster layout)
+            rnd["embed_barrier"] = float(np.median(r[:, 3] - r[:, 2]))
         r0 = tr[0, 15]
         if r0[4] > 0:
             rnd["publish"] = float(r0[4] - tr[0, 2 * self.pd.cfg.layers - 2, 6])

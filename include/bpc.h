@@ -299,8 +299,9 @@ BPC_API int bpc_stream_layout(const bpc_stream* s);
  * boundaries of each step, overwritten round after round.  bpc_stream_trace_read (after bpc_stream_stop) copies the
  * stamps of the last round served: n >= 64 x 16 x 8 values, [CTA][slot][k]; slots 0 .. 2 L - 2 are the steps (k: 0
  * start, 1 weights / gathered rows ready, 2 MMAs issued, 3 accumulators ready, 4 partials exchanged, 5 epilogue
- * done, 6 past the barrier), slot 15 the round (0 waiting for the request, 1 request accepted, 2 window embedded, 3
- * past the barrier, 4 response published); 0 where a CTA did not pass. */
+ * done, 6 past the barrier), slot 15 the round (0 waiting for the request, 1 request accepted, 2 window embedded --
+ * in the 8-cluster layout the window's detectors taken in, the embedding overlapping the first step --, 3 past the
+ * barrier after the embedding (one-cluster layout), 4 response published); 0 where a CTA did not pass. */
 BPC_API int bpc_stream_trace(bpc_stream* s, int32_t on);
 BPC_API int bpc_stream_trace_read(const bpc_stream* s, uint64_t* out, int64_t n);
 BPC_API void bpc_stream_destroy(bpc_stream* s);
