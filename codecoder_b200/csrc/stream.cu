@@ -1,7 +1,8 @@
 // Persistent streaming pre-decoder (sliding window of W rounds, batch 1, C = 64, K = 8): one resident kernel that
 // serves rounds through a request line in mapped host memory, the protocol of the reference's persistent kernel
 // (evaluation/timing/d7/kernel.cu:310-369,440-527; router.cc:170-223,576-650): the host writes a round's detectors
-// and a tag, the kernel publishes the round's residual syndrome and the newest round's X/Z logits with the same tag,
+// tagged with its sequence number -- in every 8-byte word of the line, as the reference's request tags every word
+// (poll_k) -- the kernel publishes the round's residual syndrome and the newest round's X/Z logits with the same tag,
 // a stop command or an idle watchdog ends the kernel, and a step watchdog turns any wait that never completes into
 // an error status instead of a hang.
 //
@@ -13,11 +14,13 @@
 // epilogue (GELU, residual, head, XOR) for its 16 rows -- the arithmetic of gmm_nodes_split_kernel.  Activations live
 // in device memory (L2); a bounded grid barrier separates the steps.
 //
-// A round: wait for the request; embed the window's check nodes (a device ring holds the W - 1 older rounds, the
-// new round comes from the request line); L check -> data steps and L - 1 data -> check steps (the last layer's
-// data -> check step does not reach the outputs); the last check -> data step writes the newest round's logits to
-// the response and XORs the predicted flips into the residual; CTA 0 copies the residual to the response and
-// releases the tag.
+// A round: CTA 0 takes the request and hands the detectors to the others through L2; every CTA keeps its own copy of
+// the window's detectors in shared memory.  L check -> data steps and L - 1 data -> check steps follow (the last
+// layer's data -> check step does not reach the outputs).  The first step gathers its source rows straight from the
+// embedding table by detector token, while the CTAs store the window's embedding for the later steps.  The last
+// check -> data step writes the newest round's logits and XORs the predicted flips into the residual; CTA 0 copies
+// the residual and the logits to the response and releases the tag.  A one-cluster layout of the same arithmetic
+// follows the grid kernel below.
 #include <algorithm>
 #include <atomic>
 #include <chrono>
@@ -45,9 +48,12 @@ constexpr uint32_t kSABytes = kSRows * 128;          // gathered rows
 constexpr uint32_t kSSlot = 16 * kSC * 4;            // one owner's block of a partial (16 rows x 64 fp32)
 constexpr uint32_t kSPart = kSRel * kSSlot;          // 32 KB
 
-// Request / response lines in mapped host memory.
-constexpr int kReqDets = 64;                         // request: u64 tag, u32 cmd, then the detectors at byte 64
-constexpr int kRespOff = 4096;                       // response: u64 tag, u32 status, then residual, logits
+// Request / response lines in mapped host memory.  Request: 8-byte words, word w = detectors 4w .. 4w + 3 (low half)
+// and the round's sequence number (high half: 31 bits, bit 31 = stop), each word written and read whole, so that
+// every word carries its own validity and one read of the line both finds a new round and delivers it.
+// Response: u64 tag, u32 status, then residual, logits.
+constexpr uint32_t kSeqMask = 0x7fffffffu, kSeqStop = 0x80000000u;
+constexpr int kRespOff = 4096;
 constexpr int kRespData = 64;
 
 enum : uint32_t { kCmdRound = 0, kCmdStop = 1 };
@@ -130,6 +136,36 @@ __device__ bool grid_sync(const StreamArgs& a, unsigned long long n, volatile in
   }
   __syncthreads();
   return !*cta_abort;
+}
+
+// The next request, read by every thread of one CTA (each polls its words of the line, see above): the detector words
+// go to dst (4 bytes each).  Returns kCmdRound, or kCmdStop on a stop command, once another CTA gave up, or after the
+// idle limit (then the status word says idle).  Every thread of the CTA calls it; it ends past a CTA barrier.
+__device__ uint32_t take_request(const StreamArgs& a, uint64_t tag, uint32_t* dst) {
+  const uint32_t want = static_cast<uint32_t>(tag + 1) & kSeqMask;
+  const int nw = (2 * a.nh + 3) / 4;
+  int got = 1, stop = 0;
+  const uint64_t t0 = globaltimer_ns();
+  for (int w = threadIdx.x; w < nw; w += blockDim.x) {
+    int ok = 0;
+    while (true) {
+      const uint64_t v = ld_volatile_u64(a.req + 8 * w);
+      const uint32_t hi = static_cast<uint32_t>(v >> 32);
+      if ((hi & kSeqMask) == want) {
+        ok = 1;
+        stop |= (hi & kSeqStop) ? 1 : 0;
+        dst[w] = static_cast<uint32_t>(v);
+        break;
+      }
+      if (*reinterpret_cast<volatile const int*>(a.abort_flag) || globaltimer_ns() - t0 > a.idle_ns) break;
+    }
+    got &= ok;
+  }
+  const int all = __syncthreads_and(got);
+  const int any_stop = __syncthreads_or(stop);
+  if (!all && threadIdx.x == 0 && !*reinterpret_cast<volatile const int*>(a.abort_flag))
+    *reinterpret_cast<volatile uint32_t*>(a.resp + 8) = kStIdle;
+  return all && !any_stop ? kCmdRound : kCmdStop;
 }
 
 __device__ __forceinline__ void fence_proxy_async_global() {
@@ -249,28 +285,8 @@ __global__ void __launch_bounds__(kSThreads, 1)
     // CTA 0 polls the host line, copies the detectors into device memory and releases the round on a device flag;
     // the other CTAs poll that flag in L2 (one reader of host memory instead of 64)
     if (blockIdx.x == 0) {
-      if (t == 0) {
-        const uint64_t t0 = globaltimer_ns();
-        uint32_t cmd = kCmdStop;
-        while (true) {
-          const uint64_t v = ld_volatile_u64(a.req);
-          if (v == tag + 1) {
-            __threadfence_system();
-            cmd = *reinterpret_cast<volatile const uint32_t*>(a.req + 8);
-            break;
-          }
-          if (*reinterpret_cast<volatile int*>(a.abort_flag)) break;
-          if (globaltimer_ns() - t0 > a.idle_ns) {
-            *reinterpret_cast<volatile uint32_t*>(a.resp + 8) = kStIdle;
-            break;
-          }
-        }
-        *s_cmd = cmd;
-      }
-      __syncthreads();
-      if (*s_cmd == kCmdRound)
-        for (int e = t; e < (2 * a.nh + 15) / 16; e += kSThreads)
-          reinterpret_cast<uint4*>(a.dev_req)[e] = ld_volatile_u4(a.req + kReqDets + 16 * e);
+      const uint32_t cmd = take_request(a, tag, reinterpret_cast<uint32_t*>(a.dev_req));
+      if (t == 0) *s_cmd = cmd;
       __syncthreads();
       if (t == 0) {
         __threadfence();
@@ -471,10 +487,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
       }
       __threadfence_system();
       __syncthreads();
-      if (t == 0) {
-        *reinterpret_cast<volatile unsigned long long*>(a.resp) = tag;
-        __threadfence_system();
-      }
+      if (t == 0) *reinterpret_cast<volatile unsigned long long*>(a.resp) = tag;
     }
     trace_stamp(a, blockIdx.x, kTraceSlots - 1, 4);
     head = (head + 1) % a.W;
@@ -679,28 +692,8 @@ __global__ void __launch_bounds__(kQThreads, 1)
     }
     // ------------------------------------------------------------------ the next request (idle watchdog)
     if (rank == 0) {
-      if (t == 0) {
-        const uint64_t t0 = globaltimer_ns();
-        uint32_t cmd = kCmdStop;
-        while (true) {
-          const uint64_t v = ld_volatile_u64(a.req);
-          if (v == tag + 1) {
-            __threadfence_system();
-            cmd = *reinterpret_cast<volatile const uint32_t*>(a.req + 8);
-            break;
-          }
-          if (*reinterpret_cast<volatile int*>(a.abort_flag)) break;
-          if (globaltimer_ns() - t0 > a.idle_ns) {
-            *reinterpret_cast<volatile uint32_t*>(a.resp + 8) = kStIdle;
-            break;
-          }
-        }
-        *s_cmd = cmd;
-      }
-      __syncthreads();
-      if (*s_cmd == kCmdRound)
-        for (int e = t; e < nchunk; e += kQThreads)
-          reinterpret_cast<uint4*>(sNew)[e] = ld_volatile_u4(a.req + kReqDets + 16 * e);
+      const uint32_t cmd = take_request(a, tag, reinterpret_cast<uint32_t*>(sNew));
+      if (t == 0) *s_cmd = cmd;
       __syncthreads();
       // one thread per CTA: the command and the detectors into that CTA's shared memory, then its go arrival (the
       // arrival releases this thread's stores)
@@ -933,10 +926,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
       }
       __threadfence_system();
       __syncthreads();
-      if (t == 0) {
-        *reinterpret_cast<volatile unsigned long long*>(a.resp) = tag;
-        __threadfence_system();
-      }
+      if (t == 0) *reinterpret_cast<volatile unsigned long long*>(a.resp) = tag;
     }
     trace_stamp(a, rank, kTraceSlots - 1, 4);
     head = (head + 1) % a.W;
@@ -1027,7 +1017,19 @@ int rows2(CUtensorMap* m, const void* base, int64_t rows) {
   return r == CUDA_SUCCESS ? 0 : fail(BPC_ERR_DRIVER, "cuTensorMapEncodeTiled failed: " + std::to_string(int(r)));
 }
 
-volatile uint64_t* req_tag(bpc_stream* s) { return reinterpret_cast<volatile uint64_t*>(s->host); }
+// The request for sequence number s->tag: every word of the line written whole (aligned 8-byte stores), in any
+// order -- each word carries the sequence number, so the kernel takes a word only once it is the new round's.
+void write_request(bpc_stream* s, const uint8_t* dets, bool stop) {
+  const uint32_t seq = (static_cast<uint32_t>(s->tag) & kSeqMask) | (stop ? kSeqStop : 0u);
+  const int n = 2 * s->args.nh, nw = (n + 3) / 4;
+  volatile uint64_t* line = reinterpret_cast<volatile uint64_t*>(s->host);
+  for (int w = 0; w < nw; ++w) {
+    uint32_t d = 0;
+    if (dets)
+      for (int k = 0; k < 4 && 4 * w + k < n; ++k) d |= static_cast<uint32_t>(dets[4 * w + k]) << (8 * k);
+    line[w] = (static_cast<uint64_t>(seq) << 32) | d;
+  }
+}
 volatile uint64_t* resp_tag(bpc_stream* s) { return reinterpret_cast<volatile uint64_t*>(s->host + kRespOff); }
 volatile uint32_t* resp_status(bpc_stream* s) { return reinterpret_cast<volatile uint32_t*>(s->host + kRespOff + 8); }
 
@@ -1058,7 +1060,7 @@ extern "C" int bpc_stream_create_ex(const bpc_predecoder* h, int32_t window, int
   if (tiles_c2d > kSClusters || 2 * tiles_x > kSClusters)
     return fail(BPC_ERR_ARG, "the window is larger than 8 tiles of 128 nodes per step");
   if (reinterpret_cast<uintptr_t>(embed) & 15) return fail(BPC_ERR_ARG, "the embedding table is not 16-byte aligned");
-  if (2 * window * nh > 2048 || 2 * nh > 1024 || 2 * nh + kReqDets > kRespOff || kRespData + ((c.n_checks + 15) & ~15) + nq * 8 > 65536 - kRespOff)
+  if (2 * window * nh > 2048 || 2 * nh > 1024 || 8 * ((2 * nh + 3) / 4) > kRespOff || kRespData + ((c.n_checks + 15) & ~15) + nq * 8 > 65536 - kRespOff)
     return fail(BPC_ERR_ARG, "the request or response does not fit its line");
   auto* s = new bpc_stream();
   s->pd = h;
@@ -1276,12 +1278,8 @@ extern "C" int bpc_stream_round(bpc_stream* s, const uint8_t* round_dets, uint8_
   if (s->desynced)
     return fail(BPC_ERR_DEVICE, "an earlier round timed out before its response; stop and start the stream again");
   const StreamArgs& a = s->args;
-  volatile uint8_t* dst = s->host + kReqDets;
-  for (int i = 0; i < 2 * a.nh; ++i) dst[i] = round_dets[i];
-  *reinterpret_cast<volatile uint32_t*>(s->host + 8) = kCmdRound;
-  std::atomic_thread_fence(std::memory_order_release);
   const uint64_t tag = ++s->tag;
-  *req_tag(s) = tag;
+  write_request(s, round_dets, false);
   const auto t0 = std::chrono::steady_clock::now();
   while (*resp_tag(s) != tag) {
     const uint32_t st = *resp_status(s);
@@ -1320,9 +1318,8 @@ extern "C" int bpc_stream_run(bpc_stream* s, const uint8_t* rounds, int64_t n_ro
 extern "C" int bpc_stream_stop(bpc_stream* s) {
   if (!s) return fail(BPC_ERR_ARG, "null stream");
   if (!s->running) return 0;
-  *reinterpret_cast<volatile uint32_t*>(s->host + 8) = kCmdStop;
-  std::atomic_thread_fence(std::memory_order_release);
-  *req_tag(s) = ++s->tag;
+  ++s->tag;
+  write_request(s, nullptr, true);
   const auto t0 = std::chrono::steady_clock::now();
   cudaError_t q;
   while ((q = cudaStreamQuery(s->stream)) == cudaErrorNotReady) {
