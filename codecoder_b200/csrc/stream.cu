@@ -116,18 +116,20 @@ __device__ __forceinline__ void st_volatile_u4(volatile void* p, uint4 v) {
 
 // Bounded grid barrier over every CTA of the grid: `n` is the number of barriers passed so far (the counter only
 // grows).  Returns false after the step watchdog or when another CTA gave up.
+// The arrival is a release reduction (it orders the CTA's earlier writes, seen through the CTA barrier, before the
+// count); the poll is one acquire load per iteration, the abort flag read only every 32nd (an acquire load holds
+// back every later load, so a flag read each time would add a second L2 round trip to each poll).
 __device__ bool grid_sync(const StreamArgs& a, unsigned long long n, volatile int* cta_abort) {
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence();
-    atomicAdd(a.bar, 1ull);
+    asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(a.bar) : "memory");
     const unsigned long long target = (n + 1) * gridDim.x;
     const uint64_t t0 = globaltimer_ns();
-    while (true) {
+    for (uint32_t i = 0;; ++i) {
       unsigned long long v;
       asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(a.bar) : "memory");
       if (v >= target) break;
-      if (*reinterpret_cast<volatile int*>(a.abort_flag) || globaltimer_ns() - t0 > a.step_ns) {
+      if (((i & 31) == 31 && *reinterpret_cast<volatile int*>(a.abort_flag)) || globaltimer_ns() - t0 > a.step_ns) {
         atomicExch(a.abort_flag, 1);
         *cta_abort = 1;
         break;
@@ -296,14 +298,14 @@ __global__ void __launch_bounds__(kSThreads, 1)
     } else if (t == 0) {
       const uint64_t t0 = globaltimer_ns();
       uint32_t cmd = kCmdStop;
-      while (true) {
+      for (uint32_t i = 0;; ++i) {
         unsigned long long v;
         asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(a.round_flag) : "memory");
         if (v == tag + 1) {
           cmd = kCmdRound;
           break;
         }
-        if (v == kStopFlag || *reinterpret_cast<volatile int*>(a.abort_flag)) break;
+        if (v == kStopFlag || ((i & 31) == 31 && *reinterpret_cast<volatile int*>(a.abort_flag))) break;
         if (globaltimer_ns() - t0 > a.idle_ns + 1000000000ull) break;   // CTA 0 gives up first
       }
       *s_cmd = cmd;
