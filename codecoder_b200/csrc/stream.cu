@@ -386,9 +386,10 @@ __global__ void __launch_bounds__(kSThreads, 1)
         }
         tc_fence_before();
         fence_proxy_async_smem();
-        __syncthreads();
-        if (t == 0) {
-          for (int jj = 0; jj < kSRel; ++jj)
+        __syncwarp();
+        // warp w staged the rows of owners 2w and 2w + 1: it sends them at once, without waiting for the other warps
+        if (lane == 0) {
+          for (int jj = 2 * warp; jj < 2 * warp + 2; ++jj)
             bulk_s2cluster(map_to_cta(smem_u32(sR + r * kSSlot), jj), smem_u32(sO + jj * kSSlot), kSSlot,
                            map_to_cta(smem_u32(recv), jj));
           bulk_commit();
@@ -463,7 +464,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
             }
           }
         }
-        if (t == 0) bulk_wait_read();                  // sO is free for the next step
+        if (lane == 0) bulk_wait_read();               // sO is free for the next step
         if (t == 0) mbar_arrive_expect_tx(smem_u32(recv), kSPart);   // re-armed before the peers' next copies
         if (!rec || !good) {
           if (t == 0) atomicExch(a.abort_flag, 1);
