@@ -477,8 +477,8 @@ def main():
     pk = peaks()
     achieved = tc_flops / (tc_ms / 1000.0) / 1e12
     fps = flops_per_shot(cfg, g.N_c, g.N_d)
-    step_kernel = "gmm_pair_kernel" if (cfg.channels == 128 and os.environ.get("BPC_STEP_KERNEL") == "pair") \
-        else "gmm_wide_kernel"
+    step_kernel = "gmm_pair_kernel" if (cfg.channels == 128 and os.environ.get("BPC_STEP_KERNEL") in
+                                        ("pair", "pair_stream")) else "gmm_wide_kernel"
     roof = {"bound": "tensor", "kernel": f"{step_kernel} (bipartite step)", "achieved": achieved,
             "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s", "frac": achieved / pk["bf16_tflops_sustained"],
             "peak_kind": f"{pk['source']} sustained bf16 (cuBLAS)", "traffic": None,

@@ -275,6 +275,15 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar_cluster)
       : "memory");
 }
+// The 3D form of tma_load_2d_pair.
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap* map, int32_t c0, int32_t c1,
+                                                 int32_t c2, uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
+      "%4}], [%5];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar_cluster)
+      : "memory");
+}
 // Arrive on an mbarrier of another CTA of the cluster (release at cluster scope: this thread's earlier writes,
 // shared::cluster stores included, are visible to a cluster-scope acquire that sees the phase complete).
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t bar_cluster) {

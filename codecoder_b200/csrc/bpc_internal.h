@@ -87,11 +87,13 @@ int gmm_nodes_launch(const GmmProblem& p, int* status, uint64_t timeout_ns, cuda
 // CTA-pair tcgen05 path (cta_group::2) for blocked hidden-128 steps with GELU epilogues (optionally the head) and
 // at most 8 relations: W halves resident in shared memory, activations in the blocked layout with 128-shot blocks
 // (gmm_pair_tile_shots()).  type_order: for two weight types, the targets in processing order grouped by type
-// (n_type0 of type 0 first); counters: two device words the launch clears.
+// (n_type0 of type 0 first); counters: two device words the launch clears.  stream_w: the W halves are not resident
+// but stream with the activations (two 128-shot blocks per CTA, 512-shot pair tiles).
 bool gmm_pair_supported(const GmmProblem& p);
 int gmm_pair_make_maps(const GmmProblem& p, GmmMaps* maps);
 int gmm_pair_launch(const GmmProblem& p, const GmmMaps& maps, const int32_t* type_order, int n_type0,
-                    unsigned long long* counters, int* status, uint64_t timeout_ns, cudaStream_t stream);
+                    unsigned long long* counters, int* status, uint64_t timeout_ns, cudaStream_t stream,
+                    bool stream_w = false);
 int gmm_pair_tile_shots();
 
 // CUDA-core path: fp32 (f32 = true) or bf16 storage, fp32 accumulation.  Any Ci, Co % 4 == 0, Co <= 256.

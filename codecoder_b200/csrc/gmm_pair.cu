@@ -37,6 +37,13 @@
 // half of the shared memory holding W, 96 KB of activation stages are in flight per SM against 192 KB, and under
 // load that does not cover the loads' latency: each SM draws 20 B/clk where the MMAs need 57 and the tensor pipe is
 // 32 % busy (54 % for the wide kernel).  The pre-decoder runs it only when BPC_STEP_KERNEL=pair.
+//
+// The streaming variant (template flag SW, BPC_STEP_KERNEL=pair_stream) keeps no W resident: each of 5 stages holds
+// this CTA's two 128-shot blocks of a 512-shot pair tile and its half of the stage's W block (40 KB), 200 KB in
+// flight per SM and a sixth fewer bytes per FLOP than the wide kernel (each CTA streams half of W for twice the
+// shots).  Measured on the same workload: 92.1k syndromes/s against 109.2k for the wide kernel on the same box, the
+// same bits; every stage waits for the slower of the two CTAs' loads, and the partner's loads start only after the
+// tile reaches its ring.
 #include <algorithm>
 #include <cstdio>
 #include <string>
@@ -66,7 +73,6 @@ constexpr int kPCgElems = kPHalfShots * 8;              // one channel group of 
 constexpr int kPRowElems = 256;                         // TMA rows of the activation map
 constexpr int kPStageRows = static_cast<int>(kPStageBytes / (kPRowElems * 2));   // 32
 constexpr uint32_t kPAccCols = kPC;                     // one accumulator: 128 fp32 columns
-constexpr uint32_t kPTmemCols = 2 * kPAccCols;
 
 struct PairRing {
   long long tile;      // -1: no more tiles
@@ -76,17 +82,32 @@ struct PairRing {
 };
 static_assert(sizeof(PairRing) == 48, "ring entry layout");
 
-// Shared memory of one CTA (offsets from a 1024-byte aligned base).
-constexpr uint32_t kPOffW = 0;
-constexpr uint32_t kPOffStages = kPWBytes;
-constexpr uint32_t kPOffBars = kPOffStages + kPStages * kPStageBytes;
-constexpr int kPNumBars = 2 * kPStages + 2 + 2 + 2 * kPRing + 1 + 1 + 8;   // full, empty, accf, acce, tfull, tempty,
-                                                                          // drain, wfull, hstore (quarter x acc)
-constexpr uint32_t kPOffRing = kPOffBars + 512;
-constexpr uint32_t kPOffMisc = kPOffRing + kPRing * sizeof(PairRing);
-constexpr uint32_t kPSmemBytes = 1024 + kPOffMisc + 64;
-static_assert(kPNumBars * 8 <= 512, "barrier area");
-static_assert(kPSmemBytes <= 232448, "pair kernel exceeds the shared memory per CTA");
+// Shared memory of one CTA (offsets from a 1024-byte aligned base).  Resident-W variant: the W halves, then 6 stages
+// of one 128-shot activation block.  Streaming variant (STREAMW): no resident W; 5 stages, each this CTA's two
+// 128-shot activation blocks (the pair's tile is 512 shots: two M = 256 MMAs per K step, one per block pair) and its
+// half of the step's W block for that stage (64 output channels x 64 input channels), 40 KB.
+constexpr uint32_t kPOffW = 0;                          // resident variant: the W halves
+constexpr int kSSub = 2;
+constexpr int kSStages = 5;
+constexpr uint32_t kSStageBytes = kSSub * kPStageBytes + kPWBlock;
+template <bool SW>
+struct PairLayout {
+  static constexpr int sub = SW ? kSSub : 1;                        // 128-shot blocks per CTA per tile
+  static constexpr int stages = SW ? kSStages : kPStages;
+  static constexpr uint32_t stage_bytes = SW ? kSStageBytes : kPStageBytes;
+  static constexpr uint32_t off_stages = SW ? 0 : kPWBytes;
+  static constexpr uint32_t off_bars = off_stages + stages * stage_bytes;
+  static constexpr int num_bars = 2 * stages + 2 + 2 + 2 * kPRing + 1 + 1 + 16;   // full, empty, accf, acce, tfull,
+                                                                                   // tempty, drain, wfull, hstore
+                                                                                   // (quarter x acc x block)
+  static constexpr uint32_t off_ring = off_bars + 512;
+  static constexpr uint32_t off_misc = off_ring + kPRing * sizeof(PairRing);
+  static constexpr uint32_t smem_bytes = 1024 + off_misc + 64;
+  static constexpr uint32_t tmem_cols = 2 * sub * kPAccCols;        // two accumulator sets
+  static constexpr int tile_shots = sub * kPTileShots;
+  static_assert(num_bars * 8 <= 512, "barrier area");
+  static_assert(smem_bytes <= 232448, "pair kernel exceeds the shared memory per CTA");
+};
 
 struct PairArgs {
   const int32_t* idx;        // (NT, K) sources
@@ -129,25 +150,28 @@ __device__ __forceinline__ void pair_abort(volatile int* abort_flag, uint32_t pe
   st_cluster_u32(peer_abort_cluster, 1u);
 }
 
-template <int EPI, bool HEAD>
+template <int EPI, bool HEAD, bool SW>
 __global__ void __launch_bounds__(kPThreads, 1)
     gmm_pair_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW, const PairArgs a) {
+  using Lay = PairLayout<SW>;
+  constexpr int kSub = Lay::sub;
+  constexpr int kStages = Lay::stages;
   constexpr bool kLoadY = EPI == kEpiGeluResid;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kPOffBars);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Lay::off_bars);
   uint64_t* full = bars;                          // leader: both halves of a stage landed
-  uint64_t* empty = bars + kPStages;              // both CTAs: the MMAs that read a stage are done
-  uint64_t* accf = empty + kPStages;              // both CTAs: an accumulator is complete
+  uint64_t* empty = bars + kStages;               // both CTAs: the MMAs that read a stage are done
+  uint64_t* accf = empty + kStages;               // both CTAs: an accumulator is complete
   uint64_t* acce = accf + 2;                      // leader: both CTAs' epilogues drained an accumulator
   uint64_t* tfull = acce + 2;                     // both CTAs: a ring entry is published
   uint64_t* tempty = tfull + kPRing;              // leader: every consumer of both CTAs released a ring entry
   uint64_t* drain = tempty + kPRing;
   uint64_t* wfull = drain + 1;
-  uint64_t* hstore = wfull + 1;                   // head: quarter q's first channel half is stored (per acc)
-  PairRing* ring = reinterpret_cast<PairRing*>(smem + kPOffRing);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kPOffMisc);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kPOffMisc + 4);
+  uint64_t* hstore = wfull + 1;                   // head: quarter q's first channel half is stored (per acc, block)
+  PairRing* ring = reinterpret_cast<PairRing*>(smem + Lay::off_ring);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Lay::off_misc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Lay::off_misc + 4);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -162,7 +186,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
   const uint32_t peer_abort = map_to_cta(smem_u32(const_cast<int*>(abort_flag)), peer);
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kPStages; ++i) {
+    for (int i = 0; i < kStages; ++i) {
       mbar_init(smem_u32(&full[i]), 1);
       mbar_init(smem_u32(&empty[i]), 1);
     }
@@ -176,14 +200,14 @@ __global__ void __launch_bounds__(kPThreads, 1)
     }
     mbar_init(smem_u32(drain), 1);
     mbar_init(smem_u32(wfull), 1);
-    for (int i = 0; i < 8; ++i) mbar_init(smem_u32(&hstore[i]), 1);
+    for (int i = 0; i < 16; ++i) mbar_init(smem_u32(&hstore[i]), 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmX);
     tma_prefetch_desc(&tmW);
     // this CTA's half of every W_r of its type, resident for the launch: block (r, kb) = output channels
-    // 64 rank .. + 63 of W_{type, r}, input channels 64 kb .. + 63
-    if (n_t > 0) {
+    // 64 rank .. + 63 of W_{type, r}, input channels 64 kb .. + 63 (the streaming variant loads them per stage)
+    if (!SW && n_t > 0) {
       mbar_arrive_expect_tx(smem_u32(wfull), static_cast<uint32_t>(a.K) * 2 * kPWBlock);
       for (int r = 0; r < a.K; ++r)
         for (int kb = 0; kb < 2; ++kb)
@@ -194,7 +218,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
     }
   }
   if (warp == 1) {
-    tmem_alloc_pair(smem_u32(tmem_slot), kPTmemCols);
+    tmem_alloc_pair(smem_u32(tmem_slot), Lay::tmem_cols);
     tmem_relinquish_pair();
   }
   bool ok = true;
@@ -280,13 +304,19 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 break;
               }
               const uint32_t fb = smem_u32(&full[stage]);
-              mbar_arrive_expect_tx(fb, 2 * kPStageBytes);          // both CTAs' halves
-              const int64_t row = e.src[r] * a.x_node_rows + (2 * sb) * (kPBlockElems / kPRowElems) +
-                                  kb * kPStageRows;
-              tma_load_2d(smem_u32(smem + kPOffStages + stage * kPStageBytes), &tmX, 0, static_cast<int32_t>(row), fb);
+              mbar_arrive_expect_tx(fb, 2 * Lay::stage_bytes);      // both CTAs' halves
+              uint8_t* sdst = smem + Lay::off_stages + stage * Lay::stage_bytes;
+#pragma unroll
+              for (int u = 0; u < kSub; ++u) {
+                // this CTA's 128-shot block u of the tile: block 2 (sub sb + u) + rank of the node
+                const int64_t row = e.src[r] * a.x_node_rows +
+                                    (2 * (kSub * sb + u)) * (kPBlockElems / kPRowElems) + kb * kPStageRows;
+                tma_load_2d(smem_u32(sdst + u * kPStageBytes), &tmX, 0, static_cast<int32_t>(row), fb);
+              }
+              if (SW) tma_load_3d(smem_u32(sdst + kSub * kPStageBytes), &tmW, kb * 64, r, type * kPC, fb);
               armed |= 1u << stage;
               armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
-              if (++stage == kPStages) {
+              if (++stage == kStages) {
                 stage = 0;
                 phase ^= 1u;
               }
@@ -295,7 +325,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
         }
         if (!good || *abort_flag) {
           // drain: the stages armed last may still be landing (both halves count on these barriers)
-          for (int i = 0; i < kPStages; ++i)
+          for (int i = 0; i < kStages; ++i)
             if (armed & (1u << i)) {
               const uint32_t par = (armed_parity >> i) & 1u;
               const uint64_t t0 = globaltimer_ns();
@@ -326,12 +356,17 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 good = false;
                 break;
               }
-              const int64_t row = e.src[r] * a.x_node_rows + (2 * sb + 1) * (kPBlockElems / kPRowElems) +
-                                  kb * kPStageRows;
-              tma_load_2d_pair(smem_u32(smem + kPOffStages + stage * kPStageBytes), &tmX, 0,
-                               static_cast<int32_t>(row), map_to_cta(smem_u32(&full[stage]), 0));
+              const uint32_t fb = map_to_cta(smem_u32(&full[stage]), 0);
+              uint8_t* sdst = smem + Lay::off_stages + stage * Lay::stage_bytes;
+#pragma unroll
+              for (int u = 0; u < kSub; ++u) {
+                const int64_t row = e.src[r] * a.x_node_rows +
+                                    (2 * (kSub * sb + u) + 1) * (kPBlockElems / kPRowElems) + kb * kPStageRows;
+                tma_load_2d_pair(smem_u32(sdst + u * kPStageBytes), &tmX, 0, static_cast<int32_t>(row), fb);
+              }
+              if (SW) tma_load_3d_pair(smem_u32(sdst + kSub * kPStageBytes), &tmW, kb * 64, r, type * kPC + 64, fb);
               issued = true;
-              if (++stage == kPStages) {
+              if (++stage == kStages) {
                 stage = 0;
                 phase ^= 1u;
               }
@@ -357,7 +392,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
       int rslot = 0;
       uint32_t rphase = 0;
       bool good = true;
-      const uint32_t w_base = smem_u32(smem + kPOffW);
+      const uint32_t w_base = smem_u32(smem + kPOffW);   // resident variant only
       while (good) {
         if (!mbar_wait(smem_u32(&tfull[rslot]), rphase, abort_flag, a.status, a.timeout_ns)) {
           pair_abort(abort_flag, peer_abort);
@@ -377,7 +412,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc) * kPAccCols;
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc) * kSub * kPAccCols;
         uint32_t accumulate = 0;
         for (int r = 0; r < a.K && good; ++r) {
           if (!(vm & (1u << r))) continue;
@@ -389,16 +424,21 @@ __global__ void __launch_bounds__(kPThreads, 1)
               break;
             }
             tc_fence_after();
-            const uint64_t ad = sdesc_k_none(smem_u32(smem + kPOffStages + stage * kPStageBytes), 2 * kPCgElems, 128);
-            const uint64_t bd = sdesc_k_sw128(w_base + (2 * r + kb) * kPWBlock);
+            const uint32_t sbase = smem_u32(smem + Lay::off_stages + stage * Lay::stage_bytes);
+            const uint64_t bd = SW ? sdesc_k_sw128(sbase + kSub * kPStageBytes)
+                                   : sdesc_k_sw128(w_base + (2 * r + kb) * kPWBlock);
+            // each block's accumulator takes the same MMA sequence (relations, k-blocks, 16-channel steps in order)
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              tc_mma_ss_pair(d_tmem, ad + static_cast<uint64_t>((k * 2 * 2 * kPCgElems) >> 4),
-                             bd + static_cast<uint64_t>((k * 32) >> 4), idesc, accumulate);
-              accumulate = 1;
+            for (int u = 0; u < kSub; ++u) {
+              const uint64_t ad = sdesc_k_none(sbase + u * kPStageBytes, 2 * kPCgElems, 128);
+#pragma unroll
+              for (int k = 0; k < 4; ++k)
+                tc_mma_ss_pair(d_tmem + u * kPAccCols, ad + static_cast<uint64_t>((k * 2 * 2 * kPCgElems) >> 4),
+                               bd + static_cast<uint64_t>((k * 32) >> 4), idesc, (accumulate | k) ? 1u : 0u);
             }
+            accumulate = 1;
             tc_commit_pair(smem_u32(&empty[stage]), 3);   // the stage is free in both CTAs
-            if (++stage == kPStages) {
+            if (++stage == kStages) {
               stage = 0;
               phase ^= 1u;
             }
@@ -445,112 +485,122 @@ __global__ void __launch_bounds__(kPThreads, 1)
         rphase ^= 1u;
       }
       if (tile < 0) break;
-      const int64_t s_half = (tile / n_t) * kPTileShots + static_cast<int64_t>(rank) * kPHalfShots;
-      const int sl = 32 * q + lane;           // this thread's shot within the CTA's half
-      const bool ok = s_half + sl < a.shots;
-      __nv_bfloat16* const yb = a.y + static_cast<int64_t>(n) * a.y_node_stride + (s_half / kPHalfShots) * kPBlockElems;
-      __nv_bfloat16* const yc = yb + (8 * h) * kPCgElems + sl * 8;   // channel group 8 h of this shot; + g kPCgElems
-      uint4 rb[kLoadY ? 8 : 1];
-      if (kLoadY && ok) {
-#pragma unroll
-        for (int g = 0; g < 8; ++g) rb[g] = *reinterpret_cast<const uint4*>(yc + g * kPCgElems);
-      }
-      if (!__all_sync(0xffffffffu, mbar_wait_cl(smem_u32(&accf[acc]), acc_phase, abort_flag, a.status, a.timeout_ns))) {
-        if (lane == 0) pair_abort(abort_flag, peer_abort);
-        break;
-      }
-      tc_fence_after();
-      float v[64];
-      {
-        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
-                               static_cast<uint32_t>(acc) * kPAccCols + 64 * h;
-        float* v0 = v;
-        float* v1 = v + 32;
-        if (vm) {
-          tmem_ld32(taddr, *reinterpret_cast<float(*)[32]>(v0));
-          tmem_ld32(taddr + 32, *reinterpret_cast<float(*)[32]>(v1));
-        } else {
-#pragma unroll
-          for (int i = 0; i < 64; ++i) v[i] = 0.f;
+      bool bail = false;
+#pragma unroll 1
+      for (int u = 0; u < kSub; ++u) {
+        // this CTA's 128-shot block u of the tile (kSub blocks per CTA, interleaved with the partner's)
+        const int64_t s_half = (tile / n_t) * Lay::tile_shots + u * kPTileShots + static_cast<int64_t>(rank) * kPHalfShots;
+        const int sl = 32 * q + lane;           // this thread's shot within the CTA's half
+        const bool ok = s_half + sl < a.shots;
+        __nv_bfloat16* const yb = a.y + static_cast<int64_t>(n) * a.y_node_stride + (s_half / kPHalfShots) * kPBlockElems;
+        __nv_bfloat16* const yc = yb + (8 * h) * kPCgElems + sl * 8;   // channel group 8 h of this shot; + g kPCgElems
+        uint4 rb[kLoadY ? 8 : 1];
+        if (kLoadY && ok) {
+  #pragma unroll
+          for (int g = 0; g < 8; ++g) rb[g] = *reinterpret_cast<const uint4*>(yc + g * kPCgElems);
+        }
+        if (u == 0 &&
+            !__all_sync(0xffffffffu, mbar_wait_cl(smem_u32(&accf[acc]), acc_phase, abort_flag, a.status, a.timeout_ns))) {
+          if (lane == 0) pair_abort(abort_flag, peer_abort);
+          bail = true;
+          break;
+        }
+        tc_fence_after();
+        float v[64];
+        {
+          const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                                 static_cast<uint32_t>(acc * kSub + u) * kPAccCols + 64 * h;
+          float* v0 = v;
+          float* v1 = v + 32;
+          if (vm) {
+            tmem_ld32(taddr, *reinterpret_cast<float(*)[32]>(v0));
+            tmem_ld32(taddr + 32, *reinterpret_cast<float(*)[32]>(v1));
+          } else {
+  #pragma unroll
+            for (int i = 0; i < 64; ++i) v[i] = 0.f;
+          }
+        }
+        // the accumulator is free for the pair's next tile once both CTAs' eight warps have read it
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0 && !late_release && u == kSub - 1) release_acc(leader, &acce[acc]);
+        uint32_t outw[32];
+  #pragma unroll
+        for (int g = 0; g < 8; ++g) {
+          uint4 u;
+          uint32_t* o = reinterpret_cast<uint32_t*>(&u);
+          const uint32_t* hr = reinterpret_cast<const uint32_t*>(&rb[kLoadY ? g : 0]);
+  #pragma unroll
+          for (int e4 = 0; e4 < 4; ++e4) {
+            uint64_t xx = gelu_tanh_fast2(f2_pack(v[8 * g + 2 * e4], v[8 * g + 2 * e4 + 1]));
+            if (kLoadY) xx = f2_add(xx, bf2_to_f2(hr[e4]));
+            o[e4] = f2_to_bf2(xx);
+            outw[4 * g + e4] = o[e4];
+          }
+          if (ok) *reinterpret_cast<uint4*>(yc + g * kPCgElems) = u;
+        }
+        if (HEAD) {
+          // logits over the 128 stored channels in order (channel pairs, groups 0 .. 15): the first channel half is
+          // read back once its warp has stored it, the second is this warp's own
+          if (h == 0) {
+            __threadfence_block();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&hstore[(2 * q + acc) * kSub + u]));
+          } else {
+            if (!__all_sync(0xffffffffu,
+                            mbar_wait(smem_u32(&hstore[(2 * q + acc) * kSub + u]), acc_phase, abort_flag, a.status,
+                                      a.timeout_ns))) {
+              if (lane == 0) pair_abort(abort_flag, peer_abort);
+              bail = true;
+              break;
+            }
+            uint64_t lg0 = 0, lg1 = 0;
+            const __nv_bfloat16* y0 = yb + sl * 8;
+  #pragma unroll
+            for (int g = 0; g < 8; ++g) {
+              uint4 u = make_uint4(0, 0, 0, 0);
+              if (ok) u = __ldcg(reinterpret_cast<const uint4*>(y0 + g * kPCgElems));   // through L2
+              const uint32_t* o = reinterpret_cast<const uint32_t*>(&u);
+  #pragma unroll
+              for (int e4 = 0; e4 < 4; ++e4) {
+                const uint64_t f = bf2_to_f2(o[e4]);
+                const int col = g * 8 + 2 * e4;
+                lg0 = f2_fma(f, *reinterpret_cast<const uint64_t*>(a.head.head_w + col), lg0);
+                lg1 = f2_fma(f, *reinterpret_cast<const uint64_t*>(a.head.head_w + kPC + col), lg1);
+              }
+            }
+  #pragma unroll
+            for (int g = 0; g < 8; ++g)
+  #pragma unroll
+              for (int e4 = 0; e4 < 4; ++e4) {
+                const uint64_t f = bf2_to_f2(outw[4 * g + e4]);
+                const int col = 64 + g * 8 + 2 * e4;
+                lg0 = f2_fma(f, *reinterpret_cast<const uint64_t*>(a.head.head_w + col), lg0);
+                lg1 = f2_fma(f, *reinterpret_cast<const uint64_t*>(a.head.head_w + kPC + col), lg1);
+              }
+            const float l0 = f2_lo(lg0) + f2_hi(lg0) + __ldg(a.head.head_b);
+            const float l1 = f2_lo(lg1) + f2_hi(lg1) + __ldg(a.head.head_b + 1);
+            if (ok) {
+              float2* lp = reinterpret_cast<float2*>(a.head.logits + (s_half + sl) * a.head.lg_shot_stride +
+                                                     static_cast<int64_t>(n) * a.head.lg_node_stride);
+              *lp = make_float2(l0, l1);
+            }
+            if (a.head.res_bits) {
+              const uint32_t m0 = __ballot_sync(0xffffffffu, ok && l0 > 0.f);
+              const uint32_t m1 = __ballot_sync(0xffffffffu, ok && l1 > 0.f);
+              if (lane < 4) {
+                const int32_t c = __ldg(a.head.xor_nbr + static_cast<int64_t>(n) * 4 + lane);
+                const uint32_t msk = (lane >> 1) ? m1 : m0;
+                if (c >= 0 && msk)
+                  atomicXor(a.head.res_bits + static_cast<int64_t>(c) * a.head.res_words + ((s_half + 32 * q) >> 5), msk);
+              }
+            }
+            __syncwarp();
+            if (lane == 0 && u == kSub - 1) release_acc(leader, &acce[acc]);
+          }
         }
       }
-      // the accumulator is free for the pair's next tile once both CTAs' eight warps have read it
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0 && !late_release) release_acc(leader, &acce[acc]);
-      uint32_t outw[32];
-#pragma unroll
-      for (int g = 0; g < 8; ++g) {
-        uint4 u;
-        uint32_t* o = reinterpret_cast<uint32_t*>(&u);
-        const uint32_t* hr = reinterpret_cast<const uint32_t*>(&rb[kLoadY ? g : 0]);
-#pragma unroll
-        for (int e4 = 0; e4 < 4; ++e4) {
-          uint64_t xx = gelu_tanh_fast2(f2_pack(v[8 * g + 2 * e4], v[8 * g + 2 * e4 + 1]));
-          if (kLoadY) xx = f2_add(xx, bf2_to_f2(hr[e4]));
-          o[e4] = f2_to_bf2(xx);
-          outw[4 * g + e4] = o[e4];
-        }
-        if (ok) *reinterpret_cast<uint4*>(yc + g * kPCgElems) = u;
-      }
-      if (HEAD) {
-        // logits over the 128 stored channels in order (channel pairs, groups 0 .. 15): the first channel half is
-        // read back once its warp has stored it, the second is this warp's own
-        if (h == 0) {
-          __threadfence_block();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(smem_u32(&hstore[2 * q + acc]));
-        } else {
-          if (!__all_sync(0xffffffffu,
-                          mbar_wait(smem_u32(&hstore[2 * q + acc]), acc_phase, abort_flag, a.status, a.timeout_ns))) {
-            if (lane == 0) pair_abort(abort_flag, peer_abort);
-            break;
-          }
-          uint64_t lg0 = 0, lg1 = 0;
-          const __nv_bfloat16* y0 = yb + sl * 8;
-#pragma unroll
-          for (int g = 0; g < 8; ++g) {
-            uint4 u = make_uint4(0, 0, 0, 0);
-            if (ok) u = __ldcg(reinterpret_cast<const uint4*>(y0 + g * kPCgElems));   // through L2
-            const uint32_t* o = reinterpret_cast<const uint32_t*>(&u);
-#pragma unroll
-            for (int e4 = 0; e4 < 4; ++e4) {
-              const uint64_t f = bf2_to_f2(o[e4]);
-              const int col = g * 8 + 2 * e4;
-              lg0 = f2_fma(f, *reinterpret_cast<const uint64_t*>(a.head.head_w + col), lg0);
-              lg1 = f2_fma(f, *reinterpret_cast<const uint64_t*>(a.head.head_w + kPC + col), lg1);
-            }
-          }
-#pragma unroll
-          for (int g = 0; g < 8; ++g)
-#pragma unroll
-            for (int e4 = 0; e4 < 4; ++e4) {
-              const uint64_t f = bf2_to_f2(outw[4 * g + e4]);
-              const int col = 64 + g * 8 + 2 * e4;
-              lg0 = f2_fma(f, *reinterpret_cast<const uint64_t*>(a.head.head_w + col), lg0);
-              lg1 = f2_fma(f, *reinterpret_cast<const uint64_t*>(a.head.head_w + kPC + col), lg1);
-            }
-          const float l0 = f2_lo(lg0) + f2_hi(lg0) + __ldg(a.head.head_b);
-          const float l1 = f2_lo(lg1) + f2_hi(lg1) + __ldg(a.head.head_b + 1);
-          if (ok) {
-            float2* lp = reinterpret_cast<float2*>(a.head.logits + (s_half + sl) * a.head.lg_shot_stride +
-                                                   static_cast<int64_t>(n) * a.head.lg_node_stride);
-            *lp = make_float2(l0, l1);
-          }
-          if (a.head.res_bits) {
-            const uint32_t m0 = __ballot_sync(0xffffffffu, ok && l0 > 0.f);
-            const uint32_t m1 = __ballot_sync(0xffffffffu, ok && l1 > 0.f);
-            if (lane < 4) {
-              const int32_t c = __ldg(a.head.xor_nbr + static_cast<int64_t>(n) * 4 + lane);
-              const uint32_t msk = (lane >> 1) ? m1 : m0;
-              if (c >= 0 && msk)
-                atomicXor(a.head.res_bits + static_cast<int64_t>(c) * a.head.res_words + ((s_half + 32 * q) >> 5), msk);
-            }
-          }
-          __syncwarp();
-          if (lane == 0) release_acc(leader, &acce[acc]);
-        }
-      }
+      if (bail) break;
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
@@ -564,15 +614,18 @@ __global__ void __launch_bounds__(kPThreads, 1)
   cluster_wait_acquire();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc_pair(tmem_base, kPTmemCols);
+    tmem_dealloc_pair(tmem_base, Lay::tmem_cols);
   }
 }
 
 using PairFn = void (*)(CUtensorMap, CUtensorMap, PairArgs);
 
+template <bool SW>
 PairFn pair_kernel_for(int epi, bool head) {
-  if (epi == kEpiGeluInit) return head ? &gmm_pair_kernel<kEpiGeluInit, true> : &gmm_pair_kernel<kEpiGeluInit, false>;
-  if (epi == kEpiGeluResid) return head ? &gmm_pair_kernel<kEpiGeluResid, true> : &gmm_pair_kernel<kEpiGeluResid, false>;
+  if (epi == kEpiGeluInit)
+    return head ? &gmm_pair_kernel<kEpiGeluInit, true, SW> : &gmm_pair_kernel<kEpiGeluInit, false, SW>;
+  if (epi == kEpiGeluResid)
+    return head ? &gmm_pair_kernel<kEpiGeluResid, true, SW> : &gmm_pair_kernel<kEpiGeluResid, false, SW>;
   return nullptr;
 }
 
@@ -618,7 +671,8 @@ int gmm_pair_make_maps(const GmmProblem& p, GmmMaps* maps) {
 }
 
 int gmm_pair_launch(const GmmProblem& p, const GmmMaps& maps, const int32_t* type_order, int n_type0,
-                    unsigned long long* counters, int* status, uint64_t timeout_ns, cudaStream_t stream) {
+                    unsigned long long* counters, int* status, uint64_t timeout_ns, cudaStream_t stream,
+                    bool stream_w) {
   if (!gmm_pair_supported(p)) return fail(2, "the pair kernel takes blocked hidden-128 steps with at most 8 relations");
   if (p.shots <= 0) return 0;
   if (!counters) return fail(2, "the pair kernel needs two tile counters");
@@ -650,7 +704,8 @@ int gmm_pair_launch(const GmmProblem& p, const GmmMaps& maps, const int32_t* typ
   a.n_type0 = n0;
   a.pairs_type0 = pairs0;
   a.shots = p.shots;
-  a.sblocks = (p.shots + kPTileShots - 1) / kPTileShots;
+  const int tile_shots = stream_w ? PairLayout<true>::tile_shots : PairLayout<false>::tile_shots;
+  a.sblocks = (p.shots + tile_shots - 1) / tile_shots;
   a.x_node_rows = p.x_node_stride / kPRowElems;
   a.y = static_cast<__nv_bfloat16*>(p.y);
   a.y_node_stride = p.y_node_stride;
@@ -658,15 +713,17 @@ int gmm_pair_launch(const GmmProblem& p, const GmmMaps& maps, const int32_t* typ
   a.status = status;
   a.timeout_ns = timeout_ns;
   a.counters = counters;
-  PairFn fn = pair_kernel_for(p.epi, p.head.head_w != nullptr);
+  PairFn fn = stream_w ? pair_kernel_for<true>(p.epi, p.head.head_w != nullptr)
+                       : pair_kernel_for<false>(p.epi, p.head.head_w != nullptr);
   if (!fn) return fail(2, "unsupported pair-kernel epilogue");
-  if (int e = allow_smem(reinterpret_cast<const void*>(fn), static_cast<int>(kPSmemBytes))) return e;
+  const uint32_t smem_bytes = stream_w ? PairLayout<true>::smem_bytes : PairLayout<false>::smem_bytes;
+  if (int e = allow_smem(reinterpret_cast<const void*>(fn), static_cast<int>(smem_bytes))) return e;
   cudaError_t me = cudaMemsetAsync(counters, 0, 2 * sizeof(unsigned long long), stream);
   if (me != cudaSuccess) return fail(4, std::string("cudaMemsetAsync: ") + cudaGetErrorString(me));
   cudaLaunchConfig_t lc = {};
   lc.gridDim = dim3(static_cast<unsigned>(2 * pairs));
   lc.blockDim = dim3(kPThreads);
-  lc.dynamicSmemBytes = kPSmemBytes;
+  lc.dynamicSmemBytes = smem_bytes;
   lc.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;

@@ -288,8 +288,11 @@ extern "C" int bpc_predecoder_forward(bpc_predecoder* h, const uint8_t* det, flo
   // hidden-128 steps: the single-CTA wide-tile kernel; BPC_STEP_KERNEL=pair selects the CTA-pair kernel with resident
   // relation matrices (same bits; measured slower on B200: half of its shared memory holds W, so half as many
   // activation bytes are in flight and the loads' latency is not covered)
+  // activation bytes are in flight and the loads' latency is not covered); BPC_STEP_KERNEL=pair_stream selects the
+  // CTA-pair kernel with the W halves streamed alongside two 128-shot blocks per CTA
   const char* sk = std::getenv("BPC_STEP_KERNEL");
-  const bool pair = shot_tiles && c.channels == 128 && c.K <= 8 && sk && std::strcmp(sk, "pair") == 0;
+  const bool pair_stream = sk && std::strcmp(sk, "pair_stream") == 0;
+  const bool pair = shot_tiles && c.channels == 128 && c.K <= 8 && sk && (std::strcmp(sk, "pair") == 0 || pair_stream);
   const size_t es = esize(c.dtype);
   const size_t wl = static_cast<size_t>(c.channels) * c.K * c.channels;
 
@@ -406,7 +409,7 @@ extern "C" int bpc_predecoder_forward(bpc_predecoder* h, const uint8_t* det, flo
           GmmMaps m = step == 0 ? mc2d : md2c;
           m.w = step == 0 ? wm_c2d[l] : wm_d2c[l];
           e = gmm_pair_launch(p, m, step == 0 ? nullptr : h->check_order_typed, c.z_check_begin, h->tile_counter,
-                              h->status, h->timeout_ns, stream);
+                              h->status, h->timeout_ns, stream, pair_stream);
         } else if (tc) {
           GmmMaps m = step == 0 ? mc2d : md2c;
           m.w = step == 0 ? wm_c2d[l] : wm_d2c[l];

@@ -203,9 +203,11 @@ def test_d13_wide_tiles_match_node_tiles_bitwise():
     assert torch.equal(w_lg, n_lg) and torch.equal(w_rs, n_rs)
 
 
-def test_d13_pair_steps_match_wide_tile_steps_bitwise(monkeypatch):
+@pytest.mark.parametrize("kernel", ["pair", "pair_stream"])
+def test_d13_pair_steps_match_wide_tile_steps_bitwise(monkeypatch, kernel):
     """Hidden-128 passes of more than 64 shots run the single-CTA wide-tile kernel; BPC_STEP_KERNEL=pair selects the
-    CTA-pair kernel (cta_group::2 MMAs, M = 256 shots, relation matrices resident in shared memory).  The two
+    CTA-pair kernel (cta_group::2 MMAs, M = 256 shots, relation matrices resident in shared memory), pair_stream the
+    CTA-pair kernel with the W halves streamed alongside two 128-shot blocks per CTA (512-shot pair tiles).  They
     accumulate every output in the same relation and channel order and use the same element arithmetic: every logit
     and residual bit agrees, over full and partial tiles, in both step types and the head."""
     cfg = replace(CONFIGS["d13_bf16"], layers=3)
@@ -215,7 +217,7 @@ def test_d13_pair_steps_match_wide_tile_steps_bitwise(monkeypatch):
     d = torch.as_tensor(det).to(DEV)
     pd = PreDecoder(g, cfg, params, device=DEV)
     w_lg, w_rs = pd(d)
-    monkeypatch.setenv("BPC_STEP_KERNEL", "pair")
+    monkeypatch.setenv("BPC_STEP_KERNEL", kernel)
     p_lg, p_rs = pd(d)
     torch.cuda.synchronize()
     assert pd.status() == 0
