@@ -640,17 +640,20 @@ def main():
         tcfg = CONFIGS["d11_train"]
         tg = RotatedSurface(tcfg.d, tcfg.rounds)
         torch.manual_seed(SEED)
-        trn = Trainer(PreDecoderNet(tg, tcfg, init_params(tcfg, SEED)).to(dev), lr=1e-3)
+        # one GPU: each step replays one CUDA graph (forward, backward, clipping, Adam); DDP steps run eagerly
+        graphed = world == 1
+        trn = Trainer(PreDecoderNet(tg, tcfg, init_params(tcfg, SEED)).to(dev), lr=1e-3, graph=graphed)
+        tstep = trn.step_graphed if graphed else trn.step
         batches = [sample_torch(tg, tcfg.p, args.train_batch, SEED + 1000 * rank + i, device=dev) for i in range(4)]
         losses = []
         for i in range(args.warmup):
-            losses.append(trn.step(*batches[i % 4]))
+            losses.append(tstep(*batches[i % 4]))
         torch.cuda.synchronize()
         barrier()
         s3, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s3.record()
         for i in range(args.train_steps):
-            losses.append(trn.step(*batches[(args.warmup + i) % 4]))
+            losses.append(tstep(*batches[(args.warmup + i) % 4]))
         e3.record()
         e3.synchronize()
         barrier()
@@ -659,7 +662,7 @@ def main():
         tfps = train_flops_per_shot(tg, tcfg)
         train = {"config": f"d={tcfg.d}, {tcfg.rounds} rounds, p={tcfg.p}, {tcfg.layers} layers, C={tcfg.channels}, "
                            f"bf16 autocast, BCE vs sampled data-qubit errors, Adam lr 1e-3, grad-norm clip 1, "
-                           f"{'DDP over NCCL' if world > 1 else 'one GPU'}",
+                           f"{'DDP over NCCL, eager steps' if world > 1 else 'one GPU, each step one CUDA graph replay'}",
                  "shots_per_gpu": args.train_batch, "steps": args.train_steps, "warmup": args.warmup,
                  "ms_per_step": ms3 / args.train_steps,
                  "shots_per_s": args.train_steps * args.train_batch * world / (ms3 / 1000.0),

@@ -122,9 +122,11 @@ class PreDecoderNet(nn.Module):
 
 class Trainer:
     """One process per GPU.  model: PreDecoderNet on `device`; with an initialised process group of world > 1 the
-    model is wrapped in DDP (NCCL on GPUs, gloo on CPU)."""
+    model is wrapped in DDP (NCCL on GPUs, gloo on CPU).  graph=True (one GPU): step_graphed replays the whole step
+    from a CUDA graph (the optimiser then keeps its step count on the device)."""
 
-    def __init__(self, model: PreDecoderNet, lr: float = 1e-3, clip: float = 1.0, autocast: bool = True):
+    def __init__(self, model: PreDecoderNet, lr: float = 1e-3, clip: float = 1.0, autocast: bool = True,
+                 graph: bool = False):
         import torch.distributed as dist
         self.model = model
         self.device = next(model.parameters()).device
@@ -138,20 +140,54 @@ class Trainer:
             self.net = DDP(model, device_ids=ids, broadcast_buffers=False, bucket_cap_mb=1,
                            gradient_as_bucket_view=True)
         self.params = [p for p in model.parameters() if p.requires_grad]
-        self.opt = torch.optim.Adam(self.params, lr=lr)
+        self.graphable = graph and self.world == 1 and self.device.type == "cuda"
+        if graph and not self.graphable:
+            raise ValueError("graphed training steps run on one GPU (DDP's all-reduce is not captured)")
+        self.opt = torch.optim.Adam(self.params, lr=lr, capturable=self.graphable)
         self.clip = clip
         self.autocast = autocast and self.device.type == "cuda"
+        self._graph = None
 
     def step(self, det: torch.Tensor, err: torch.Tensor) -> torch.Tensor:
         """det (B, N_c) uint8, err (B, N_d, 2) 0/1 labels -> the batch loss (a device scalar, not synchronised)."""
-        ctx = torch.autocast("cuda", dtype=torch.bfloat16) if self.autocast else nullcontext()
+        loss = self._forward_backward(det, err)
+        self.opt.zero_grad(set_to_none=True)
+        return loss
+
+    def _forward_backward(self, det: torch.Tensor, err: torch.Tensor, cache: bool = True) -> torch.Tensor:
+        ctx = torch.autocast("cuda", dtype=torch.bfloat16, cache_enabled=cache) if self.autocast else nullcontext()
         with ctx:
             loss = self.net(det, err)            # logits and loss (fused on the GPU path)
         loss.backward()
         torch.nn.utils.clip_grad_norm_(self.params, self.clip)
         self.opt.step()
-        self.opt.zero_grad(set_to_none=True)
         return loss.detach()
+
+    def step_graphed(self, det: torch.Tensor, err: torch.Tensor, warmup: int = 2) -> torch.Tensor:
+        """The same step replayed from one CUDA graph (forward, backward, clipping, optimiser step), so that the ~230
+        launches of a step no longer wait on the host.  The first call runs `warmup` eager steps on det / err on a side
+        stream, captures the step over static copies of the inputs and replays it; later calls copy det / err into
+        those and replay.  The gradients live in the graph's memory between replays."""
+        if not self.graphable:
+            raise RuntimeError("graphed steps need Trainer(..., graph=True) on one GPU")
+        if self._graph is None:
+            self._det, self._err = det.clone(), err.clone()
+            side = torch.cuda.Stream(self.device)
+            side.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(side):
+                for _ in range(warmup):
+                    self.step(self._det, self._err)
+            torch.cuda.current_stream(self.device).wait_stream(side)
+            self.opt.zero_grad(set_to_none=True)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self._loss = self._forward_backward(self._det, self._err, cache=False)
+            self._graph = g
+        else:
+            self._det.copy_(det)
+            self._err.copy_(err)
+        self._graph.replay()
+        return self._loss.clone()
 
     def agree(self, stop: bool, bad: bool) -> tuple[bool, bool]:
         """Every rank takes the same decision: MAX over ranks of the stop / non-finite flags."""

@@ -73,6 +73,25 @@ def test_training_lowers_the_loss():
     assert np.mean(losses[-10:]) < 0.7 * np.mean(losses[:5]), losses
 
 
+def test_graphed_training_steps_match_eager_steps():
+    """Trainer(graph=True).step_graphed replays forward, backward, clipping and the Adam step from one CUDA graph:
+    from the same weights and the same batches it gives the eager steps' losses and weights bit for bit (its first
+    call runs two eager warm-up steps on its batch before the captured one, so the eager run does the same)."""
+    cfg = replace(CONFIGS["d11_train"], d=5, rounds=5, layers=3)            # C = 96: tensor-core kernels
+    g = RotatedSurface(cfg.d, cfg.rounds)
+    batches = [sample_torch(g, 0.03, 384, 60 + i, device="cuda") for i in range(3)]
+    eager = Trainer(PreDecoderNet(g, cfg, init_params(cfg, 59)).cuda(), lr=1e-3, graph=True)
+    graphed = Trainer(PreDecoderNet(g, cfg, init_params(cfg, 59)).cuda(), lr=1e-3, graph=True)
+    order = [0, 1, 2, 1, 0]
+    le = [eager.step(*batches[0]) for _ in range(2)]
+    le += [eager.step(*batches[i]) for i in order]
+    lg = [graphed.step_graphed(*batches[i]) for i in order]
+    torch.cuda.synchronize()
+    assert torch.equal(torch.stack(le[2:]), torch.stack(lg))
+    for pe, pg in zip(eager.model.parameters(), graphed.model.parameters()):
+        assert torch.equal(pe, pg)
+
+
 def test_fused_steps_match_the_unfused_network():
     """Under bf16 autocast PreDecoderNet runs each residual step as ops.bipartite_step (op kernels + one GELU /
     residual pass each way, both check types in one pre-activation block); the unfused torch composition of the same
