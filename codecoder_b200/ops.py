@@ -339,10 +339,17 @@ class BipartiteStepB200(torch.autograd.Function):
     The T forwards write one type-major pre-activation block (T, B, NT / T, C_out) that is kept for the backward;
     GELU, the add and the cast run as one pass (bpc_gelu_residual_fwd), the GELU gradient and the residual sum as
     one pass back (bpc_gelu_residual_bwd); the input gradients of the T types accumulate in the second dgrad's
-    epilogue, and the weight gradients are fp32 from the deterministic wgrad kernel."""
+    epilogue, and the weight gradients are fp32 from the deterministic wgrad kernel.
+
+    carry: None, or (dict, give, take) linking two steps of one forward that share a bf16 tensor (the data stream
+    h_d, the residual input h of a check -> data step and the input x of the data -> check step before it).  The
+    step with give = k hands the residual gradient (its output's gradient, passed through) to dict[k] instead of
+    returning it; the step with take = k starts its input gradient from dict[k] and accumulates both types' dgrads into
+    it in the kernel's add epilogue, so the two gradients of h_d are summed without a separate add.  The giving step's
+    backward always runs first: the taking step's output feeds the giving step's x."""
 
     @staticmethod
-    def forward(ctx, x, h, tables, *ws):
+    def forward(ctx, x, h, tables, carry, *ws):
         T = len(ws)
         B, NS, Ci = x.shape
         NTt = tables[0][0].shape[0]
@@ -363,7 +370,7 @@ class BipartiteStepB200(torch.autograd.Function):
         _lib.check(rc, "bpc_gelu_residual_fwd")
         ctx.save_for_backward(x, a, *w16)
         ctx.set_materialize_grads(False)     # an unused output's gradient stays None, not a zero-filled tensor
-        ctx.tables, ctx.f32, ctx.has_h = tables, f32, h is not None
+        ctx.tables, ctx.f32, ctx.has_h, ctx.carry = tables, f32, h is not None, carry
         return (y, y16) if f32 else y
 
     @staticmethod
@@ -374,7 +381,7 @@ class BipartiteStepB200(torch.autograd.Function):
         L = _lib.lib()
         st = _stream_ptr(x.device)
         if gy is None and gy16 is None:
-            return (None, None, None, *([None] * T))
+            return (None, None, None, None, *([None] * T))
         gh = None
         ga = torch.empty_like(a)
         if ctx.f32:
@@ -391,13 +398,23 @@ class BipartiteStepB200(torch.autograd.Function):
                                          _lib.BPC_DTYPE_BF16, st)
             gh = gy if ctx.has_h and ctx.needs_input_grad[1] else None
         _lib.check(rc, "bpc_gelu_residual_bwd")
+        carry = ctx.carry
+        if carry is not None and carry[1] is not None and gh is not None and gh.dtype == torch.bfloat16:
+            carry[0][carry[1]] = gh                # the taking step adds its input gradient to it
+            gh = None
         gx = None
         if ctx.needs_input_grad[0]:
-            gx = torch.empty_like(x)
-            for t in range(T):
-                _dgrad_into(ga[t], ctx.tables[t][1], w16[t], gx, accumulate=t > 0)
-        gws = [gmm_wgrad(x, ga[t], ctx.tables[t][0]) if ctx.needs_input_grad[3 + t] else None for t in range(T)]
-        return (gx, gh, None, *gws)
+            base = carry[0].pop(carry[2], None) if carry is not None and carry[2] is not None else None
+            if base is not None and base.shape == x.shape and base.dtype == x.dtype and base.is_contiguous():
+                gx = base
+                for t in range(T):
+                    _dgrad_into(ga[t], ctx.tables[t][1], w16[t], gx, accumulate=True)
+            else:
+                gx = torch.empty_like(x)
+                for t in range(T):
+                    _dgrad_into(ga[t], ctx.tables[t][1], w16[t], gx, accumulate=t > 0)
+        gws = [gmm_wgrad(x, ga[t], ctx.tables[t][0]) if ctx.needs_input_grad[4 + t] else None for t in range(T)]
+        return (gx, gh, None, None, *gws)
 
 
 class EmbedTokensB200(torch.autograd.Function):
@@ -491,9 +508,9 @@ def embed_tokens(det, check_type, E):
     return EmbedTokensB200.apply(det, check_type, E)
 
 
-def bipartite_step(x, h, tables, *ws):
+def bipartite_step(x, h, tables, *ws, carry=None):
     """BipartiteStepB200.apply (see there)."""
-    return BipartiteStepB200.apply(x, h, tables, *ws)
+    return BipartiteStepB200.apply(x, h, tables, carry, *ws)
 
 
 def gather_mm(x, w, idx, inv):

@@ -108,11 +108,12 @@ class PreDecoderNet(nn.Module):
         c2d = ((self.c2d_i32, self.c2d_tgt),)
         d2c = ((self.d2c0_i32, self.d2c0_tgt), (self.d2c1_i32, self.d2c1_tgt))
         hd = None
+        carry = {}                              # h_d's two gradients summed in the dgrad epilogue (see bipartite_step)
         for l in range(self.cfg.layers):
-            hd = bipartite_step(hc16, hd, c2d, self.w_c2d[l])
+            hd = bipartite_step(hc16, hd, c2d, self.w_c2d[l], carry=(carry, l - 1 if l > 0 else None, None))
             if l == self.cfg.layers - 1:
                 break
-            hc, hc16 = bipartite_step(hd, hc, d2c, self.w_d2c[2 * l], self.w_d2c[2 * l + 1])
+            hc, hc16 = bipartite_step(hd, hc, d2c, self.w_d2c[2 * l], self.w_d2c[2 * l + 1], carry=(carry, None, l))
         if labels is not None and self.cfg.channels <= 128:
             # head and loss in one pass each way, the logits never materialised (ops.HeadBCEB200)
             return head_bce(hd, self.head_w, self.head_b, labels)
