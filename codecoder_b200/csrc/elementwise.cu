@@ -496,9 +496,15 @@ extern "C" int bpc_embed_tokens_bwd(const uint8_t* det, const uint8_t* check_typ
   if (workspace_bytes < bpc_embed_tokens_bwd_workspace_size(C)) return fail(BPC_ERR_SPACE, "embedding workspace too small");
   float* partial = static_cast<float*>(workspace);
   auto partial_kernel = C <= 128 ? embed_tokens_bwd_partial_kernel<1, 8> : embed_tokens_bwd_partial_kernel<2, 4>;
-  partial_kernel<<<kEmbBwdBlocks, kEmbBwdThreads, 0, s>>>(
-      det, check_type, g, static_cast<const __nv_bfloat16*>(g_bf16), partial, B * N, N, C);
-  embed_tokens_bwd_sum_kernel<<<(4 * C + 127) / 128, 128, 0, s>>>(partial, dE, 4 * C, kEmbBwdBlocks);
+  // every block resident at once (no partial last wave): the blocks that fit on the SMs, at most the workspace's
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, reinterpret_cast<const void*>(partial_kernel),
+                                                    kEmbBwdThreads, 0) != cudaSuccess || per_sm < 1)
+    per_sm = 1;
+  const int grid = std::min(kEmbBwdBlocks, per_sm * num_sms());
+  partial_kernel<<<grid, kEmbBwdThreads, 0, s>>>(det, check_type, g, static_cast<const __nv_bfloat16*>(g_bf16),
+                                                 partial, B * N, N, C);
+  embed_tokens_bwd_sum_kernel<<<(4 * C + 127) / 128, 128, 0, s>>>(partial, dE, 4 * C, grid);
   cudaError_t le = cudaGetLastError();
   if (le != cudaSuccess) return fail(BPC_ERR_LAUNCH, std::string("embed_tokens_bwd launch: ") + cudaGetErrorString(le));
   return 0;
