@@ -54,6 +54,8 @@ SIGNATURES = {
                                         c_i32, c_vp]),
     "bpc_embed_tokens_bwd": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, ctypes.c_size_t, c_i64, c_i32, c_i32,
                                             c_vp]),
+    "bpc_gather_mm_fwd_gelu": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_i32, c_i32, c_i32, c_vp,
+                                              c_i32, c_vp, c_vp, c_i64, c_vp]),
     "bpc_gather_mm_dgrad": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_i32, c_i32, c_i32,
                                            c_i32, c_vp]),
     "bpc_gather_mm_dgrad_ex": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_i32, c_i32, c_i32,

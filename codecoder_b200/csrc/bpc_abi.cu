@@ -119,6 +119,45 @@ extern "C" int bpc_gather_mm_fwd_ex(const void* x, const void* w, const int32_t*
   return run_gather_mm(x, w, idx, y, B, NS, NT, K, Ci, Co, n_wtypes, type_split, epi, scale, shift, dtype, stream);
 }
 
+extern "C" int bpc_gather_mm_fwd_gelu(const void* x, const void* w, const int32_t* idx, void* a, int64_t B,
+                                     int32_t NS, int32_t NT, int32_t K, int32_t Ci, int32_t Co, const void* h,
+                                     int32_t h_dtype, void* out, void* out_bf16, int64_t stream_shot_stride,
+                                     bpc_stream_t stream) {
+  if (B < 0 || NS < 1 || NT < 0 || K < 1 || Ci < 1 || Co < 1) return fail(BPC_ERR_ARG, "invalid gather_mm shape");
+  if (h && h_dtype != BPC_DTYPE_F32 && h_dtype != BPC_DTYPE_BF16) return fail(BPC_ERR_ARG, "h must be f32 or bf16");
+  if (stream_shot_stride < static_cast<int64_t>(NT) * Co) return fail(BPC_ERR_ARG, "stream rows overlap");
+  if (B == 0 || NT == 0) return 0;
+  if (!x || !w || !idx || !a || !out || (h && h_dtype == BPC_DTYPE_F32 && !out_bf16))
+    return fail(BPC_ERR_ARG, "null buffer");
+  GmmProblem p;
+  p.x = x;
+  p.x_shot_stride = static_cast<int64_t>(NS) * Ci;
+  p.x_node_stride = Ci;
+  p.shots = B;
+  p.NS = NS;
+  p.w = w;
+  p.type_split = NT;
+  p.idx = idx;
+  p.NT = NT;
+  p.K = K;
+  p.Ci = Ci;
+  p.Co = Co;
+  p.y = a;
+  p.y_shot_stride = static_cast<int64_t>(NT) * Co;
+  p.y_node_stride = Co;
+  p.epi = kEpiGeluStream;
+  p.res_h = h;
+  p.res_f32 = h && h_dtype == BPC_DTYPE_F32;
+  p.res_out = out;
+  p.res_out16 = out_bf16;
+  p.res_shot_stride = stream_shot_stride;
+  p.res_node_stride = Co;
+  if (int e = gmm_tc_check(p)) return e;
+  GmmMaps maps;
+  if (int e = gmm_tc_make_maps(p, &maps)) return e;
+  return gmm_tc_launch(p, maps, op_status_ptr(), 2000000000ull, reinterpret_cast<cudaStream_t>(stream));
+}
+
 extern "C" int bpc_gather_mm_dgrad(const void* gy, const void* w, const int32_t* tgt, void* gx, void* w_t, int64_t B,
                                    int32_t NT, int32_t NS, int32_t K, int32_t Ci, int32_t Co, int32_t dtype,
                                    bpc_stream_t stream) {

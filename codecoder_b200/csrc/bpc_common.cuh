@@ -426,6 +426,14 @@ __device__ __forceinline__ uint64_t silu_tanh_fast2(uint64_t x) {
 // SiLU with CUDA's expf (fp32 networks)
 __device__ __forceinline__ float silu_exact(float x) { return x / (1.0f + expf(-x)); }
 
+// GELU (tanh form) as the training network's residual steps compute it before rounding to bf16:
+// t = tanh.approx(k (x + c x^3)), x (1 + t) / 2, k = sqrt(2 / pi), c = 0.044715 (one definition for the memory-bound
+// passes and the step kernel's fused epilogue, so both give the same bits).
+__device__ __forceinline__ float gelu_tanh_pass(float x) {
+  const float t = tanh_approx(0.7978845608028654f * fmaf(0.044715f * x, x * x, x));
+  return 0.5f * x * (1.0f + t);
+}
+
 __device__ __forceinline__ float gelu_tanh(float x) {
   const float u = 0.7978845608028654f * fmaf(0.044715f * x, x * x, x);
   return 0.5f * x * (1.0f + tanhf(u));

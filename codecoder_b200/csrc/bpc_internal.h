@@ -18,6 +18,8 @@ enum EpiMode : int {
   kEpiGeluResid = 2,  // y = y + GELU(acc)
   kEpiAffineSilu = 3, // y = SiLU(scale[c] acc + shift[c])  (an inference BatchNorm folded into scale / shift)
   kEpiAdd = 4,        // y = y + acc  (row layouts: accumulate a second input gradient onto the first)
+  kEpiGeluStream = 5, // y = acc (bf16, kept), and the residual stream: out = h + bf16(GELU(y)) (h fp32 -> out fp32 and
+                      // its bf16 copy out16; h bf16 -> out bf16; no h -> out = bf16(GELU(y)))  (row layouts)
 };
 
 // Optional work fused into the epilogue of the last check -> data step of the pre-decoder.
@@ -57,6 +59,13 @@ struct GmmProblem {
   const float* epi_scale = nullptr;   // kEpiAffineSilu: per output channel (Co,) fp32
   const float* epi_shift = nullptr;
   HeadEpilogue head;
+  // kEpiGeluStream: the residual stream rows of the targets (channel c of shot s at node n: s res_shot_stride +
+  // n res_node_stride + c), 16-byte aligned
+  const void* res_h = nullptr;
+  bool res_f32 = false;
+  void* res_out = nullptr;
+  void* res_out16 = nullptr;
+  int64_t res_shot_stride = 0, res_node_stride = 0;
   // tensor-core path: a device counter that is zero when the kernel starts hands out tiles dynamically (null:
   // static striding)
   unsigned long long* tile_counter = nullptr;

@@ -77,10 +77,7 @@ __global__ void __launch_bounds__(256) residual_affine_silu_kernel(const float* 
 constexpr float kGeluK = 0.7978845608028654f;
 constexpr float kGeluC = 0.044715f;
 
-__device__ __forceinline__ float gelu_acc(float x) {
-  const float t = tanh_approx(kGeluK * fmaf(kGeluC * x, x * x, x));
-  return 0.5f * x * (1.0f + t);
-}
+__device__ __forceinline__ float gelu_acc(float x) { return gelu_tanh_pass(x); }
 __device__ __forceinline__ float gelu_grad(float x) {
   const float t = tanh_approx(kGeluK * fmaf(kGeluC * x, x * x, x));
   return 0.5f * (1.0f + t) + 0.5f * x * (1.0f - t * t) * kGeluK * fmaf(3.0f * kGeluC, x * x, 1.0f);

@@ -68,6 +68,11 @@ struct TcArgs {
   const float* epi_scale;
   const float* epi_shift;
   HeadEpilogue head;
+  const void* res_h;                      // kEpiGeluStream: residual stream in (null: none), out, bf16 copy out
+  int res_f32;
+  void* res_out;
+  void* res_out16;
+  int64_t res_shot_stride, res_node_stride;
   int* status;
   uint64_t timeout_ns;
   uint32_t tmem_cols;
@@ -495,6 +500,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr bool kLoadY = EPI == kEpiGeluResid || EPI == kEpiAdd;     // the epilogue reads y before writing it
   constexpr bool kGelu = EPI == kEpiGeluInit || EPI == kEpiGeluResid;
   constexpr bool kAffine = EPI == kEpiAffineSilu;                    // SiLU(scale acc + shift) per output channel
+  constexpr bool kStream = EPI == kEpiGeluStream;                    // y = acc, and the GELU residual stream
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* scratch = smem + kWideStages * kWideStageBytes;
@@ -726,6 +732,26 @@ __global__ void __launch_bounds__(kThreads, 1)
             rb[j][1] = *reinterpret_cast<const uint4*>(yc + j * step_j + step_g);
           }
       }
+      // kStream: this thread's 16 channels (32 q + 16 h ..) of the residual stream row of its shot in each piece,
+      // loaded one piece ahead
+      const int64_t rbase = kStream ? static_cast<int64_t>(n) * a.res_node_stride + 32 * q + 16 * h : 0;
+      float4 hf[4], hfn[4];
+      uint4 hb[2], hbn[2];
+      auto load_res = [&](int j, float4 (&f)[4], uint4 (&b)[2]) {
+        const int64_t sj = s0 + 128 * half + 16 * j + s;
+        if (!live || sj >= a.shots || !a.res_h) return;
+        const int64_t off = sj * a.res_shot_stride + rbase;
+        if (a.res_f32) {
+          const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(a.res_h) + off);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) f[i] = p[i];
+        } else {
+          const uint4* p = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.res_h) + off);
+          b[0] = p[0];
+          b[1] = p[1];
+        }
+      };
+      if (kStream) load_res(0, hf, hb);
       if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&accf[acc]), acc_phase, abort_flag, a.status, a.timeout_ns)))
         break;
       tc_fence_after();
@@ -733,6 +759,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                              static_cast<uint32_t>(acc * kWideShots + 128 * half);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
+        if (kStream && j + 1 < 8) load_res(j + 1, hfn, hbn);
         float v[16];
         if (vm && live) {
           tmem_ld16(taddr + 16 * j, v);
@@ -778,7 +805,51 @@ __global__ void __launch_bounds__(kThreads, 1)
               o[e4] = f2_to_bf2(xx);
             }
             *reinterpret_cast<uint4*>(yc + j * step_j + g * step_g) = u;
+            if (kStream) {
+              // the residual step of the training network on the stored (bf16) pre-activation, the arithmetic of
+              // the GELU / residual pass: g = bf16(GELU(a)); fp32 stream: out = h + g and its bf16 copy; bf16
+              // stream: out = bf16(g + h); no stream: out = g
+              float gv[8];
+#pragma unroll
+              for (int e4 = 0; e4 < 4; ++e4) {
+                gv[2 * e4] = __bfloat162float(__float2bfloat16_rn(gelu_tanh_pass(__uint_as_float(o[e4] << 16))));
+                gv[2 * e4 + 1] =
+                    __bfloat162float(__float2bfloat16_rn(gelu_tanh_pass(__uint_as_float(o[e4] & 0xFFFF0000u))));
+              }
+              const int64_t off = (s0 + 128 * half + 16 * j + s) * a.res_shot_stride + rbase + 8 * g;
+              uint4 w16;
+              uint32_t* w16w = reinterpret_cast<uint32_t*>(&w16);
+              if (a.res_h && a.res_f32) {
+                const float4 h0 = hf[2 * g], h1 = hf[2 * g + 1];
+                const float vv[8] = {h0.x + gv[0], h0.y + gv[1], h0.z + gv[2], h0.w + gv[3],
+                                     h1.x + gv[4], h1.y + gv[5], h1.z + gv[6], h1.w + gv[7]};
+                float4* op = reinterpret_cast<float4*>(static_cast<float*>(a.res_out) + off);
+                op[0] = make_float4(vv[0], vv[1], vv[2], vv[3]);
+                op[1] = make_float4(vv[4], vv[5], vv[6], vv[7]);
+#pragma unroll
+                for (int e4 = 0; e4 < 4; ++e4) w16w[e4] = f2_to_bf2(f2_pack(vv[2 * e4], vv[2 * e4 + 1]));
+                *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.res_out16) + off) = w16;
+              } else {
+                const uint32_t* hw = reinterpret_cast<const uint32_t*>(&hb[g]);
+#pragma unroll
+                for (int e4 = 0; e4 < 4; ++e4) {
+                  float v0 = gv[2 * e4], v1 = gv[2 * e4 + 1];
+                  if (a.res_h) {
+                    v0 += __uint_as_float(hw[e4] << 16);
+                    v1 += __uint_as_float(hw[e4] & 0xFFFF0000u);
+                  }
+                  w16w[e4] = f2_to_bf2(f2_pack(v0, v1));
+                }
+                *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.res_out) + off) = w16;
+              }
+            }
           }
+        }
+        if (kStream) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) hf[i] = hfn[i];
+          hb[0] = hbn[0];
+          hb[1] = hbn[1];
         }
       }
       if (HEAD) {
@@ -918,6 +989,7 @@ const void* wide_kernel_for(bool blocked, int epi, bool head, int Ci) {
   if (epi == kEpiStore) return wide_for_ci<false, kEpiStore, false>(Ci);
   if (epi == kEpiAdd) return wide_for_ci<false, kEpiAdd, false>(Ci);
   if (epi == kEpiAffineSilu) return wide_for_ci<false, kEpiAffineSilu, false>(Ci);
+  if (epi == kEpiGeluStream) return wide_for_ci<false, kEpiGeluStream, false>(Ci);
   return nullptr;
 }
 
@@ -997,6 +1069,13 @@ int gmm_tc_check(const GmmProblem& p) {
   if (p.head.head_w && (!p.head.logits || (reinterpret_cast<uintptr_t>(p.head.logits) & 7) ||
                         ((p.head.lg_shot_stride | p.head.lg_node_stride) & 1)))
     return fail(2, "head logits must be 8-byte aligned with even strides");
+  if (p.epi == kEpiGeluStream) {
+    if (p.blocked || p.head.head_w || !p.res_out || (p.res_h && p.res_f32 && !p.res_out16))
+      return fail(2, "the GELU stream epilogue takes row layouts, an output stream and (fp32 stream) its bf16 copy");
+    if ((reinterpret_cast<uintptr_t>(p.res_h) | reinterpret_cast<uintptr_t>(p.res_out) |
+         reinterpret_cast<uintptr_t>(p.res_out16)) & 15 || (p.res_shot_stride | p.res_node_stride) & 7)
+      return fail(2, "the residual stream must be 16-byte aligned with strides that are multiples of 8 elements");
+  }
   if (p.epi == kEpiAffineSilu && (!p.epi_scale || !p.epi_shift ||
                                   ((reinterpret_cast<uintptr_t>(p.epi_scale) | reinterpret_cast<uintptr_t>(p.epi_shift)) & 7)))
     return fail(2, "the affine + SiLU epilogue needs 8-byte aligned scale and shift vectors");
@@ -1060,6 +1139,12 @@ int gmm_tc_launch(const GmmProblem& p, const GmmMaps& maps, int* status, uint64_
   a.epi_scale = p.epi_scale;
   a.epi_shift = p.epi_shift;
   a.head = p.head;
+  a.res_h = p.res_h;
+  a.res_f32 = p.res_f32 ? 1 : 0;
+  a.res_out = p.res_out;
+  a.res_out16 = p.res_out16;
+  a.res_shot_stride = p.res_shot_stride;
+  a.res_node_stride = p.res_node_stride;
   a.status = status;
   a.timeout_ns = timeout_ns;
   a.tile_counter = p.tile_counter;
@@ -1072,7 +1157,10 @@ int gmm_tc_launch(const GmmProblem& p, const GmmMaps& maps, int* status, uint64_
   const bool wide_shape = p.Co >= 64 && p.Co <= kWideM && p.Co % 32 == 0 && (p.Ci == 64 || p.Ci == 96 || p.Ci == 128);
   const bool wide_blocked = p.blocked && p.Ci == p.Co && (p.epi == kEpiGeluInit || p.epi == kEpiGeluResid);
   const bool wide_rows = !p.blocked && !head && p.y_cg_stride == 8 &&
-                         (p.epi == kEpiStore || p.epi == kEpiAdd || p.epi == kEpiAffineSilu);
+                         (p.epi == kEpiStore || p.epi == kEpiAdd || p.epi == kEpiAffineSilu ||
+                          p.epi == kEpiGeluStream);
+  if (p.epi == kEpiGeluStream && !(wide_shape && wide_rows))
+    return fail(2, "the GELU stream epilogue runs on the wide-tile kernel: C_in, C_out in {64, 96, 128}, row layouts");
   if (wide_shape && (wide_blocked || wide_rows)) {
     const void* wf = wide_kernel_for(p.blocked, p.epi, head, p.Ci);
     if (!wf) return fail(2, "unsupported wide-tile configuration");

@@ -19,6 +19,13 @@ from . import _lib
 _DTYPES = {torch.bfloat16: _lib.BPC_DTYPE_BF16, torch.float32: _lib.BPC_DTYPE_F32}
 
 
+# True: the fused steps' forward runs the op and its GELU / residual pass in one launch where the wide-tile kernel
+# takes the shape (bpc_gather_mm_fwd_gelu); False (default): the op, then the pass.  Both give the same bits; on a
+# B200 the one-launch form measured slower (d = 11 training step 146 against 139 ms on the same box: the stream's
+# loads and stores in the epilogue slow the L2-bound op by more than the separate pass costs).
+_FUSED_GELU = False
+
+
 def _stream_ptr(device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
@@ -357,17 +364,32 @@ class BipartiteStepB200(torch.autograd.Function):
         w16 = [w.to(torch.bfloat16).contiguous() for w in ws]
         Co = w16[0].shape[0]
         a = torch.empty(T, B, NTt, Co, device=x.device, dtype=torch.bfloat16)
-        for t in range(T):
-            _gmm_into(x, tables[t][0], w16[t], a[t])
         L = _lib.lib()
         st = _stream_ptr(x.device)
         f32 = h is not None and h.dtype == torch.float32
         y = torch.empty(B, NT, Co, device=x.device, dtype=torch.float32 if f32 else torch.bfloat16)
         y16 = torch.empty(B, NT, Co, device=x.device, dtype=torch.bfloat16) if f32 else None
         hdt = _lib.BPC_DTYPE_F32 if f32 else _lib.BPC_DTYPE_BF16
-        rc = L.bpc_gelu_residual_fwd(a.data_ptr(), h.data_ptr() if h is not None else None, y.data_ptr(),
-                                     y16.data_ptr() if f32 else None, B, NT, Co, T, hdt, st)
-        _lib.check(rc, "bpc_gelu_residual_fwd")
+        K = tables[0][0].shape[1]
+        if _FUSED_GELU and x.is_cuda and x.dtype == torch.bfloat16 and Ci in (64, 96, 128) and \
+                Co in (64, 96, 128) and K <= 16:
+            # the op and the GELU / residual pass in one launch per target type (bpc_gather_mm_fwd_gelu): the
+            # epilogue writes the kept pre-activation and this type's block of the residual stream
+            x = x.contiguous()
+            h = h.contiguous() if h is not None else None
+            for t in range(T):
+                off = t * NTt * Co
+                rc = L.bpc_gather_mm_fwd_gelu(
+                    x.data_ptr(), w16[t].data_ptr(), tables[t][0].data_ptr(), a[t].data_ptr(), B, NS, NTt, K, Ci, Co,
+                    h.data_ptr() + off * h.element_size() if h is not None else None, hdt,
+                    y.data_ptr() + off * y.element_size(), y16.data_ptr() + off * 2 if f32 else None, NT * Co, st)
+                _lib.check(rc, "bpc_gather_mm_fwd_gelu")
+        else:
+            for t in range(T):
+                _gmm_into(x, tables[t][0], w16[t], a[t])
+            rc = L.bpc_gelu_residual_fwd(a.data_ptr(), h.data_ptr() if h is not None else None, y.data_ptr(),
+                                         y16.data_ptr() if f32 else None, B, NT, Co, T, hdt, st)
+            _lib.check(rc, "bpc_gelu_residual_fwd")
         ctx.save_for_backward(x, a, *w16)
         ctx.set_materialize_grads(False)     # an unused output's gradient stays None, not a zero-filled tensor
         ctx.tables, ctx.f32, ctx.has_h, ctx.carry = tables, f32, h is not None, carry

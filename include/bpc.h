@@ -151,6 +151,17 @@ BPC_API int bpc_head_bce_bwd(const void* hd, const float* W, const float* b, con
                              const float* grad_loss, void* dh, float* dW, float* db, void* workspace,
                              size_t workspace_bytes, int64_t rows, int32_t C, bpc_stream_t stream);
 
+/* One residual step of the training network in one launch (one weight set; row layouts; bf16; the wide-tile
+ * tensor-core kernel: C_in, C_out in {64, 96, 128}): a = gather_mm(x, w, idx), (B, NT, Co) bf16, kept for the
+ * backward, and in the same epilogue the residual stream of these NT targets, as bpc_gelu_residual_fwd computes it:
+ *   g = bf16(GELU(a));  h fp32: out = h + g (fp32) and out_bf16 = bf16(out);  h bf16: out = bf16(h + g);  h NULL:
+ *   out = g (bf16).
+ * h, out, out_bf16: the targets' first row of (B, *, Co) streams whose shots are stream_shot_stride elements apart
+ * (a target type's block of a type-major stream), 16-byte aligned.  No reference counterpart: the reference composes
+ * gather_mm, GELU and the add under autocast (cascade_net.py:140-175,228-233). */
+BPC_API int bpc_gather_mm_fwd_gelu(const void* x, const void* w, const int32_t* idx, void* a, int64_t B, int32_t NS,
+                                   int32_t NT, int32_t K, int32_t Ci, int32_t Co, const void* h, int32_t h_dtype,
+                                   void* out, void* out_bf16, int64_t stream_shot_stride, bpc_stream_t stream);
 /* Input gradient of bpc_gather_mm_fwd through the target table:
  *   gx[b, s, :] = sum_r gy[b, tgt[s, r], :] W_r,   tgt (NS, K) int32, NT (or any value outside [0, NT)) = none
  * gy (B, NT, Co), gx (B, NS, Ci), W (Co, K*Ci) as in the forward.  tgt[s, r] is the target that reads source s

@@ -92,6 +92,30 @@ def test_graphed_training_steps_match_eager_steps():
         assert torch.equal(pe, pg)
 
 
+def test_fused_gelu_launch_matches_the_two_launch_form(monkeypatch):
+    """The training network's residual steps run the op and their GELU / residual pass in one launch
+    (bpc_gather_mm_fwd_gelu: the step kernel's epilogue writes the kept pre-activation and the residual stream).  It
+    gives the bits of the op followed by bpc_gelu_residual_fwd in every mode (the first check -> data step without a
+    residual, the bf16 data stream, the fp32 check stream with two target types), over a partial tile: the same
+    loss and gradients."""
+    from codecoder_b200 import ops
+    cfg = replace(CONFIGS["d11_train"], d=5, rounds=5, layers=3)            # C = 96: the wide-tile kernel
+    g = RotatedSurface(cfg.d, cfg.rounds)
+    det, err = sample_torch(g, 0.03, 384, 71, device="cuda")
+    out = []
+    for fused in (True, False):
+        monkeypatch.setattr(ops, "_FUSED_GELU", fused)
+        net = PreDecoderNet(g, cfg, init_params(cfg, 70)).cuda()
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = net(det, err)
+        loss.backward()
+        out.append((loss.detach(), [p.grad.clone() for p in net.parameters() if p.grad is not None]))
+    torch.cuda.synchronize()
+    (lf, gf), (lu, gu) = out
+    assert torch.equal(lf, lu)
+    assert len(gf) == len(gu) and all(torch.equal(a, b) for a, b in zip(gf, gu))
+
+
 def test_fused_steps_match_the_unfused_network():
     """Under bf16 autocast PreDecoderNet runs each residual step as ops.bipartite_step (op kernels + one GELU /
     residual pass each way, both check types in one pre-activation block); the unfused torch composition of the same
