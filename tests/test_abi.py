@@ -96,3 +96,11 @@ def test_training_entry_points_check_arguments_first(lib):
     assert lib.bpc_gather_mm_dgrad_ex(None, None, None, None, None, 4, 10, 10, 8, 64, 64, 1, 9, None) == 2
     assert lib.bpc_gather_mm_dgrad_ex(None, None, None, None, None, 4, 10, 10, 8, 64, 64, 1, bf16, None) == 2
     assert "null" in _lib.last_error()
+    # the one-launch residual step: shape, stream dtype, stream rows that overlap, null buffers
+    gelu = lib.bpc_gather_mm_fwd_gelu
+    assert gelu(None, None, None, None, 4, 0, 10, 8, 96, 96, None, bf16, None, None, 960, None) == 2
+    assert gelu(None, None, None, None, 4, 20, 10, 8, 96, 96, 16, 9, None, None, 960, None) == 2
+    assert gelu(None, None, None, None, 4, 20, 10, 8, 96, 96, None, bf16, None, None, 959, None) == 2
+    assert "overlap" in _lib.last_error()
+    assert gelu(None, None, None, None, 4, 20, 10, 8, 96, 96, None, bf16, None, None, 960, None) == 2
+    assert "null" in _lib.last_error()
