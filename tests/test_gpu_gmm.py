@@ -165,6 +165,37 @@ def test_gather_mm_dropin_signature():
     assert torch.ops.cascade.gmm(x, idx.to(torch.int32), w, False).shape == (4, g.N_d, 64)
 
 
+@pytest.mark.parametrize("B", [0, 1])
+def test_gather_mm_empty_and_single_shot_batches(B):
+    """gather_mm forward and backward on the tensor-core path (bf16 autocast, C = 64) for an empty batch and a single
+    shot: an empty batch gives empty outputs and input gradient and a zero weight gradient; one shot matches the
+    oracle's forward and its autograd gradients (bf16 tolerances as the other op tests)."""
+    g = RotatedSurface(5, 5)
+    rng = np.random.default_rng(12 + B)
+    x0 = rng.standard_normal((B, g.N_c, 64)).astype(np.float32)
+    w0 = (rng.standard_normal((64, 8 * 64)) / 20).astype(np.float32)
+    idx = torch.as_tensor(g.c2d[0]).to(DEV)
+    inv = torch.as_tensor(g.inv_c2d[0]).to(DEV)
+    x = torch.as_tensor(x0).to(DEV).requires_grad_()
+    w = torch.as_tensor(w0).to(DEV).requires_grad_()
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        y = gather_mm(x, w, idx, inv)
+    gy = torch.as_tensor(rng.standard_normal((B, g.N_d, 64)).astype(np.float32)).to(DEV)
+    (y.float() * gy).sum().backward()
+    torch.cuda.synchronize()
+    assert y.shape == (B, g.N_d, 64) and x.grad.shape == x.shape and w.grad.shape == w.shape
+    if B == 0:
+        assert torch.count_nonzero(w.grad) == 0
+        return
+    xr = torch.as_tensor(x0).requires_grad_()
+    wr = torch.as_tensor(w0).requires_grad_()
+    yr = orc.gather_mm(xr, wr, g.c2d[0])
+    (yr * gy.cpu()).sum().backward()
+    assert rel_err(y.detach().float().cpu().numpy(), yr.detach().numpy()) < 2e-2
+    assert rel_err(x.grad.cpu().numpy(), xr.grad.numpy()) < 5e-2
+    assert rel_err(w.grad.cpu().numpy(), wr.grad.numpy()) < 5e-2
+
+
 @pytest.mark.parametrize("C,B", [(128, 300), (64, 257), (96, 130)])
 def test_affine_silu_epilogue_two_weight_sets(C, B):
     """The op with two weight sets and the affine + SiLU epilogue (the Cascade block's data -> check convolution with
