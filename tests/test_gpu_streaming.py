@@ -41,7 +41,7 @@ def test_streaming_latency_is_measured():
 
 
 @pytest.mark.parametrize("layout", ["clusters", "one_cluster"])
-@pytest.mark.parametrize("d", [9, 17])
+@pytest.mark.parametrize("d", [9, 13, 17])
 def test_persistent_stream_matches_graph_stream(d, layout):
     """The resident kernel (mapped request line) gives the graph-replay decoder's bits round after round, in both
     layouts (the one-cluster layout adds relations 0-3 in one CTA and 4-7 in its partner, in the same order)."""
