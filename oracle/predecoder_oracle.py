@@ -1,7 +1,7 @@
 """CPU oracle of the bipartite-conv pre-decoder path -- TEST INFRASTRUCTURE ONLY.
 
-Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg may import this module, and only as the checker
-(or the timed CPU baseline): the product path (codecoder_b200) never calls it.
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg may import this module, and only to verify
+results (or as the timed CPU baseline): the product path (codecoder_b200) never calls it.
 
 What it restates:
   gather_mm      the reference's _GatherMM.forward (training/bb/ising_compare/bb/cascade_net.py:146-153): pad the
